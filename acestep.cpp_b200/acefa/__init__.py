@@ -1,0 +1,251 @@
+"""Python host side of the acefa attention engine (ctypes over include/acefa.h).
+
+The operator is ggml_flash_attn_ext; tensors are torch tensors whose dims are
+ggml's ne[] reversed (torch shape (ne3, ne2, ne1, ne0)), so a ggml Q
+[D, n_q, Hq, B] is a torch tensor of shape (B, Hq, n_q, D) and the result
+[D, Hq, n_q, B] comes back with shape (B, n_q, Hq, D).  Q8_0 K/V are uint8
+tensors whose last axis holds a row's 34-byte blocks (D/32 of them).
+
+There is no fallback: if libacefa.so is missing or the current device is not
+an sm_100 GPU every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
+PREC_DEFAULT, PREC_F32 = 0, 10
+
+OK = 0
+STATUS_NAMES = {
+    0: "ACEFA_OK", -1: "ACEFA_ERR_NULL", -2: "ACEFA_ERR_TYPE", -3: "ACEFA_ERR_SHAPE",
+    -4: "ACEFA_ERR_LAYOUT", -5: "ACEFA_ERR_WORKSPACE", -6: "ACEFA_ERR_CUDA",
+    -7: "ACEFA_ERR_DEVICE", -8: "ACEFA_ERR_DEVICE_TIMEOUT",
+}
+
+_PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG_DIR, "libacefa.so")
+
+EXPORTED_SYMBOLS = (
+    "acefa_flash_attn_ext",
+    "acefa_workspace_bytes",
+    "acefa_supports",
+    "acefa_check",
+    "acefa_device_error",
+    "acefa_status_string",
+    "acefa_last_launch_count",
+    "acefa_last_path",
+    "acefa_version",
+)
+
+
+class AcefaError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        super().__init__(f"{what}: {STATUS_NAMES.get(status, status)}" if what else STATUS_NAMES.get(status, str(status)))
+
+
+class Tensor(ctypes.Structure):
+    """struct acefa_tensor"""
+
+    _fields_ = [
+        ("type", ctypes.c_int32),
+        ("ne", ctypes.c_int64 * 4),
+        ("nb", ctypes.c_size_t * 4),
+        ("data", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+
+
+def load_library(path: str | None = None):
+    """Load libacefa.so (raises OSError if it was not built)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise OSError(f"libacefa.so not found at {p}; run acestep.cpp_b200/build.py")
+    lib = ctypes.CDLL(p)
+    T = ctypes.POINTER(Tensor)
+    lib.acefa_flash_attn_ext.argtypes = [T, T, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                         ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+    lib.acefa_flash_attn_ext.restype = ctypes.c_int
+    lib.acefa_workspace_bytes.argtypes = [T, T, T, T, T]
+    lib.acefa_workspace_bytes.restype = ctypes.c_size_t
+    lib.acefa_supports.argtypes = [T, T, T, T, T, T]
+    lib.acefa_supports.restype = ctypes.c_int
+    lib.acefa_check.argtypes = [T, T, T, T, T, T]
+    lib.acefa_check.restype = ctypes.c_int
+    lib.acefa_device_error.argtypes = [ctypes.c_void_p]
+    lib.acefa_device_error.restype = ctypes.c_int
+    lib.acefa_status_string.argtypes = [ctypes.c_int]
+    lib.acefa_status_string.restype = ctypes.c_char_p
+    lib.acefa_last_launch_count.restype = ctypes.c_int
+    lib.acefa_last_path.restype = ctypes.c_int
+    lib.acefa_version.restype = ctypes.c_int
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _ggml_type(t: torch.Tensor, gtype: int | None) -> int:
+    if gtype is not None:
+        return gtype
+    if t.dtype == torch.float32:
+        return GGML_F32
+    if t.dtype == torch.float16:
+        return GGML_F16
+    if t.dtype == torch.bfloat16:
+        return GGML_BF16
+    raise TypeError(f"no ggml type for {t.dtype}; pass gtype=GGML_Q8_0 for uint8 Q8_0 blocks")
+
+
+def describe(t: torch.Tensor | None, gtype: int | None = None, ne0: int | None = None):
+    """acefa_tensor for a torch tensor (dims reversed into ggml ne order)."""
+    if t is None:
+        return None
+    if t.dim() > 4:
+        raise ValueError("at most 4 dims")
+    shape = list(t.shape)[::-1] + [1] * (4 - t.dim())
+    es = t.element_size()
+    strides = [s * es for s in list(t.stride())[::-1]]
+    while len(strides) < 4:
+        strides.append(strides[-1] * shape[len(strides) - 1] if strides else es)
+    g = _ggml_type(t, gtype)
+    d = Tensor()
+    d.type = g
+    if g == GGML_Q8_0:
+        if t.dtype != torch.uint8 or t.stride(-1) != 1:
+            raise ValueError("Q8_0 tensors are contiguous uint8 block rows")
+        if t.shape[-1] % 34:
+            raise ValueError("Q8_0 row bytes must be a multiple of 34")
+        shape[0] = ne0 if ne0 is not None else t.shape[-1] // 34 * 32
+        strides[0] = 34
+    d.ne[:] = shape
+    d.nb[:] = strides
+    d.data = t.data_ptr()
+    return d
+
+
+def _ref(x):
+    return ctypes.byref(x) if x is not None else None
+
+
+def _stream_ptr(stream) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+def result_shape(q: torch.Tensor, v: torch.Tensor, v_type: int | None = None):
+    B, Hq, n_q, _ = q.shape
+    Dv = v.shape[-1] // 34 * 32 if v_type == GGML_Q8_0 else v.shape[-1]
+    return (B, n_q, Hq, Dv)
+
+
+class Op:
+    """One ggml_flash_attn_ext node's operands, described once, callable many times."""
+
+    def __init__(self, q, k, v, mask=None, sinks=None, out=None, kv_type=None, scale=None,
+                 max_bias=0.0, softcap=0.0, prec=PREC_F32):
+        self.lib = load_library()
+        self.q, self.k, self.v, self.mask, self.sinks = q, k, v, mask, sinks
+        D = q.shape[-1]
+        self.kv_type = kv_type
+        if out is None:
+            out = torch.empty(result_shape(q, v, kv_type), dtype=torch.float32, device=q.device)
+        self.out = out
+        self.tq = describe(q)
+        self.tk = describe(k, kv_type, D)
+        self.tv = describe(v, kv_type, D)
+        self.tm = describe(mask, GGML_F16) if mask is not None else None
+        self.ts = describe(sinks.reshape(-1), GGML_F32) if sinks is not None else None
+        self.td = describe(out)
+        self.scale = float(scale if scale is not None else D ** -0.5)
+        self.max_bias, self.softcap, self.prec = float(max_bias), float(softcap), int(prec)
+        st = self.lib.acefa_check(_ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts),
+                                  _ref(self.td))
+        if st != OK:
+            raise AcefaError(st, "acefa_check")
+        self.ws_bytes = int(self.lib.acefa_workspace_bytes(_ref(self.tq), _ref(self.tk), _ref(self.tv),
+                                                           _ref(self.tm), _ref(self.td)))
+        self.workspace = torch.empty(max(self.ws_bytes, 256), dtype=torch.uint8, device=q.device)
+
+    def __call__(self, stream=None):
+        st = self.lib.acefa_flash_attn_ext(
+            _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),
+            self.scale, self.max_bias, self.softcap, self.prec, ctypes.c_void_p(_stream_ptr(stream)),
+            ctypes.c_void_p(self.workspace.data_ptr()), ctypes.c_size_t(self.workspace.numel()))
+        if st != OK:
+            raise AcefaError(st, "acefa_flash_attn_ext")
+        return self.out
+
+
+def flash_attn_ext(q, k, v, mask=None, scale=None, max_bias=0.0, softcap=0.0, sinks=None, kv_type=None,
+                   out=None, prec=PREC_F32, stream=None):
+    """ggml_flash_attn_ext on the GPU.  Returns dst with torch shape (B, n_q, Hq, Dv)."""
+    return Op(q, k, v, mask=mask, sinks=sinks, out=out, kv_type=kv_type, scale=scale, max_bias=max_bias,
+              softcap=softcap, prec=prec)(stream)
+
+
+def supports(q, k, v, mask=None, sinks=None, kv_type=None) -> bool:
+    lib = load_library()
+    D = q.shape[-1]
+    out = torch.empty(0)
+    td = Tensor()
+    td.type = GGML_F32
+    B, Hq, n_q, _ = q.shape
+    td.ne[:] = [D, Hq, n_q, B]
+    td.nb[:] = [4, 4 * D, 4 * D * Hq, 4 * D * Hq * n_q]
+    td.data = 256
+    del out
+    return bool(lib.acefa_supports(_ref(describe(q)), _ref(describe(k, kv_type, D)), _ref(describe(v, kv_type, D)),
+                                   _ref(describe(mask, GGML_F16) if mask is not None else None),
+                                   _ref(describe(sinks.reshape(-1), GGML_F32) if sinks is not None else None),
+                                   ctypes.byref(td)))
+
+
+def device_error(stream=None) -> int:
+    return load_library().acefa_device_error(ctypes.c_void_p(_stream_ptr(stream)))
+
+
+def last_launch_count() -> int:
+    return load_library().acefa_last_launch_count()
+
+
+def last_path() -> int:
+    return load_library().acefa_last_path()
+
+
+# --------------------------------------------------------------------------
+# input preparation helpers (torch ops; not on the attention path)
+
+def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:
+    """ggml Q8_0 blocks of x (..., n) -> uint8 (..., n/32*34), bit-exact with
+    ggml-quants.c quantize_row_q8_0_ref (d = amax/127 in f32, q = roundf(x/d),
+    d stored as f16).  Works on any device; used to build K/V caches."""
+    assert x.shape[-1] % 32 == 0
+    xb = x.float().reshape(*x.shape[:-1], x.shape[-1] // 32, 32)
+    d = xb.abs().amax(dim=-1, keepdim=True) / 127.0
+    inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+    y = xb * inv
+    a = y.abs()
+    fl = torch.floor(a)
+    r = torch.sign(y) * (fl + torch.floor(2.0 * (a - fl)))  # round half away from zero
+    qs = r.to(torch.int8).view(torch.uint8)
+    dh = d.to(torch.float16).view(torch.uint8)  # (..., nb, 2)
+    blocks = torch.cat([dh, qs], dim=-1)  # (..., nb, 34)
+    return blocks.reshape(*x.shape[:-1], x.shape[-1] // 32 * 34).contiguous()
+
+
+def dequantize_q8_0(y: torch.Tensor) -> torch.Tensor:
+    nb = y.shape[-1] // 34
+    b = y.reshape(*y.shape[:-1], nb, 34)
+    d = b[..., :2].contiguous().view(torch.float16).float()
+    q = b[..., 2:].contiguous().view(torch.int8).float()
+    return (q * d).reshape(*y.shape[:-1], nb * 32)

@@ -1,0 +1,385 @@
+// fa_api.cu -- the C ABI (include/acefa.h): operand validation in ggml terms,
+// workspace sizing, TMA descriptor encoding and kernel dispatch.
+//
+// Mirrors what ggml's CUDA backend does for GGML_OP_FLASH_ATTN_EXT
+// (supports_op check, then ggml_cuda_flash_attn_ext(ctx, dst) reading
+// dst->src[0..4] and dst->op_params {scale, max_bias, logit_softcap}) without any
+// ggml type in the signature.  Status codes replace ggml's GGML_ABORT.
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+
+#include "fa_internal.h"
+#include "ptx.cuh"
+
+namespace acefa {
+
+__device__ int g_dev_err;  // device-side failure word (see DEVERR_*)
+
+namespace {
+
+thread_local int t_last_launches = 0;
+thread_local int t_last_path     = 0;
+
+constexpr int kMaxDevices = 64;
+
+struct DevInfo {
+    int  sm_count = 0;
+    int  cc_major = 0, cc_minor = 0;
+    int *err_ptr  = nullptr;
+    bool ready    = false;
+};
+DevInfo g_dev[kMaxDevices];  // immutable once ready (per-device properties cache)
+
+int dev_info(DevInfo **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        return ACEFA_ERR_CUDA;
+    }
+    DevInfo &d = g_dev[dev];
+    if (!d.ready) {
+        if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+            return ACEFA_ERR_CUDA;
+        }
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) {
+            return ACEFA_ERR_CUDA;
+        }
+        d.err_ptr = static_cast<int *>(p);
+        d.ready   = true;
+    }
+    if (d.cc_major != 10 || d.cc_minor != 0) {
+        return ACEFA_ERR_DEVICE;
+    }
+    *out = &d;
+    return ACEFA_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (fn == nullptr) {
+        void                            *p = nullptr;
+        cudaDriverEntryPointQueryResult  q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    }
+    return fn;
+}
+
+uint64_t wait_limit_ns() {
+    static uint64_t lim = 0;
+    if (lim == 0) {
+        const char *e  = std::getenv("ACEFA_WAIT_LIMIT_MS");
+        long        ms = e ? std::atol(e) : 0;
+        lim            = (ms > 0 ? (uint64_t) ms : 1000ull) * 1000000ull;
+    }
+    return lim;
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ------------------------------------------------------------------ validation
+struct Checked {
+    OpDesc op;
+    int    status;
+};
+
+Checked check_operands(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                       const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
+    Checked r;
+    std::memset(&r.op, 0, sizeof(r.op));
+    r.status = ACEFA_OK;
+    auto fail = [&](int s) {
+        r.status = s;
+        return r;
+    };
+    if (!q || !k || !v || !dst || !q->data || !k->data || !v->data || !dst->data) {
+        return fail(ACEFA_ERR_NULL);
+    }
+    if (q->type != ACEFA_TYPE_F32 || dst->type != ACEFA_TYPE_F32) {
+        return fail(ACEFA_ERR_TYPE);
+    }
+    if (k->type != ACEFA_TYPE_F16 && k->type != ACEFA_TYPE_BF16 && k->type != ACEFA_TYPE_Q8_0) {
+        return fail(ACEFA_ERR_TYPE);
+    }
+    if (v->type != k->type) {
+        return fail(ACEFA_ERR_TYPE);
+    }
+    for (int i = 0; i < 4; ++i) {
+        if (q->ne[i] <= 0 || k->ne[i] <= 0 || v->ne[i] <= 0 || dst->ne[i] <= 0) {
+            return fail(ACEFA_ERR_SHAPE);
+        }
+    }
+    const int64_t D = q->ne[0], n_q = q->ne[1], Hq = q->ne[2], B = q->ne[3];
+    const int64_t n_kv = k->ne[1], Hkv = k->ne[2], Bk = k->ne[3];
+    if (k->ne[0] != D || v->ne[0] != D || v->ne[1] != n_kv || v->ne[2] != Hkv || v->ne[3] != Bk) {
+        return fail(ACEFA_ERR_SHAPE);
+    }
+    if (Hq % Hkv != 0 || B % Bk != 0) {
+        return fail(ACEFA_ERR_SHAPE);
+    }
+    if (dst->ne[0] != D || dst->ne[1] != Hq || dst->ne[2] != n_q || dst->ne[3] != B) {
+        return fail(ACEFA_ERR_SHAPE);
+    }
+    if (D != 64 && D != 128) {
+        return fail(ACEFA_ERR_SHAPE);
+    }
+    if (n_kv > (1ll << 30) || n_q > (1ll << 30) || Hq > 4096 || B > (1ll << 20) ||
+        (Hq / Hkv) * n_q > (1ll << 30)) {
+        return fail(ACEFA_ERR_SHAPE);
+    }
+    if (mask) {
+        if (!mask->data) {
+            return fail(ACEFA_ERR_NULL);
+        }
+        if (mask->type != ACEFA_TYPE_F16) {
+            return fail(ACEFA_ERR_TYPE);
+        }
+        if (mask->ne[0] < n_kv || mask->ne[1] < n_q || mask->ne[2] <= 0 || mask->ne[3] <= 0 ||
+            Hq % mask->ne[2] != 0 || B % mask->ne[3] != 0) {
+            return fail(ACEFA_ERR_SHAPE);
+        }
+        if (mask->nb[0] != 2 || mask->nb[1] % 2 || mask->nb[2] % 2 || mask->nb[3] % 2 || !aligned(mask->data, 2)) {
+            return fail(ACEFA_ERR_LAYOUT);
+        }
+    }
+    if (sinks) {
+        if (!sinks->data) {
+            return fail(ACEFA_ERR_NULL);
+        }
+        if (sinks->type != ACEFA_TYPE_F32) {
+            return fail(ACEFA_ERR_TYPE);
+        }
+        if (sinks->ne[0] < Hq || sinks->nb[0] != 4 || !aligned(sinks->data, 4)) {
+            return fail(ACEFA_ERR_SHAPE);
+        }
+    }
+    // Q: f32 elements contiguous along D
+    if (q->nb[0] != 4 || q->nb[1] % 4 || q->nb[2] % 4 || q->nb[3] % 4 || !aligned(q->data, 4)) {
+        return fail(ACEFA_ERR_LAYOUT);
+    }
+    if (dst->nb[0] != 4 || dst->nb[1] % 4 || dst->nb[2] % 4 || dst->nb[3] % 4 || !aligned(dst->data, 4)) {
+        return fail(ACEFA_ERR_LAYOUT);
+    }
+    // K/V: the streaming kernels need 16-B aligned rows and head/batch strides
+    for (const acefa_tensor *t : {k, v}) {
+        if (!aligned(t->data, 16)) {
+            return fail(ACEFA_ERR_LAYOUT);
+        }
+        if (t->type == ACEFA_TYPE_Q8_0) {
+            if (D % 32 || t->nb[0] != 34 || t->nb[1] != (size_t) (D / 32 * 34)) {
+                return fail(ACEFA_ERR_LAYOUT);
+            }
+        } else {
+            if (t->nb[0] != 2 || t->nb[1] % 16 || t->nb[1] < (size_t) (2 * D)) {
+                return fail(ACEFA_ERR_LAYOUT);
+            }
+        }
+        if ((t->ne[2] > 1 && t->nb[2] % 16) || (t->ne[3] > 1 && t->nb[3] % 16)) {
+            return fail(ACEFA_ERR_LAYOUT);
+        }
+    }
+
+    OpDesc &o = r.op;
+    o.q       = static_cast<const char *>(q->data);
+    o.q_nb1 = q->nb[1], o.q_nb2 = q->nb[2], o.q_nb3 = q->nb[3];
+    o.k = static_cast<const char *>(k->data), o.v = static_cast<const char *>(v->data);
+    o.k_nb1 = k->nb[1], o.k_nb2 = k->nb[2], o.k_nb3 = k->nb[3];
+    o.v_nb1 = v->nb[1], o.v_nb2 = v->nb[2], o.v_nb3 = v->nb[3];
+    o.kv_type = k->type;
+    if (mask) {
+        o.mask  = static_cast<const char *>(mask->data);
+        o.m_nb1 = mask->nb[1], o.m_nb2 = mask->nb[2], o.m_nb3 = mask->nb[3];
+        o.m_ne2 = (int) mask->ne[2], o.m_ne3 = (int) mask->ne[3];
+    } else {
+        o.m_ne2 = o.m_ne3 = 1;
+    }
+    o.sinks = sinks ? static_cast<const float *>(sinks->data) : nullptr;
+    o.dst   = static_cast<char *>(dst->data);
+    o.d_nb0 = dst->nb[0], o.d_nb1 = dst->nb[1], o.d_nb2 = dst->nb[2], o.d_nb3 = dst->nb[3];
+    o.D = (int) D, o.n_q = (int) n_q, o.Hq = (int) Hq, o.B = (int) B;
+    o.n_kv = (int) n_kv, o.Hkv = (int) Hkv, o.Bk = (int) Bk;
+    o.G   = (int) (Hq / Hkv);
+    o.rk3 = (int) (B / Bk);
+    return r;
+}
+
+void set_scalars(OpDesc &o, float scale, float max_bias, float softcap) {
+    o.softcap   = softcap;
+    o.scale_eff = softcap != 0.0f ? scale / softcap : scale;
+    o.max_bias  = max_bias;
+    const int n_head_log2 = 1 << (int) std::floor(std::log2((float) o.Hq));
+    o.n_head_log2         = n_head_log2;
+    o.alibi_m0            = std::pow(2.0f, -(max_bias) / (float) n_head_log2);
+    o.alibi_m1            = std::pow(2.0f, -(max_bias / 2.0f) / (float) n_head_log2);
+}
+
+// ------------------------------------------------------------------ decode plan
+struct DecodePlan {
+    int     n_rb, units, tpu, n_ctas;
+    int64_t total_tiles;
+    size_t  ws_bytes;
+};
+
+DecodePlan plan_decode(const OpDesc &o, int sm_count) {
+    DecodePlan p;
+    const int rows   = o.G * o.n_q;
+    p.n_rb           = (rows + kDecRows - 1) / kDecRows;
+    p.units          = o.B * o.Hkv * p.n_rb;
+    p.tpu            = (o.n_kv + kDecBN - 1) / kDecBN;
+    p.total_tiles    = (int64_t) p.units * p.tpu;
+    const int64_t cap = (int64_t) sm_count * decode_ctas_per_sm(o.kv_type, o.D);
+    p.n_ctas         = (int) (p.total_tiles < cap ? p.total_tiles : cap);
+    p.ws_bytes       = (size_t) (p.n_ctas + p.units) * (size_t) dec_slot_floats(o.D) * sizeof(float);
+    p.ws_bytes       = (p.ws_bytes + 255) / 256 * 256;
+    return p;
+}
+
+int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) {
+        return ACEFA_ERR_CUDA;
+    }
+    cuuint64_t dims[4]    = {(cuuint64_t) D, (cuuint64_t) t->ne[1], (cuuint64_t) t->ne[2], (cuuint64_t) t->ne[3]};
+    cuuint64_t s1         = t->nb[1];
+    cuuint64_t s2         = t->ne[2] > 1 ? t->nb[2] : s1 * (cuuint64_t) t->ne[1];
+    cuuint64_t s3         = t->ne[3] > 1 ? t->nb[3] : s2 * (cuuint64_t) t->ne[2];
+    cuuint64_t strides[3] = {s1, s2, s3};
+    cuuint32_t box[4]     = {64, (cuuint32_t) kDecBN, 1, 1};
+    cuuint32_t estr[4]    = {1, 1, 1, 1};
+    CUresult   rc = enc(map, t->type == ACEFA_TYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        4, t->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return rc == CUDA_SUCCESS ? ACEFA_OK : ACEFA_ERR_LAYOUT;
+}
+
+}  // namespace
+}  // namespace acefa
+
+using namespace acefa;
+
+extern "C" {
+
+ACEFA_API int acefa_check(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                          const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
+    return check_operands(q, k, v, mask, sinks, dst).status;
+}
+
+ACEFA_API int acefa_supports(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                             const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
+    return check_operands(q, k, v, mask, sinks, dst).status == ACEFA_OK ? 1 : 0;
+}
+
+ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                       const acefa_tensor *mask, const acefa_tensor *dst) {
+    Checked c = check_operands(q, k, v, mask, nullptr, dst);
+    if (c.status != ACEFA_OK) {
+        return 0;
+    }
+    DevInfo *di = nullptr;
+    if (dev_info(&di) != ACEFA_OK) {
+        return 0;
+    }
+    return plan_decode(c.op, di->sm_count).ws_bytes;
+}
+
+ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                   const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst,
+                                   float scale, float max_bias, float logit_softcap, int prec, void *stream,
+                                   void *workspace, size_t workspace_bytes) {
+    (void) prec;  // accumulation is F32 for both GGML_PREC_DEFAULT and GGML_PREC_F32
+    Checked c = check_operands(q, k, v, mask, sinks, dst);
+    if (c.status != ACEFA_OK) {
+        return c.status;
+    }
+    if (!std::isfinite(scale) || !std::isfinite(max_bias) || !std::isfinite(logit_softcap) || max_bias < 0.0f) {
+        return ACEFA_ERR_SHAPE;
+    }
+    DevInfo *di = nullptr;
+    int      rc = dev_info(&di);
+    if (rc != ACEFA_OK) {
+        return rc;
+    }
+    set_scalars(c.op, scale, max_bias, logit_softcap);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    DecodePlan plan = plan_decode(c.op, di->sm_count);
+    if (workspace_bytes < plan.ws_bytes || (plan.ws_bytes && (!workspace || !aligned(workspace, 256)))) {
+        return ACEFA_ERR_WORKSPACE;
+    }
+    DecodeLaunch L;
+    std::memset(&L, 0, sizeof(L));
+    L.p.op             = c.op;
+    L.p.n_rb           = plan.n_rb;
+    L.p.units          = plan.units;
+    L.p.tiles_per_unit = plan.tpu;
+    L.p.total_tiles    = plan.total_tiles;
+    L.p.n_ctas         = plan.n_ctas;
+    L.p.partials       = static_cast<float *>(workspace);
+    L.p.dev_err        = di->err_ptr;
+    L.p.wait_limit_ns  = wait_limit_ns();
+    if (c.op.kv_type != ACEFA_TYPE_Q8_0) {
+        if ((rc = encode_kv_map(&L.kmap, k, c.op.D)) != ACEFA_OK || (rc = encode_kv_map(&L.vmap, v, c.op.D)) != ACEFA_OK) {
+            return rc;
+        }
+    }
+    int         launches = 0;
+    cudaError_t e        = launch_decode(L, s, &launches);
+    if (e != cudaSuccess) {
+        return ACEFA_ERR_CUDA;
+    }
+    t_last_launches = launches;
+    t_last_path     = 1;
+    return ACEFA_OK;
+}
+
+ACEFA_API int acefa_device_error(void *stream) {
+    DevInfo *di = nullptr;
+    int      rc = dev_info(&di);
+    if (rc != ACEFA_OK) {
+        return rc;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaStreamSynchronize(s) != cudaSuccess) {
+        return ACEFA_ERR_CUDA;
+    }
+    int v = 0;
+    if (cudaMemcpy(&v, di->err_ptr, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        return ACEFA_ERR_CUDA;
+    }
+    const int zero = 0;
+    if (cudaMemcpy(di->err_ptr, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+        return ACEFA_ERR_CUDA;
+    }
+    return v;
+}
+
+ACEFA_API const char *acefa_status_string(int status) {
+    switch (status) {
+        case ACEFA_OK: return "ok";
+        case ACEFA_ERR_NULL: return "null tensor or pointer";
+        case ACEFA_ERR_TYPE: return "unsupported element type";
+        case ACEFA_ERR_SHAPE: return "shapes violate the flash_attn_ext contract";
+        case ACEFA_ERR_LAYOUT: return "unsupported stride or alignment";
+        case ACEFA_ERR_WORKSPACE: return "workspace too small or misaligned";
+        case ACEFA_ERR_CUDA: return "CUDA call failed";
+        case ACEFA_ERR_DEVICE: return "device is not sm_100";
+        case ACEFA_ERR_DEVICE_TIMEOUT: return "device-side wait expired";
+        default: return "unknown status";
+    }
+}
+
+ACEFA_API int acefa_last_launch_count(void) { return t_last_launches; }
+ACEFA_API int acefa_last_path(void) { return t_last_path; }
+ACEFA_API int acefa_version(void) { return 100; }
+
+}  // extern "C"

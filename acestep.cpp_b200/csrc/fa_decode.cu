@@ -1,0 +1,802 @@
+// fa_decode.cu -- split-KV flash-decode for sm_100a.
+//
+// Serves ggml_flash_attn_ext nodes whose query side is small: acestep.cpp's
+// batched CFG decode (src/qwen3-lm.h:789-794: Q [128,1,Hq,N], K/V views
+// [128,n_kv_pad,8,N] of the F16 cache), single-sequence decode
+// (src/qwen3-lm.h:465-469 with n_tokens == 1) and the short FSQ encoders
+// (src/fsq-tok.h:183, src/fsq-detok.h:171; S = 5..6).
+//
+// Design (memory bound; the roofline is HBM bytes of K and V):
+//   * Work unit = (batch b, kv head hk, row block rb).  A unit's rows are the
+//     G*n_q (query, q-head) pairs that share K/V head hk, 16 per block, so each
+//     K/V byte is read once per unit and feeds G*n_q rows of tensor-core math.
+//   * The flattened (unit, 64-key tile) list is cut into equal contiguous
+//     ranges, one per persistent CTA (2 CTAs per SM).  A CTA that sees a unit
+//     only partly writes an unnormalised partial (m, l, O); the combine kernel
+//     merges partials.  Grid and splits depend on shapes only, so a captured
+//     CUDA graph replays with any mask contents.
+//   * Warp-specialised pipeline: one producer warp streams K/V tiles into a
+//     3-stage shared-memory ring -- TMA tensor tiles with 128-B swizzle for
+//     F16/BF16, 1-D bulk copies of whole 34-B-block rows for Q8_0 -- and skips
+//     tiles whose mask is entirely -inf (the padded decode window tail).
+//   * Four consumer warps each take 16 keys of every tile: S = Q K^T and O += P V
+//     on mma.sync m16n8k16 with F32 accumulation, online softmax in the log2
+//     domain with quad shuffles.  Q8_0 K/V are dequantised in registers
+//     (int8 -> f16 by exponent splicing, times the block scale).
+//   * Every mbarrier wait is bounded; on expiry the CTA records an error word,
+//     drains its in-flight copies (bounded) and exits.
+#include <cfloat>
+
+#include "fa_internal.h"
+#include "ptx.cuh"
+
+namespace acefa {
+
+namespace {
+
+constexpr int kMetaData  = 1;
+constexpr int kMetaFlush = 2;
+constexpr int kMetaTerm  = 3;
+
+constexpr uint16_t kHalfNegInf = 0xFC00u;
+
+template <int KV_TYPE, int D>
+struct DecCfg {
+    static constexpr bool kQ8        = KV_TYPE == ACEFA_TYPE_Q8_0;
+    static constexpr bool kBF16      = KV_TYPE == ACEFA_TYPE_BF16;
+    static constexpr int  kRowBytes  = kQ8 ? D / 32 * 34 : D * 2;
+    static constexpr int  kTileBytes = ((kDecBN * kRowBytes) + 1023) / 1024 * 1024;
+    static constexpr int  kStageBytes = 2 * kTileBytes;
+    static constexpr int  kMergeStride = D + 8;  // floats per merge row (bank spread)
+    // shared memory carve-up (offsets from the 1024-B aligned base)
+    static constexpr int kOffStages = 0;
+    static constexpr int kOffMerge  = kOffStages + kDecStages * kStageBytes;
+    static constexpr int kOffStats  = kOffMerge + kDecRows * kMergeStride * 4;  // m,l per warp per row
+    static constexpr int kOffBars   = kOffStats + 2 * kDecWarps * kDecRows * 4;
+    static constexpr int kOffMeta   = kOffBars + 2 * kDecStages * 8;
+    static constexpr int kOffFlags  = kOffMeta + kDecStages * 16;
+    static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
+    static constexpr int kThreads   = (kDecWarps + 1) * 32;
+};
+
+__device__ __forceinline__ int64_t cta_of_tile(int64_t t, int64_t T, int C) { return ((t + 1) * C - 1) / T; }
+
+struct UnitCoord {
+    int b, hk, rb, bk, rows;
+};
+
+__device__ __forceinline__ UnitCoord unit_coord(const DecodeParams &P, int u) {
+    UnitCoord c;
+    c.rb            = u % P.n_rb;
+    c.hk            = (u / P.n_rb) % P.op.Hkv;
+    c.b             = u / (P.n_rb * P.op.Hkv);
+    c.bk            = c.b / P.op.rk3;
+    const int total = P.op.G * P.op.n_q;
+    c.rows          = min(kDecRows, total - c.rb * kDecRows);
+    return c;
+}
+
+// Row rr of unit -> (query index iq, q head hq).
+__device__ __forceinline__ void row_coord(const DecodeParams &P, const UnitCoord &uc, int rr, int &iq, int &hq) {
+    const int gr = uc.rb * kDecRows + rr;
+    iq           = gr / P.op.G;
+    hq           = uc.hk * P.op.G + gr % P.op.G;
+}
+
+__device__ __forceinline__ const uint16_t *mask_row(const OpDesc &o, int iq, int hq, int b) {
+    return reinterpret_cast<const uint16_t *>(o.mask + (int64_t) iq * o.m_nb1 + (int64_t) (hq % o.m_ne2) * o.m_nb2 +
+                                              (int64_t) (b % o.m_ne3) * o.m_nb3);
+}
+
+// True if some mask entry of this tile, for some row of the unit, is not -inf.
+__device__ bool tile_live(const DecodeParams &P, const UnitCoord &uc, int tile) {
+    const OpDesc &o = P.op;
+    if (o.mask == nullptr) {
+        return true;
+    }
+    const int       j0   = tile * kDecBN;
+    const int       cnt  = min(kDecBN, o.n_kv - j0);
+    const uint16_t *prev = nullptr;
+    for (int rr = 0; rr < uc.rows; ++rr) {
+        int iq, hq;
+        row_coord(P, uc, rr, iq, hq);
+        const uint16_t *m = mask_row(o, iq, hq, uc.b);
+        if (m == prev) {
+            continue;
+        }
+        prev = m;
+        m += j0;
+        bool dead = true;
+        for (int j = 0; j < cnt; j += 8) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if (j + e < cnt) {
+                    dead &= (__ldg(m + j + e) == kHalfNegInf);
+                }
+            }
+            if (!dead) {
+                return true;
+            }
+        }
+    }
+    return false;
+}
+
+// -------------------------------------------------------------------------
+// int8 -> f16 pair helpers (exact): byte b becomes 1024 + (b ^ 0x80) by exponent
+// splicing; subtracting 1152 recovers the signed value exactly.
+__device__ __forceinline__ __half2 i8pair_to_h2(uint32_t spliced) {
+    const uint32_t t = (spliced & 0x00FF00FFu) ^ 0x64806480u;
+    return __hsub2(*reinterpret_cast<const __half2 *>(&t), __half2half2(__ushort_as_half((unsigned short) 0x6480u)));
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint16_t lds16(uint32_t addr) {
+    uint16_t v;
+    asm volatile("ld.shared.b16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
+// N bytes starting at a 2-B aligned shared address, as N/4 words.
+template <int NW>
+__device__ __forceinline__ void lds_bytes_unaligned(uint32_t addr, uint32_t (&out)[NW]) {
+    const uint32_t base = addr & ~3u;
+    const uint32_t sh   = (addr & 3u) * 8u;
+    uint32_t       w[NW + 1];
+#pragma unroll
+    for (int i = 0; i <= NW; ++i) {
+        w[i] = lds32(base + 4 * i);
+    }
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        out[i] = __funnelshift_r(w[i], w[i + 1], sh);
+    }
+}
+
+}  // namespace
+
+template <int KV_TYPE, int D>
+__global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
+    fa_decode_kernel(const __grid_constant__ DecodeParams P, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap) {
+    using Cfg                 = DecCfg<KV_TYPE, D>;
+    constexpr bool kQ8        = Cfg::kQ8;
+    constexpr bool kBF16      = Cfg::kBF16;
+    constexpr int  KS         = D / 16;  // k-steps over the head dim
+    constexpr int  NT         = D / 8;   // n8 tiles over the head dim
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    uint64_t     *full_bar  = reinterpret_cast<uint64_t *>(smem + Cfg::kOffBars);
+    uint64_t     *empty_bar = full_bar + kDecStages;
+    int4         *meta      = reinterpret_cast<int4 *>(smem + Cfg::kOffMeta);
+    volatile int *abort_f   = reinterpret_cast<volatile int *>(smem + Cfg::kOffFlags);
+    float        *merge     = reinterpret_cast<float *>(smem + Cfg::kOffMerge);
+    float        *s_m       = reinterpret_cast<float *>(smem + Cfg::kOffStats);
+    float        *s_l       = s_m + kDecWarps * kDecRows;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDecStages; ++i) {
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&empty_bar[i], kDecWarps);
+        }
+        *abort_f = 0;
+        fence_barrier_init();
+    }
+    for (int i = threadIdx.x; i < kDecRows * Cfg::kMergeStride; i += blockDim.x) {
+        merge[i] = 0.0f;
+    }
+    __syncthreads();
+
+    // Everything below reads tensors that an earlier kernel may have written.
+    pdl_wait_primary();
+    pdl_launch_dependents();
+
+    const OpDesc &o  = P.op;
+    const int64_t T  = P.total_tiles;
+    const int     C  = P.n_ctas;
+    const int64_t t0 = (int64_t) blockIdx.x * T / C;
+    const int64_t t1 = (int64_t) (blockIdx.x + 1) * T / C;
+    const int     tpu = P.tiles_per_unit;
+
+    if (warp == kDecWarps) {
+        // ============================ producer ============================
+        if (!kQ8 && lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+        }
+        int      stage = 0;
+        uint32_t phase = 0;
+        bool     ok    = true;
+        int      pend[kDecStages];  // parity of the last phase armed on each full barrier
+        for (int i = 0; i < kDecStages; ++i) {
+            pend[i] = -1;
+        }
+        auto advance = [&]() {
+            if (++stage == kDecStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        };
+        auto acquire = [&]() -> bool {
+            return mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_f, P.dev_err, DEVERR_TIMEOUT_EMPTY,
+                                     P.wait_limit_ns);
+        };
+        for (int64_t t = t0; t < t1 && ok;) {
+            const int       u   = (int) (t / tpu);
+            const int64_t   ue  = min(t1, (int64_t) (u + 1) * tpu);
+            const int       tlo = (int) (t - (int64_t) u * tpu);
+            const int       thi = (int) (ue - (int64_t) u * tpu);
+            const UnitCoord uc  = unit_coord(P, u);
+            const char *kbase = o.k + (int64_t) uc.hk * o.k_nb2 + (int64_t) uc.bk * o.k_nb3;
+            const char *vbase = o.v + (int64_t) uc.hk * o.v_nb2 + (int64_t) uc.bk * o.v_nb3;
+            for (int tb = tlo; tb < thi && ok; tb += 32) {
+                const int  tile = tb + lane;
+                const bool live = tile < thi && tile_live(P, uc, tile);
+                uint32_t   bits = __ballot_sync(0xffffffffu, live);
+                while (bits && ok) {
+                    const int i = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    const int ti = tb + i;
+                    ok           = acquire();
+                    if (!ok) {
+                        break;
+                    }
+                    uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
+                    uint8_t *sV = sK + Cfg::kTileBytes;
+                    if constexpr (kQ8) {
+                        const int      j0    = ti * kDecBN;
+                        const int      nrows = min(kDecBN, o.n_kv - j0);
+                        const uint32_t bytes = (uint32_t) nrows * Cfg::kRowBytes;
+                        const uint32_t bulk  = bytes & ~15u;
+                        const char    *kg    = kbase + (int64_t) j0 * Cfg::kRowBytes;
+                        const char    *vg    = vbase + (int64_t) j0 * Cfg::kRowBytes;
+                        // ragged tail (< 16 B): plain copies, made visible to the
+                        // async proxy before the next TMA reuses the stage
+                        if ((uint32_t) lane < bytes - bulk) {
+                            sK[bulk + lane] = (uint8_t) kg[bulk + lane];
+                            sV[bulk + lane] = (uint8_t) vg[bulk + lane];
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            meta[stage] = make_int4(u, ti, kMetaData, 0);
+                            mbar_arrive_expect_tx(&full_bar[stage], 2 * bulk);
+                            bulk_load(sK, kg, bulk, &full_bar[stage]);
+                            bulk_load(sV, vg, bulk, &full_bar[stage]);
+                        }
+                    } else {
+                        if (lane == 0) {
+                            meta[stage] = make_int4(u, ti, kMetaData, 0);
+                            mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) Cfg::kStageBytes);
+#pragma unroll
+                            for (int h = 0; h < D / 64; ++h) {
+                                tma_load_4d(sK + h * kDecBN * 128, &kmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
+                                            &full_bar[stage]);
+                                tma_load_4d(sV + h * kDecBN * 128, &vmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
+                                            &full_bar[stage]);
+                            }
+                        }
+                    }
+                    pend[stage] = (int) phase;
+                    __syncwarp();
+                    advance();
+                }
+            }
+            if (!ok) {
+                break;
+            }
+            ok = acquire();
+            if (!ok) {
+                break;
+            }
+            if (lane == 0) {
+                meta[stage] = make_int4(u, 0, kMetaFlush, 0);
+                mbar_arrive(&full_bar[stage]);
+            }
+            pend[stage] = (int) phase;
+            __syncwarp();
+            advance();
+            t = ue;
+        }
+        if (ok) {
+            ok = acquire();
+            if (ok && lane == 0) {
+                meta[stage] = make_int4(-1, 0, kMetaTerm, 0);
+                mbar_arrive(&full_bar[stage]);
+            }
+        }
+        if (!ok) {
+            // Aborting: let the last copy armed on each stage land before the CTA
+            // exits (a phase can never run more than one ahead of its last arm).
+            for (int i = 0; i < kDecStages; ++i) {
+                if (pend[i] < 0) {
+                    continue;
+                }
+                const uint64_t t_start = globaltimer_ns();
+                while (!mbar_try_wait(&full_bar[i], (uint32_t) pend[i])) {
+                    if (globaltimer_ns() - t_start > P.wait_limit_ns) {
+                        atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_DRAIN);
+                        break;
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ============================== consumers ==============================
+    const int g = lane >> 2;  // fragment row group
+    const int c = lane & 3;   // fragment column pair
+    int       stage = 0;
+    uint32_t  phase = 0;
+
+    int       cur_unit = -1;
+    UnitCoord uc{};
+    float     m_run[2], l_run[2];
+    float     oacc[NT][4];
+    uint32_t  qa[KS][4];
+    const uint16_t *mrow[2];
+    float     slope[2];
+
+    auto setup_unit = [&](int u) {
+        uc = unit_coord(P, u);
+        m_run[0] = m_run[1] = -INFINITY;
+        l_run[0] = l_run[1] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                oacc[j][e] = 0.0f;
+            }
+        }
+        const float *qrow[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int rr = g + 8 * i;
+            int       iq, hq;
+            row_coord(P, uc, rr < uc.rows ? rr : 0, iq, hq);
+            qrow[i]  = rr < uc.rows ? reinterpret_cast<const float *>(o.q + (int64_t) iq * o.q_nb1 +
+                                                                     (int64_t) hq * o.q_nb2 + (int64_t) uc.b * o.q_nb3)
+                                    : nullptr;
+            mrow[i]  = o.mask ? mask_row(o, iq, hq, uc.b) : nullptr;
+            slope[i] = alibi_slope(o, hq);
+        }
+        auto qv = [&](int i, int d) -> float { return qrow[i] ? __ldg(qrow[i] + d) : 0.0f; };
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            if constexpr (kQ8) {
+                // dims permuted so each thread's K bytes are one contiguous run
+                const int d0 = c * (D / 4) + 4 * ks;
+                qa[ks][0]    = pack2<false>(qv(0, d0), qv(0, d0 + 1));
+                qa[ks][1]    = pack2<false>(qv(1, d0), qv(1, d0 + 1));
+                qa[ks][2]    = pack2<false>(qv(0, d0 + 2), qv(0, d0 + 3));
+                qa[ks][3]    = pack2<false>(qv(1, d0 + 2), qv(1, d0 + 3));
+            } else {
+                const int d0 = 16 * ks + 2 * c;
+                qa[ks][0]    = pack2<kBF16>(qv(0, d0), qv(0, d0 + 1));
+                qa[ks][1]    = pack2<kBF16>(qv(1, d0), qv(1, d0 + 1));
+                qa[ks][2]    = pack2<kBF16>(qv(0, d0 + 8), qv(0, d0 + 9));
+                qa[ks][3]    = pack2<kBF16>(qv(1, d0 + 8), qv(1, d0 + 9));
+            }
+        }
+    };
+
+    // Head-dim index held by accumulator element (j, e) (column part only).
+    auto out_dim = [&](int j, int e) -> int {
+        if constexpr (kQ8) {
+            return (D / 8) * (2 * c + (e & 1)) + j;
+        } else {
+            return 8 * j + 2 * c + (e & 1);
+        }
+    };
+
+    auto process_tile = [&](const uint8_t *sK, const uint8_t *sV, int tile) {
+        float s[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                s[nt][e] = 0.0f;
+            }
+        }
+        // ---- S = Q K^T over this warp's 16 keys
+        if constexpr (kQ8) {
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const int      row   = 16 * warp + 8 * nt + g;
+                const int      dim0  = c * (D / 4);
+                const uint32_t rbase = smem_u32(sK) + row * Cfg::kRowBytes + (dim0 / 32) * 34;
+                uint32_t       qw[D / 16];
+                lds_bytes_unaligned<D / 16>(rbase + 2 + (dim0 % 32), qw);
+                const __half  dsc = __ushort_as_half(lds16(rbase));
+                const __half2 d2  = __half2half2(dsc);
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    const __half2 lo = __hmul2(i8pair_to_h2(__byte_perm(qw[ks], 0, 0x4140)), d2);
+                    const __half2 hi = __hmul2(i8pair_to_h2(__byte_perm(qw[ks], 0, 0x4342)), d2);
+                    mma_16816<false>(s[nt], qa[ks], *reinterpret_cast<const uint32_t *>(&lo),
+                                     *reinterpret_cast<const uint32_t *>(&hi));
+                }
+            }
+        } else {
+            const int mi   = lane >> 3;
+            const int r8   = lane & 7;
+            const int krow = 16 * warp + (mi >> 1) * 8 + r8;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int      dim  = 16 * ks + (mi & 1) * 8;
+                const uint32_t addr = smem_u32(sK) + (dim >> 6) * (kDecBN * 128) + krow * 128 +
+                                      ((((dim & 63) >> 3) ^ r8) << 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(addr, b0, b1, b2, b3);
+                mma_16816<kBF16>(s[0], qa[ks], b0, b1);
+                mma_16816<kBF16>(s[1], qa[ks], b2, b3);
+            }
+        }
+        // ---- scale, softcap, mask, bounds; to log2 units
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i   = e >> 1;
+                const int pos = tile * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1);
+                float     x   = s[nt][e] * o.scale_eff;
+                if (o.softcap != 0.0f) {
+                    x = o.softcap * tanhf(x);
+                }
+                if (pos < o.n_kv) {
+                    if (mrow[i]) {
+                        // a -inf entry removes the key outright, whatever K held there
+                        const float mv = slope[i] * __half2float(__ushort_as_half(__ldg(mrow[i] + pos)));
+                        x              = mv == -INFINITY ? -INFINITY : x + mv;
+                    }
+                    x *= kLog2e;
+                } else {
+                    x = -INFINITY;
+                }
+                s[nt][e] = x;
+            }
+        }
+        // ---- online softmax (rows g and g+8)
+        float alpha[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            float mx = fmaxf(fmaxf(s[0][2 * i], s[0][2 * i + 1]), fmaxf(s[1][2 * i], s[1][2 * i + 1]));
+            mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mnew = fmaxf(m_run[i], mx);
+            const float muse = mnew == -INFINITY ? 0.0f : mnew;
+            alpha[i]         = fast_exp2(m_run[i] - muse);
+            m_run[i]         = mnew;
+            float rs         = 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                s[nt][2 * i]     = fast_exp2(s[nt][2 * i] - muse);
+                s[nt][2 * i + 1] = fast_exp2(s[nt][2 * i + 1] - muse);
+                rs += s[nt][2 * i] + s[nt][2 * i + 1];
+            }
+            l_run[i] = l_run[i] * alpha[i] + rs;
+        }
+        if (__any_sync(0xffffffffu, alpha[0] != 1.0f || alpha[1] != 1.0f)) {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                oacc[j][0] *= alpha[0];
+                oacc[j][1] *= alpha[0];
+                oacc[j][2] *= alpha[1];
+                oacc[j][3] *= alpha[1];
+            }
+        }
+        // ---- O += P V
+        constexpr bool kPB = kQ8 ? false : kBF16;
+        uint32_t       pa[4];
+        pa[0] = pack2<kPB>(s[0][0], s[0][1]);
+        pa[1] = pack2<kPB>(s[0][2], s[0][3]);
+        pa[2] = pack2<kPB>(s[1][0], s[1][1]);
+        pa[3] = pack2<kPB>(s[1][2], s[1][3]);
+        if constexpr (kQ8) {
+            // this thread's B fragments: keys 2c,2c+1 (b0) and 2c+8,2c+9 (b1) of the
+            // warp's 16, head dims (D/8)*g .. +D/8 (one contiguous byte run per key)
+            const int dim0 = (D / 8) * g;
+            uint32_t  qv[4][D / 32];
+            __half    dv[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int      key   = 16 * warp + 2 * c + (r & 1) + 8 * (r >> 1);
+                const uint32_t rbase = smem_u32(sV) + key * Cfg::kRowBytes + (dim0 / 32) * 34;
+                lds_bytes_unaligned<D / 32>(rbase + 2 + (dim0 % 32), qv[r]);
+                dv[r] = __ushort_as_half(lds16(rbase));
+            }
+            const __half2 d01 = __halves2half2(dv[0], dv[1]);
+            const __half2 d89 = __halves2half2(dv[2], dv[3]);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const int      wi  = j >> 2;
+                const uint32_t sel = (uint32_t) (j & 3) | ((uint32_t) (4 + (j & 3)) << 8);
+                const __half2  b0  = __hmul2(i8pair_to_h2(__byte_perm(qv[0][wi], qv[1][wi], sel)), d01);
+                const __half2  b1  = __hmul2(i8pair_to_h2(__byte_perm(qv[2][wi], qv[3][wi], sel)), d89);
+                mma_16816<false>(oacc[j], pa, *reinterpret_cast<const uint32_t *>(&b0),
+                                 *reinterpret_cast<const uint32_t *>(&b1));
+            }
+        } else {
+            const int mi   = lane >> 3;
+            const int r8   = lane & 7;
+            const int vrow = 16 * warp + (mi & 1) * 8 + r8;
+#pragma unroll
+            for (int dn = 0; dn < D / 16; ++dn) {
+                const int      dim  = 16 * dn + (mi >> 1) * 8;
+                const uint32_t addr = smem_u32(sV) + (dim >> 6) * (kDecBN * 128) + vrow * 128 +
+                                      ((((dim & 63) >> 3) ^ r8) << 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(addr, b0, b1, b2, b3);
+                mma_16816<kBF16>(oacc[2 * dn], pa, b0, b1);
+                mma_16816<kBF16>(oacc[2 * dn + 1], pa, b2, b3);
+            }
+        }
+    };
+
+    auto flush_unit = [&](int u) {
+        // per-warp row statistics
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 2);
+        }
+        if (c == 0) {
+            s_m[warp * kDecRows + g]     = m_run[0];
+            s_m[warp * kDecRows + g + 8] = m_run[1];
+            s_l[warp * kDecRows + g]     = l_run[0];
+            s_l[warp * kDecRows + g + 8] = l_run[1];
+        }
+        named_bar_sync(1, kDecWarps * 32);
+        float fac[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int row = g + 8 * i;
+            float     mx  = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kDecWarps; ++w) {
+                mx = fmaxf(mx, s_m[w * kDecRows + row]);
+            }
+            fac[i] = m_run[i] == -INFINITY ? 0.0f : fast_exp2(m_run[i] - mx);
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = g + 8 * (e >> 1);
+                atomicAdd(&merge[row * Cfg::kMergeStride + out_dim(j, e)], oacc[j][e] * fac[e >> 1]);
+            }
+        }
+        named_bar_sync(1, kDecWarps * 32);
+        const int64_t cf     = cta_of_tile((int64_t) u * tpu, T, C);
+        const int64_t cl     = cta_of_tile((int64_t) (u + 1) * tpu - 1, T, C);
+        const bool    direct = cf == cl;
+        float        *slot   = P.partials + (int64_t) (blockIdx.x + u) * dec_slot_floats(D);
+        for (int idx = threadIdx.x; idx < kDecRows * D; idx += kDecWarps * 32) {
+            const int row = idx / D;
+            const int d   = idx % D;
+            float    *mp  = &merge[row * Cfg::kMergeStride + d];
+            if (row < uc.rows) {
+                float mx = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kDecWarps; ++w) {
+                    mx = fmaxf(mx, s_m[w * kDecRows + row]);
+                }
+                float l = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kDecWarps; ++w) {
+                    const float mw = s_m[w * kDecRows + row];
+                    l += mw == -INFINITY ? 0.0f : s_l[w * kDecRows + row] * fast_exp2(mw - mx);
+                }
+                float acc = *mp;
+                if (direct) {
+                    int iq, hq;
+                    row_coord(P, uc, row, iq, hq);
+                    if (o.sinks) {
+                        const float ts = o.sinks[hq] * kLog2e;
+                        if (ts > mx) {
+                            const float f = fast_exp2(mx - ts);
+                            acc *= f;
+                            l = l * f + 1.0f;
+                        } else {
+                            l += fast_exp2(ts - mx);
+                        }
+                    }
+                    const float out = l == 0.0f ? 0.0f : acc / l;
+                    *reinterpret_cast<float *>(o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 +
+                                               (int64_t) iq * o.d_nb2 + (int64_t) uc.b * o.d_nb3) = out;
+                } else {
+                    if (d == 0) {
+                        slot[row]            = mx;
+                        slot[kDecRows + row] = l;
+                    }
+                    slot[2 * kDecRows + row * D + d] = acc;
+                }
+            }
+            *mp = 0.0f;
+        }
+        named_bar_sync(1, kDecWarps * 32);
+    };
+
+    while (true) {
+        if (!mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err, DEVERR_TIMEOUT_FULL, P.wait_limit_ns)) {
+            break;
+        }
+        const int4 md = meta[stage];
+        if (md.z == kMetaTerm) {
+            break;
+        }
+        if (md.x != cur_unit) {
+            setup_unit(md.x);
+            cur_unit = md.x;
+        }
+        if (md.z == kMetaData) {
+            const uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
+            process_tile(sK, sK + Cfg::kTileBytes, md.y);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&empty_bar[stage]);
+        }
+        if (md.z == kMetaFlush) {
+            flush_unit(cur_unit);
+            cur_unit = -1;
+        }
+        if (++stage == kDecStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Combine: merge the partials of every unit split across CTAs.
+template <int D>
+__global__ void __launch_bounds__(D) fa_decode_combine(const __grid_constant__ DecodeParams P) {
+    pdl_wait_primary();
+    const OpDesc &o   = P.op;
+    const int     u   = blockIdx.x;
+    const int64_t T   = P.total_tiles;
+    const int     C   = P.n_ctas;
+    const int     tpu = P.tiles_per_unit;
+    const int64_t cf  = cta_of_tile((int64_t) u * tpu, T, C);
+    const int64_t cl  = cta_of_tile((int64_t) (u + 1) * tpu - 1, T, C);
+    if (cf == cl) {
+        return;
+    }
+    const UnitCoord uc = unit_coord(P, u);
+    const int       d  = threadIdx.x;
+    for (int row = 0; row < uc.rows; ++row) {
+        float mx = -INFINITY;
+        for (int64_t cta = cf; cta <= cl; ++cta) {
+            mx = fmaxf(mx, P.partials[(cta + u) * dec_slot_floats(D) + row]);
+        }
+        float l = 0.0f, acc = 0.0f;
+        for (int64_t cta = cf; cta <= cl; ++cta) {
+            const float *slot = P.partials + (cta + u) * dec_slot_floats(D);
+            const float  mc   = slot[row];
+            if (mc == -INFINITY) {
+                continue;
+            }
+            const float f = fast_exp2(mc - mx);
+            l += f * slot[kDecRows + row];
+            acc += f * slot[2 * kDecRows + row * D + d];
+        }
+        int iq, hq;
+        row_coord(P, uc, row, iq, hq);
+        if (o.sinks) {
+            const float ts = o.sinks[hq] * kLog2e;
+            if (ts > mx) {
+                const float f = fast_exp2(mx - ts);
+                acc *= f;
+                l = l * f + 1.0f;
+            } else {
+                l += fast_exp2(ts - mx);
+            }
+        }
+        const float out = l == 0.0f ? 0.0f : acc / l;
+        *reinterpret_cast<float *>(o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
+                                   (int64_t) uc.b * o.d_nb3) = out;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+namespace {
+
+template <int KV_TYPE, int D>
+cudaError_t launch_impl(const DecodeLaunch &L, cudaStream_t s, int *launches) {
+    using Cfg = DecCfg<KV_TYPE, D>;
+    auto kern = fa_decode_kernel<KV_TYPE, D>;
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+        if (e != cudaSuccess) {
+            return e;
+        }
+        configured_dev = dev;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) L.p.n_ctas);
+    cfg.blockDim           = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes   = Cfg::kSmemBytes;
+    cfg.stream             = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = attr;
+    cfg.numAttrs                                       = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, L.p, L.kmap, L.vmap);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    int n = 1;
+    // The combine only has work when some unit spans several CTAs.
+    if (decode_needs_combine(L.p)) {
+        cudaLaunchConfig_t c2 = cfg;
+        c2.gridDim            = dim3((unsigned) L.p.units);
+        c2.blockDim           = dim3(D);
+        c2.dynamicSmemBytes   = 0;
+        e                     = cudaLaunchKernelEx(&c2, fa_decode_combine<D>, L.p);
+        if (e != cudaSuccess) {
+            return e;
+        }
+        n = 2;
+    }
+    if (launches) {
+        *launches = n;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+bool decode_needs_combine(const DecodeParams &p) {
+    // a unit is split iff some CTA range boundary falls strictly inside it
+    for (int c = 1; c < p.n_ctas; ++c) {
+        const int64_t lo = (int64_t) c * p.total_tiles / p.n_ctas;
+        if (lo % p.tiles_per_unit != 0) {
+            return true;
+        }
+    }
+    return false;
+}
+
+cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches) {
+    const int t = L.p.op.kv_type, D = L.p.op.D;
+    if (t == ACEFA_TYPE_F16 && D == 128) return launch_impl<ACEFA_TYPE_F16, 128>(L, s, launches);
+    if (t == ACEFA_TYPE_F16 && D == 64) return launch_impl<ACEFA_TYPE_F16, 64>(L, s, launches);
+    if (t == ACEFA_TYPE_BF16 && D == 128) return launch_impl<ACEFA_TYPE_BF16, 128>(L, s, launches);
+    if (t == ACEFA_TYPE_BF16 && D == 64) return launch_impl<ACEFA_TYPE_BF16, 64>(L, s, launches);
+    if (t == ACEFA_TYPE_Q8_0 && D == 128) return launch_impl<ACEFA_TYPE_Q8_0, 128>(L, s, launches);
+    if (t == ACEFA_TYPE_Q8_0 && D == 64) return launch_impl<ACEFA_TYPE_Q8_0, 64>(L, s, launches);
+    return cudaErrorInvalidValue;
+}
+
+size_t decode_smem_bytes(int kv_type, int D) {
+    if (kv_type == ACEFA_TYPE_Q8_0) {
+        return D == 128 ? DecCfg<ACEFA_TYPE_Q8_0, 128>::kSmemBytes : DecCfg<ACEFA_TYPE_Q8_0, 64>::kSmemBytes;
+    }
+    return D == 128 ? DecCfg<ACEFA_TYPE_F16, 128>::kSmemBytes : DecCfg<ACEFA_TYPE_F16, 64>::kSmemBytes;
+}
+
+int decode_ctas_per_sm(int kv_type, int D) {
+    // Two CTAs per SM share the 228 KB of shared memory; the launch bounds ask
+    // the register allocator for the same.
+    const size_t per = decode_smem_bytes(kv_type, D) + 1024;  // + per-CTA reserve
+    return per * 2 <= 228 * 1024 ? 2 : 1;
+}
+
+}  // namespace acefa

@@ -1,0 +1,93 @@
+// fa_internal.h -- host/device shared parameter blocks of the attention kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/acefa.h"
+
+namespace acefa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Operands after host-side validation, in ggml terms.  Strides in bytes.
+struct OpDesc {
+    // Q [D, n_q, Hq, B] f32
+    const char *q;
+    int64_t     q_nb1, q_nb2, q_nb3;
+    // K/V [D, n_kv, Hkv, Bk]
+    const char *k, *v;
+    int64_t     k_nb1, k_nb2, k_nb3;
+    int64_t     v_nb1, v_nb2, v_nb3;
+    int         kv_type;  // ACEFA_TYPE_F16 / BF16 / Q8_0
+    // mask [>=n_kv, >=n_q, m_ne2, m_ne3] f16 (nullptr = none)
+    const char *mask;
+    int64_t     m_nb1, m_nb2, m_nb3;
+    int         m_ne2, m_ne3;
+    // sinks [Hq] f32 (nullptr = none)
+    const float *sinks;
+    // dst [D, Hq, n_q, B] f32
+    char   *dst;
+    int64_t d_nb0, d_nb1, d_nb2, d_nb3;
+    // shapes
+    int D, n_q, Hq, B, n_kv, Hkv, Bk;
+    int G;    // Hq / Hkv
+    int rk3;  // B / Bk
+    // scalars
+    float scale_eff;  // scale, divided by softcap when softcap != 0
+    float softcap;
+    float max_bias, alibi_m0, alibi_m1;
+    int   n_head_log2;
+};
+
+__host__ __device__ inline float alibi_slope(const OpDesc &o, int h) {
+    if (o.max_bias <= 0.0f) {
+        return 1.0f;
+    }
+#ifdef __CUDA_ARCH__
+    return h < o.n_head_log2 ? powf(o.alibi_m0, (float) (h + 1)) : powf(o.alibi_m1, (float) (2 * (h - o.n_head_log2) + 1));
+#else
+    return h < o.n_head_log2 ? powf(o.alibi_m0, (float) (h + 1)) : powf(o.alibi_m1, (float) (2 * (h - o.n_head_log2) + 1));
+#endif
+}
+
+// ------------------------------------------------------------------ decode
+// The split-KV decode kernel works on "units" (batch b, kv head hk, row block
+// rb); a unit's rows are the G*n_q (query, head) pairs that share one K/V head,
+// 16 at a time.  Its keys are cut into tiles of kDecBN positions and the
+// flattened (unit, tile) list is split evenly over the persistent CTAs.
+constexpr int kDecBN      = 64;  // keys per pipeline stage
+constexpr int kDecWarps   = 4;   // consumer warps (16 keys each per stage)
+constexpr int kDecStages  = 3;   // pipeline depth
+constexpr int kDecRows    = 16;  // rows per unit (one m16 MMA tile)
+
+struct DecodeParams {
+    OpDesc  op;
+    int     n_rb;            // row blocks per (b, hk)
+    int     units;           // B * Hkv * n_rb
+    int     tiles_per_unit;  // ceil(n_kv / kDecBN)
+    int64_t total_tiles;     // units * tiles_per_unit
+    int     n_ctas;          // persistent CTAs
+    float  *partials;        // workspace: (n_ctas + units) slots
+    int    *dev_err;
+    uint64_t wait_limit_ns;
+};
+
+// Slot layout: m[kDecRows], l[kDecRows], O[kDecRows][D] (f32).
+__host__ __device__ inline int64_t dec_slot_floats(int D) { return (int64_t) kDecRows * (D + 2); }
+
+struct DecodeLaunch {
+    DecodeParams p;
+    CUtensorMap  kmap, vmap;  // F16/BF16 tiles via TMA (unused for Q8_0)
+};
+
+cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches);
+bool        decode_needs_combine(const DecodeParams &p);
+int         decode_ctas_per_sm(int kv_type, int D);
+size_t      decode_smem_bytes(int kv_type, int D);
+
+// ------------------------------------------------------------------ dense
+struct DenseParams;  // defined in fa_dense.cu
+
+}  // namespace acefa

@@ -1,0 +1,427 @@
+"""Benchmark of the acefa attention engine on BASELINE config 2.
+
+Workload (one "step"): the decode attention of a Qwen3-4B layer stack -- 36
+ggml_flash_attn_ext ops, one per layer, each over that layer's own F16 KV cache
+of 16 sets (8 requests x CFG cond/uncond), Hq=32 / Hkv=8, D=128, KV length
+8192.  Inputs are seeded N(0,1) synthetic tensors resident in HBM; every layer's
+KV (537 MB) is larger than L2, so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N>1 runs under torchrun, one process per GPU; requests are sharded with no
+collective on the data path (each rank owns a full 8-request batch: weak
+scaling).  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "acestep.cpp_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+# ---- BASELINE config 2 (the metric's headline configuration) -------------
+LAYERS, HQ, HKV, D = 36, 32, 8, 128
+SETS, KV_LEN = 16, 8192
+SEED = 42 + 1000 * 2
+
+
+def algo_bytes_per_op(sets=SETS, kv_len=KV_LEN, kv_bytes_per_row=2 * D, hq=HQ, hkv=HKV, d=D, mask=True):
+    """Algorithmic HBM bytes of one decode op: K+V rows read once, Q read,
+    O written (f32), mask read once per set."""
+    kv = sets * hkv * kv_len * kv_bytes_per_row * 2
+    qo = sets * hq * d * 4 * 2
+    m = sets * kv_len * 2 if mask else 0
+    return kv + qo + m
+
+
+def read_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def read_traffic(kernel_key):
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    try:
+        with open(p) as f:
+            return json.load(f).get(kernel_key, {}).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# -------------------------------------------------------------------------
+def cpu_baseline(budget_s=12.0, threads=None):
+    """The reference operator's CPU arithmetic (oracle, ggml-cpu mode) on a
+    bounded sample of the same workload: whole layers of config 2."""
+    import numpy as np
+
+    import oracle
+
+    threads = threads or os.cpu_count()
+    rng = np.random.default_rng(SEED)
+    q = rng.standard_normal((SETS, HQ, 1, D), dtype=np.float32)
+    k = rng.standard_normal((SETS, HKV, KV_LEN, D), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((SETS, HKV, KV_LEN, D), dtype=np.float32).astype(np.float16)
+    m = np.zeros((SETS, 1, 1, KV_LEN), np.float16)
+    oracle.flash_attn_ext(q[:1], k[:1], v[:1], m[:1], scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.flash_attn_ext(q, k, v, m, scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=threads)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or n >= 200:
+            break
+    gbs = n * algo_bytes_per_op() / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} layer(s) of the config-2 decode op (16 sets x 8192 keys, F16 KV) in {dt:.1f} s; "
+                      f"oracle/fa_oracle.c ggml-cpu arithmetic, OpenMP"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    import oracle
+
+    threads = os.cpu_count()
+    rng = np.random.default_rng(SEED)
+    q = rng.standard_normal((SETS, HQ, 1, D), dtype=np.float32)
+    k = rng.standard_normal((SETS, HKV, KV_LEN, D), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((SETS, HKV, KV_LEN, D), dtype=np.float32).astype(np.float16)
+    m = np.zeros((SETS, 1, 1, KV_LEN), np.float16)
+
+    def step():  # one bounded sample: one layer of the stack
+        oracle.flash_attn_ext(q, k, v, m, scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    gbs = args.steps * algo_bytes_per_op() / dt / 1e9
+    line = {
+        "impl": "reference", "metric": "decode_attention_hbm_gbs", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1), seed 2042",
+        "config": config_dict(args, note="one step = one layer of the stack on the host CPU"),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "one layer (16 sets x 8192 keys) per step; the reference's ggml "
+                                   "kernels are absent from its tree, so the CPU restatement "
+                                   "(oracle/fa_oracle.c, ggml-cpu arithmetic) stands in"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(args, note=None):
+    c = {"workload": "qwen3-4b decode attention stack (BASELINE config 2): 36 layers x ggml_flash_attn_ext, "
+                     "8 requests x CFG = 16 KV sets, Hq 32 / Hkv 8, D 128, KV 8192, F16 KV, mask [8192,1,1,16]",
+         "layers": LAYERS, "kv_sets_per_gpu": SETS, "kv_len": KV_LEN, "head_dim": D, "q_heads": HQ,
+         "kv_heads": HKV, "kv_type": "f16", "l2": "inputs larger than L2 (537 MB of KV per op); no flush",
+         "parallelism": f"requests sharded one batch per GPU x{args.gpus}, no collective"}
+    if note:
+        c["note"] = note
+    return c
+
+
+# -------------------------------------------------------------------------
+def build_stack(device, kv="f16", layers=LAYERS, sets=SETS, kv_len=KV_LEN, seed=SEED):
+    import torch
+
+    import acefa
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    ops, hosts = [], []
+    mask = torch.zeros(sets, 1, 1, kv_len, device=device, dtype=torch.float16)
+    ws = None
+    for _ in range(layers):
+        q = torch.randn(sets, HQ, 1, D, device=device, generator=g)
+        kf = torch.randn(sets, HKV, kv_len, D, device=device, generator=g, dtype=torch.float16)
+        vf = torch.randn(sets, HKV, kv_len, D, device=device, generator=g, dtype=torch.float16)
+        if kv == "q8_0":
+            k, v, kt = acefa.quantize_q8_0(kf), acefa.quantize_q8_0(vf), acefa.GGML_Q8_0
+            del kf, vf
+        else:
+            k, v, kt = kf, vf, None
+        op = acefa.Op(q, k, v, mask=mask, kv_type=kt, scale=D ** -0.5)
+        if ws is None or ws.numel() < op.workspace.numel():
+            ws = op.workspace
+        ops.append(op)
+    for op in ops:  # one pooled workspace, like ggml-cuda's pool (ops run stream-ordered)
+        op.workspace = ws
+    return ops, mask
+
+
+def time_graph(ops, steps, warmup, stream):
+    import torch
+
+    for _ in range(2):
+        for op in ops:
+            op(stream=stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for op in ops:
+            op(stream=stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    return graph
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import acefa
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    stream = torch.cuda.Stream(device=device)
+    per_op = algo_bytes_per_op()
+    with torch.cuda.stream(stream):
+        ops, mask = build_stack(device, seed=SEED + 7919 * rank)
+        launches_per_op = 0
+        ops[0](stream=stream)
+        launches_per_op = acefa.last_launch_count()
+        graph = time_graph(ops, args.steps, max(args.warmup, 3), stream)
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    step_bytes = per_op * LAYERS
+    value = world * step_bytes * args.steps / (ms_max / 1e3) / 1e9
+    assert acefa.device_error(stream) == 0
+
+    # ---- end to end through the C ABI with host buffers ----------------------
+    q_host = [torch.empty_like(op.q, device="cpu").pin_memory() for op in ops]
+    for qh, op in zip(q_host, ops):
+        qh.copy_(op.q)
+    m_host = torch.empty_like(mask, device="cpu").pin_memory()
+    m_host.copy_(mask)
+    o_host = [torch.empty_like(op.out, device="cpu").pin_memory() for op in ops]
+    e2e_steps = max(2, min(args.steps, 10))
+
+    def e2e_step():
+        mask.copy_(m_host, non_blocking=True)
+        for qh, op in zip(q_host, ops):
+            op.q.copy_(qh, non_blocking=True)
+        for op in ops:
+            op(stream=stream)
+        for oh, op in zip(o_host, ops):
+            oh.copy_(op.out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_gbs = world * step_bytes * e2e_steps / (float(te.item()) / 1e3) / 1e9
+    h2d = mask.numel() * mask.element_size() + sum(op.q.numel() * 4 for op in ops)
+    d2h = sum(op.out.numel() * 4 for op in ops)
+
+    out = None
+    if rank == 0:
+        peak, peak_kind = read_peaks()
+        per_launch_s = (ms_step / 1e3) / LAYERS
+        achieved = per_op / per_launch_s / 1e9
+        out = {
+            "metric": "decode_attention_hbm_gbs", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1) K/V/Q, seeded (2042 + 7919*rank); random values, zero mask",
+            "config": config_dict(args),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": read_traffic("fa_decode_kernel_f16_d128"),
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "fa_decode_kernel<F16,128> (+combine)",
+                         "algo_bytes_per_launch": per_op},
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h),
+                    "how": "pinned H2D of mask + 36 Q, 36 C-ABI calls, D2H of 36 outputs, CUDA events"},
+            "gpu_launches": int(launches_per_op * LAYERS * args.steps),
+            "clocks": clk.summary(),
+        }
+    # free the F16 stack before optional extras
+    del graph, ops
+    torch.cuda.empty_cache()
+
+    if rank == 0 and not args.no_extras:
+        out["extras"] = extras(device, stream, args)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+def extras(device, stream, args):
+    """Secondary figures on rank 0: Q8_0 KV stack and the config-1 single op."""
+    import torch
+
+    res = {}
+    peak, _ = read_peaks()
+    with torch.cuda.stream(stream):
+        ops, _ = build_stack(device, kv="q8_0", seed=SEED + 1)
+        graph = time_graph(ops, 5, 3, stream)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(5):
+            graph.replay()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1) / 5
+        qb = algo_bytes_per_op(kv_bytes_per_row=D // 32 * 34) * LAYERS
+        res["q8_0_stack"] = {"gbs": round(qb / (ms / 1e3) / 1e9, 1), "ms_per_step": round(ms, 4),
+                             "frac_of_hbm_peak": round(qb / (ms / 1e3) / 1e9 / peak, 4)}
+        del graph, ops
+        torch.cuda.empty_cache()
+        # config 1: one Qwen3-0.6B decode op (8.4 MB), many back-to-back in a graph
+        import acefa
+
+        g = torch.Generator(device=device).manual_seed(42 + 1000)
+        reps = 64
+        ops = []
+        for _ in range(reps):
+            q = torch.randn(1, 16, 1, D, device=device, generator=g)
+            k = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
+            v = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
+            m = torch.zeros(1, 1, 1, 2048, device=device, dtype=torch.float16)
+            ops.append(acefa.Op(q, k, v, mask=m, scale=D ** -0.5))
+        graph = time_graph(ops, 10, 3, stream)
+        s0.record(stream)
+        for _ in range(10):
+            graph.replay()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) * 1e3 / (10 * reps)
+        b1 = 8_409_088
+        res["config1_single_op"] = {"us_per_op": round(us, 2), "gbs": round(b1 / (us / 1e6) / 1e9, 1),
+                                    "note": "64 distinct ops back to back in one CUDA graph (8.4 MB each)"}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,136 @@
+/*
+ * acefa.h -- C ABI of the B200 (sm_100a) attention engine behind acestep.cpp's
+ * ggml_flash_attn_ext operator.
+ *
+ * The engine replaces the CUDA-side execution of one GGML_OP_FLASH_ATTN_EXT
+ * graph node.  acestep.cpp creates those nodes at
+ *   src/qwen3-lm.h:465-469    (LM prefill / single decode, PREC_F32)
+ *   src/qwen3-lm.h:789-794    (LM batched CFG decode, PREC_F32)
+ *   src/qwen3-enc.h:195-199   (text / lyric / timbre / FSQ encoders)
+ *   src/dit-graph.h:227-231   (DiT self-attention)
+ *   src/dit-graph.h:348-352   (DiT cross-attention)
+ * and ggml's CUDA backend executes them in its per-node switch
+ * (case GGML_OP_FLASH_ATTN_EXT -> ggml_cuda_flash_attn_ext(ctx, dst) in the
+ * ggml fork that acestep.cpp pins as a submodule, .gitmodules:1-3).  That call
+ * is what acefa_flash_attn_ext() replaces; acefa_supports() replaces the
+ * GGML_OP_FLASH_ATTN_EXT branch of ggml_backend_cuda_device_supports_op, which
+ * acestep.cpp's static_graph_alloc consults (src/static-graph.h:12-19).
+ *
+ * Tensors use ggml's conventions: ne[0] innermost, nb[] byte strides, type ids
+ * equal to enum ggml_type.  All data pointers are device pointers owned by the
+ * caller (ggml's allocator).  No entry point allocates device memory, synchronises
+ * the stream or aborts; every call is safe inside CUDA-graph stream capture.
+ */
+#ifndef ACEFA_H
+#define ACEFA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define ACEFA_API __attribute__((visibility("default")))
+#else
+#define ACEFA_API
+#endif
+
+/* Same numeric values as enum ggml_type. */
+typedef enum acefa_type {
+    ACEFA_TYPE_F32  = 0,
+    ACEFA_TYPE_F16  = 1,
+    ACEFA_TYPE_Q8_0 = 8,
+    ACEFA_TYPE_BF16 = 30,
+} acefa_type;
+
+/* Same numeric values as enum ggml_prec (ggml_flash_attn_ext_set_prec). */
+typedef enum acefa_prec {
+    ACEFA_PREC_DEFAULT = 0,
+    ACEFA_PREC_F32     = 10,
+} acefa_prec;
+
+typedef enum acefa_status {
+    ACEFA_OK             = 0,
+    ACEFA_ERR_NULL       = -1, /* a required tensor or pointer is NULL */
+    ACEFA_ERR_TYPE       = -2, /* unsupported element type */
+    ACEFA_ERR_SHAPE      = -3, /* shapes violate the ggml_flash_attn_ext contract */
+    ACEFA_ERR_LAYOUT     = -4, /* stride/alignment this engine does not support */
+    ACEFA_ERR_WORKSPACE  = -5, /* workspace too small or not 256-B aligned */
+    ACEFA_ERR_CUDA       = -6, /* a CUDA runtime/driver call failed */
+    ACEFA_ERR_DEVICE     = -7, /* current device is not sm_100 */
+    ACEFA_ERR_DEVICE_TIMEOUT = -8, /* a bounded device-side wait expired */
+} acefa_status;
+
+/* ggml_tensor reduced to what the operator reads. */
+typedef struct acefa_tensor {
+    int32_t type;  /* acefa_type */
+    int64_t ne[4]; /* elements per dimension, ne[0] innermost */
+    size_t  nb[4]; /* byte strides; for Q8_0 nb[0] = 34 (block bytes) */
+    void   *data;  /* device pointer */
+} acefa_tensor;
+
+/*
+ * dst = softmax(scale * Q K^T [softcap] + slope * mask [+ sinks]) V, permuted.
+ *
+ *   q     [D,  n_q,  Hq,  B ]  F32, any strides with nb[0] == 4
+ *   k     [D,  n_kv, Hkv, Bk]  F16, BF16 or Q8_0; Hq % Hkv == 0, B % Bk == 0
+ *   v     [Dv, n_kv, Hkv, Bk]  same type as k, Dv == D
+ *   mask  [>=n_kv, >=n_q, Hm, Bm] F16 or NULL; Hq % Hm == 0, B % Bm == 0
+ *   sinks [Hq] F32 or NULL (extra softmax logit per head, no value row)
+ *   dst   [Dv, Hq, n_q, B] F32
+ *
+ * scale, max_bias (ALiBi) and logit_softcap have ggml's meaning.  prec is
+ * accepted for either value; accumulation is always F32.  stream is a
+ * cudaStream_t (NULL = legacy default stream).  workspace must hold
+ * acefa_workspace_bytes() bytes, 256-B aligned, caller-owned; its contents need
+ * no initialisation and are dead after the call's kernels finish.
+ * Returns ACEFA_OK or a negative acefa_status; launches nothing on error.
+ */
+ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                   const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst,
+                                   float scale, float max_bias, float logit_softcap, int prec, void *stream,
+                                   void *workspace, size_t workspace_bytes);
+
+/* Workspace the call above needs for these operands on the current device
+ * (split-KV partial results, mask tile classes).  A function of shapes, types
+ * and the device only -- never of tensor contents -- so it can be sized once
+ * before CUDA-graph capture.  Returns 0 for unsupported operands. */
+ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                       const acefa_tensor *mask, const acefa_tensor *dst);
+
+/* 1 if acefa_flash_attn_ext accepts these operands, else 0 (mirrors
+ * ggml_backend_cuda_device_supports_op for GGML_OP_FLASH_ATTN_EXT; when it
+ * returns 0 the ggml scheduler keeps the node on the CPU backend). */
+ACEFA_API int acefa_supports(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                             const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst);
+
+/* Validation only: the status acefa_flash_attn_ext would return before
+ * launching (ACEFA_OK when the operands are accepted).  Touches no device. */
+ACEFA_API int acefa_check(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                          const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst);
+
+/* Reads and clears the device-side error word set by bounded waits inside the
+ * kernels (0 = none).  Synchronises `stream`; for diagnostics, not hot paths.
+ * Returns a negative acefa_status if the read itself fails. */
+ACEFA_API int acefa_device_error(void *stream);
+
+/* Human-readable name of an acefa_status. */
+ACEFA_API const char *acefa_status_string(int status);
+
+/* Kernel-launch count of the last successful acefa_flash_attn_ext call on this
+ * host thread (1 to 3: mask classification, attention, split-KV combine). */
+ACEFA_API int acefa_last_launch_count(void);
+
+/* Which kernel family served the last successful call on this thread:
+ * 1 = split-KV decode (mma.sync), 2 = dense tcgen05/TMEM. */
+ACEFA_API int acefa_last_path(void);
+
+/* ABI version: major*10000 + minor*100 + patch. */
+ACEFA_API int acefa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ACEFA_H */

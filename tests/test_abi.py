@@ -1,0 +1,155 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the header
+declares, and validates operands exactly like the ggml operator contract."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+import acefa
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "acefa.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("acestep_build", os.path.join(ROOT, "acestep.cpp_b200", "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
+    return acefa.load_library()
+
+
+def header_functions():
+    txt = open(HEADER).read()
+    return re.findall(r"ACEFA_API\s+[\w\s\*]+?\b(acefa_\w+)\s*\(", txt)
+
+
+def test_header_declares_expected_api():
+    names = header_functions()
+    assert set(names) == set(acefa.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.check_output(["nm", "-D", "--defined-only", acefa.LIB_PATH], text=True)
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    for name in header_functions():
+        assert name in exported, name
+        assert hasattr(lib, name)
+    # nothing else leaks out of the library's C++ internals
+    leaked = [s for s in exported if s.startswith("_ZN5acefa")]
+    assert not leaked, leaked[:5]
+
+
+def test_status_strings(lib):
+    for code in range(-8, 1):
+        s = lib.acefa_status_string(code)
+        assert s and s != b"unknown status"
+    assert lib.acefa_version() >= 100
+
+
+def _td(shape_ne, nb, gtype, ptr=256):
+    t = acefa.Tensor()
+    t.type = gtype
+    t.ne[:] = shape_ne
+    t.nb[:] = nb
+    t.data = ptr
+    return t
+
+
+def _contig(ne, es):
+    nb = [es]
+    for i in range(1, 4):
+        nb.append(nb[-1] * ne[i - 1])
+    return nb
+
+
+def _ops(D=128, nq=1, Hq=16, B=1, nkv=2048, Hkv=8, Bk=1, kt=acefa.GGML_F16, mask=True):
+    q = _td([D, nq, Hq, B], _contig([D, nq, Hq, B], 4), acefa.GGML_F32)
+    if kt == acefa.GGML_Q8_0:
+        knb = [34, D // 32 * 34, D // 32 * 34 * nkv, D // 32 * 34 * nkv * Hkv]
+    else:
+        knb = _contig([D, nkv, Hkv, Bk], 2)
+    k = _td([D, nkv, Hkv, Bk], knb, kt)
+    v = _td([D, nkv, Hkv, Bk], knb, kt)
+    m = _td([nkv, nq, 1, B], _contig([nkv, nq, 1, B], 2), acefa.GGML_F16) if mask else None
+    d = _td([D, Hq, nq, B], _contig([D, Hq, nq, B], 4), acefa.GGML_F32)
+    return q, k, v, m, d
+
+
+def _check(lib, q, k, v, m, d, s=None):
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    return lib.acefa_check(r(q), r(k), r(v), r(m), r(s), r(d))
+
+
+def test_check_accepts_reference_shapes(lib):
+    # config 1 (Qwen3-0.6B decode), config 2 (4B batched decode), DiT self/cross
+    assert _check(lib, *_ops()) == 0
+    assert _check(lib, *_ops(Hq=32, B=16, Bk=16, nkv=8192)) == 0
+    assert _check(lib, *_ops(Hq=32, B=16, Bk=16, nkv=8192, kt=acefa.GGML_Q8_0)) == 0
+    assert _check(lib, *_ops(nq=1500, Hq=16, Hkv=16, B=2, Bk=2, nkv=1500, mask=False)) == 0
+    assert _check(lib, *_ops(nq=6000, Hq=16, Hkv=16, B=2, Bk=2, nkv=512)) == 0
+    assert _check(lib, *_ops(D=64, kt=acefa.GGML_BF16)) == 0
+
+
+def test_check_rejects_contract_violations(lib):
+    q, k, v, m, d = _ops()
+    assert _check(lib, None, k, v, m, d) == -1
+    bad = _ops(Hq=12, Hkv=8)  # 12 % 8 != 0
+    assert _check(lib, *bad) == -3
+    q2, k2, v2, m2, d2 = _ops()
+    q2.type = acefa.GGML_F16
+    assert _check(lib, q2, k2, v2, m2, d2) == -2
+    q3, k3, v3, m3, d3 = _ops()
+    v3.type = acefa.GGML_BF16  # K and V types differ
+    assert _check(lib, q3, k3, v3, m3, d3) == -2
+    q4, k4, v4, m4, d4 = _ops()
+    m4.ne[0] = 100  # mask narrower than n_kv
+    assert _check(lib, q4, k4, v4, m4, d4) == -3
+    q5, k5, v5, m5, d5 = _ops(D=96)
+    assert _check(lib, q5, k5, v5, m5, d5) == -3
+    q6, k6, v6, m6, d6 = _ops()
+    k6.nb[1] = 264  # row stride not 16-B aligned
+    assert _check(lib, q6, k6, v6, m6, d6) == -4
+    q7, k7, v7, m7, d7 = _ops()
+    k7.data = 256 + 8  # K base not 16-B aligned
+    assert _check(lib, q7, k7, v7, m7, d7) == -4
+    q8, k8, v8, m8, d8 = _ops()
+    d8.ne[1] = 8  # dst not [D, Hq, n_q, B]
+    assert _check(lib, q8, k8, v8, m8, d8) == -3
+    q9, k9, v9, m9, d9 = _ops(kt=acefa.GGML_Q8_0)
+    k9.nb[1] = 144  # Q8_0 rows must be contiguous blocks
+    assert _check(lib, q9, k9, v9, m9, d9) == -4
+
+
+def test_supports_mirrors_check(lib):
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    ok = _ops()
+    assert lib.acefa_supports(*[r(x) for x in ok[:4]], None, r(ok[4])) == 1
+    bad = _ops(Hq=12)
+    assert lib.acefa_supports(*[r(x) for x in bad[:4]], None, r(bad[4])) == 0
+
+
+def test_flash_attn_without_gpu_fails_cleanly(lib):
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    q, k, v, m, d = _ops()
+    st = lib.acefa_flash_attn_ext(r(q), r(k), r(v), r(m), None, r(d), 0.088, 0.0, 0.0, 10, None, None, 0)
+    assert st in (-6, -7)  # CUDA error / not an sm_100 device: no launch, no crash
+    assert lib.acefa_workspace_bytes(r(q), r(k), r(v), r(m), r(d)) == 0
+
+
+def test_torch_q8_0_quantiser_bit_exact(oracle_mod):
+    x = np.load(os.path.join(ROOT, "tests", "golden", "q8_0_input.npy"))
+    want = np.load(os.path.join(ROOT, "tests", "golden", "q8_0_gguf.npy"))
+    got = acefa.quantize_q8_0(torch.from_numpy(x)).numpy()
+    assert np.array_equal(got, want)
+    back = acefa.dequantize_q8_0(torch.from_numpy(want)).numpy()
+    assert np.array_equal(back, oracle_mod.dequantize_q8_0(want))

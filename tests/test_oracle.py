@@ -1,0 +1,88 @@
+"""CPU tests of the oracle: Q8_0 pinned against gguf, attention cross-checked
+against independent float64 fixtures, and the ggml-cpu (F16 accumulation)
+mode's known drift."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def test_q8_0_matches_gguf_bit_exact(oracle_mod):
+    x = np.load(os.path.join(GOLDEN, "q8_0_input.npy"))
+    want = np.load(os.path.join(GOLDEN, "q8_0_gguf.npy"))
+    got = oracle_mod.quantize_q8_0(x)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+
+
+def test_q8_0_dequant_roundtrip(oracle_mod):
+    x = np.load(os.path.join(GOLDEN, "q8_0_input.npy"))
+    y = oracle_mod.quantize_q8_0(x)
+    xr = oracle_mod.dequantize_q8_0(y)
+    blocks = x.reshape(x.shape[0], -1, 32)
+    d = np.abs(blocks).max(-1, keepdims=True) / np.float32(127.0)
+    d16 = d.astype(np.float16).astype(np.float32)
+    err = np.abs(xr.reshape(blocks.shape) - blocks)
+    # half a quantisation step plus the f16 rounding of the block scale
+    assert np.all(err <= 0.5 * d * (1 + 1e-5) + 127.0 * np.abs(d - d16) + 1e-30)
+
+
+def _load_case(path):
+    z = np.load(path)
+    return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "attn_case_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[10:-4])
+def test_oracle_matches_float64_fixtures(oracle_mod, path):
+    c = _load_case(path)
+    out = oracle_mod.flash_attn_ext(c["q"], c["k"], c["v"], c.get("mask"), c.get("sinks"), scale=float(c["scale"]),
+                                    max_bias=float(c["max_bias"]), softcap=float(c["softcap"]))
+    np.testing.assert_allclose(out, c["out"], atol=2e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "attn_case_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[10:-4])
+def test_ggml_cpu_mode_close_to_f32(oracle_mod, path):
+    """The ggml-cpu restatement (F16 Q and V accumulator) drifts but stays close."""
+    c = _load_case(path)
+    kw = dict(scale=float(c["scale"]), max_bias=float(c["max_bias"]), softcap=float(c["softcap"]))
+    ref = oracle_mod.flash_attn_ext(c["q"], c["k"], c["v"], c.get("mask"), c.get("sinks"), **kw)
+    g = oracle_mod.flash_attn_ext(c["q"], c["k"], c["v"], c.get("mask"), c.get("sinks"),
+                                  mode=oracle_mod.MODE_GGML_CPU, **kw)
+    assert np.abs(g - ref).max() < 2e-2
+    # rows with no visible key are exactly zero in both modes
+    assert np.array_equal(ref == 0, g == 0) or np.abs(g - ref).max() < 2e-2
+
+
+def test_all_masked_row_is_zero(oracle_mod):
+    rng = np.random.default_rng(42)
+    q = rng.standard_normal((1, 2, 3, 64)).astype(np.float32)
+    k = rng.standard_normal((1, 1, 10, 64)).astype(np.float16)
+    v = rng.standard_normal((1, 1, 10, 64)).astype(np.float16)
+    m = np.zeros((1, 1, 3, 10), np.float16)
+    m[0, 0, 1, :] = -np.inf
+    out = oracle_mod.flash_attn_ext(q, k, v, m, scale=0.125)
+    assert np.all(out[0, 1] == 0.0)
+    assert np.all(np.abs(out[0, 0]) > 0)
+
+
+def test_q8_0_kv_oracle_equals_dequantised_f32(oracle_mod):
+    rng = np.random.default_rng(43)
+    q = rng.standard_normal((2, 4, 1, 128)).astype(np.float32)
+    kf = rng.standard_normal((2, 2, 70, 128)).astype(np.float32)
+    vf = rng.standard_normal((2, 2, 70, 128)).astype(np.float32)
+    kq, vq = oracle_mod.quantize_q8_0(kf), oracle_mod.quantize_q8_0(vf)
+    a = oracle_mod.flash_attn_ext(q, kq, vq, scale=0.088, k_type=oracle_mod.GGML_Q8_0, v_type=oracle_mod.GGML_Q8_0)
+    b = oracle_mod.flash_attn_ext(q, oracle_mod.dequantize_q8_0(kq), oracle_mod.dequantize_q8_0(vq), scale=0.088)
+    np.testing.assert_allclose(a, b, atol=1e-6, rtol=1e-6)
+
+
+def test_contract_violations_rejected(oracle_mod):
+    q = np.zeros((1, 3, 1, 64), np.float32)  # Hq = 3
+    k = np.zeros((1, 2, 8, 64), np.float16)  # Hkv = 2 does not divide 3
+    with pytest.raises(ValueError):
+        oracle_mod.flash_attn_ext(q, k, k, scale=1.0)
