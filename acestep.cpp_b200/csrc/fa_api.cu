@@ -184,7 +184,10 @@ Checked check_operands(const acefa_tensor *q, const acefa_tensor *k, const acefa
                 return fail(ACEFA_ERR_LAYOUT);
             }
         }
-        if ((t->ne[2] > 1 && t->nb[2] % 16) || (t->ne[3] > 1 && t->nb[3] % 16)) {
+        // F16/BF16 go through TMA tensor maps (16-B strides); Q8_0 tiles are
+        // copied from the 16-B boundary below them, so even strides suffice.
+        const size_t sa = t->type == ACEFA_TYPE_Q8_0 ? 2 : 16;
+        if ((t->ne[2] > 1 && t->nb[2] % sa) || (t->ne[3] > 1 && t->nb[3] % sa)) {
             return fail(ACEFA_ERR_LAYOUT);
         }
     }
@@ -199,7 +202,7 @@ Checked check_operands(const acefa_tensor *q, const acefa_tensor *k, const acefa
     if (mask) {
         o.mask  = static_cast<const char *>(mask->data);
         o.m_nb1 = mask->nb[1], o.m_nb2 = mask->nb[2], o.m_nb3 = mask->nb[3];
-        o.m_ne2 = (int) mask->ne[2], o.m_ne3 = (int) mask->ne[3];
+        o.m_ne0 = (int) mask->ne[0], o.m_ne2 = (int) mask->ne[2], o.m_ne3 = (int) mask->ne[3];
     } else {
         o.m_ne2 = o.m_ne3 = 1;
     }
@@ -237,7 +240,11 @@ DecodePlan plan_decode(const OpDesc &o, int sm_count) {
     p.units          = o.B * o.Hkv * p.n_rb;
     p.tpu            = (o.n_kv + kDecBN - 1) / kDecBN;
     p.total_tiles    = (int64_t) p.units * p.tpu;
-    const int64_t cap = (int64_t) sm_count * decode_ctas_per_sm(o.kv_type, o.D);
+    // persistent CTAs fill the SMs, but no unit is cut into more than
+    // ~kDecMaxParts pieces (small ops would otherwise pay for a wide combine)
+    int64_t cap = (int64_t) sm_count * decode_ctas_per_sm(o.kv_type, o.D);
+    const int64_t part_cap = (int64_t) p.units * kDecMaxParts;
+    cap = cap < part_cap ? cap : part_cap;
     p.n_ctas         = (int) (p.total_tiles < cap ? p.total_tiles : cap);
     p.ws_bytes       = (size_t) (p.n_ctas + p.units) * (size_t) dec_slot_floats(o.D) * sizeof(float);
     p.ws_bytes       = (p.ws_bytes + 255) / 256 * 256;

@@ -45,8 +45,14 @@ struct DecCfg {
     static constexpr bool kQ8        = KV_TYPE == ACEFA_TYPE_Q8_0;
     static constexpr bool kBF16      = KV_TYPE == ACEFA_TYPE_BF16;
     static constexpr int  kRowBytes  = kQ8 ? D / 32 * 34 : D * 2;
-    static constexpr int  kTileBytes = ((kDecBN * kRowBytes) + 1023) / 1024 * 1024;
-    static constexpr int  kStageBytes = 2 * kTileBytes;
+    // F16/BF16: exactly the TMA boxes (D/64 swizzled 64-key x 128-B boxes).
+    // Q8_0: raw rows plus up to 15 lead bytes, rounded to keep stages 1 KB aligned.
+    static constexpr int  kTmaBytes  = kDecBN * kRowBytes;
+    static constexpr int  kTileBytes = kQ8 ? ((kDecBN * kRowBytes + 16) + 1023) / 1024 * 1024 : kTmaBytes;
+    static constexpr int  kMaskBytes  = kDecRows * kDecBN * 2;  // up to 16 mask rows x 64 keys (f16)
+    static constexpr int  kStageBytes = 2 * kTileBytes + kMaskBytes;
+    static_assert(kQ8 || kTileBytes % 1024 == 0, "TMA 128-B swizzle needs 1 KB aligned boxes");
+    static_assert(kStageBytes % 1024 == 0, "stages must stay 1 KB aligned");
     static constexpr int  kMergeStride = D + 8;  // floats per merge row (bank spread)
     // shared memory carve-up (offsets from the 1024-B aligned base)
     static constexpr int kOffStages = 0;
@@ -128,6 +134,13 @@ __device__ bool tile_live(const DecodeParams &P, const UnitCoord &uc, int tile) 
 __device__ __forceinline__ __half2 i8pair_to_h2(uint32_t spliced) {
     const uint32_t t = (spliced & 0x00FF00FFu) ^ 0x64806480u;
     return __hsub2(*reinterpret_cast<const __half2 *>(&t), __half2half2(__ushort_as_half((unsigned short) 0x6480u)));
+}
+
+// Residual of a bf16x2 rounding: bf16(x - float(bf16(x))) for both lanes.
+__device__ __forceinline__ uint32_t split_lo_bf16(float x0, float x1, uint32_t hi) {
+    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162 *>(&hi);
+    const float2         f = __bfloat1622float2(h);
+    return pack2<true>(x0 - f.x, x1 - f.y);
 }
 
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
@@ -230,6 +243,31 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             return mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_f, P.dev_err, DEVERR_TIMEOUT_EMPTY,
                                      P.wait_limit_ns);
         };
+        // Stage the mask segment [64*ti, 64*ti + 64) of every slot row.  Returns
+        // the bytes the caller must add to the barrier's transaction count (the
+        // bulk-copy case, issued by the caller after arming the barrier); rows
+        // that are not 16-B aligned, or a segment running past the mask's row
+        // length, are copied here with plain loads instead.
+        auto stage_mask = [&](int ti, int n_ms, const uint16_t *my_mr, bool bulk, uint8_t *dst) -> uint32_t {
+            if (n_ms == 0) {
+                return 0;
+            }
+            const int j0 = ti * kDecBN;
+            if (bulk && j0 + kDecBN <= o.m_ne0) {
+                return (uint32_t) (n_ms * kDecBN * 2);
+            }
+            uint16_t *d16 = reinterpret_cast<uint16_t *>(dst);
+            for (int sl = 0; sl < n_ms; ++sl) {
+                const uint16_t *src = reinterpret_cast<const uint16_t *>(
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(my_mr), sl));
+                for (int j = lane; j < kDecBN; j += 32) {
+                    d16[sl * kDecBN + j] = j0 + j < o.m_ne0 ? __ldg(src + j0 + j) : kHalfNegInf;
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            return 0;
+        };
         for (int64_t t = t0; t < t1 && ok;) {
             const int       u   = (int) (t / tpu);
             const int64_t   ue  = min(t1, (int64_t) (u + 1) * tpu);
@@ -238,6 +276,29 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             const UnitCoord uc  = unit_coord(P, u);
             const char *kbase = o.k + (int64_t) uc.hk * o.k_nb2 + (int64_t) uc.bk * o.k_nb3;
             const char *vbase = o.v + (int64_t) uc.hk * o.v_nb2 + (int64_t) uc.bk * o.v_nb3;
+            // Mask slots: the distinct mask rows this unit reads (one per query
+            // index when the mask is shared by all heads).  Lane s owns slot s and
+            // stages its 64-key segment of every tile into shared memory.
+            int             n_ms   = 0;
+            const uint16_t *my_mr  = nullptr;
+            if (o.mask) {
+                if (o.m_ne2 == 1) {
+                    const int iq0 = (uc.rb * kDecRows) / o.G;
+                    n_ms          = (uc.rb * kDecRows + uc.rows - 1) / o.G - iq0 + 1;
+                    if (lane < n_ms) {
+                        my_mr = mask_row(o, iq0 + lane, 0, uc.b);
+                    }
+                } else {
+                    n_ms = uc.rows;
+                    if (lane < n_ms) {
+                        int iq, hq;
+                        row_coord(P, uc, lane, iq, hq);
+                        my_mr = mask_row(o, iq, hq, uc.b);
+                    }
+                }
+            }
+            const bool mask_bulk =
+                __all_sync(0xffffffffu, lane >= n_ms || (reinterpret_cast<uintptr_t>(my_mr) & 15u) == 0);
             for (int tb = tlo; tb < thi && ok; tb += 32) {
                 const int  tile = tb + lane;
                 const bool live = tile < thi && tile_live(P, uc, tile);
@@ -253,30 +314,47 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
                     uint8_t *sV = sK + Cfg::kTileBytes;
                     if constexpr (kQ8) {
-                        const int      j0    = ti * kDecBN;
-                        const int      nrows = min(kDecBN, o.n_kv - j0);
-                        const uint32_t bytes = (uint32_t) nrows * Cfg::kRowBytes;
-                        const uint32_t bulk  = bytes & ~15u;
-                        const char    *kg    = kbase + (int64_t) j0 * Cfg::kRowBytes;
-                        const char    *vg    = vbase + (int64_t) j0 * Cfg::kRowBytes;
-                        // ragged tail (< 16 B): plain copies, made visible to the
-                        // async proxy before the next TMA reuses the stage
-                        if ((uint32_t) lane < bytes - bulk) {
-                            sK[bulk + lane] = (uint8_t) kg[bulk + lane];
-                            sV[bulk + lane] = (uint8_t) vg[bulk + lane];
+                        // Rows are contiguous 34-B blocks; a tile starts at any even
+                        // address.  Copy from the 16-B boundary below it (inside the
+                        // tensor: its base is 16-B aligned) and let the consumers
+                        // index from the lead; the last <16 bytes go by plain copies.
+                        const int      j0     = ti * kDecBN;
+                        const int      nrows  = min(kDecBN, o.n_kv - j0);
+                        const uint32_t bytes  = (uint32_t) nrows * Cfg::kRowBytes;
+                        const char    *kg     = kbase + (int64_t) j0 * Cfg::kRowBytes;
+                        const char    *vg     = vbase + (int64_t) j0 * Cfg::kRowBytes;
+                        const uint32_t lead_k = (uint32_t) (reinterpret_cast<uintptr_t>(kg) & 15u);
+                        const uint32_t lead_v = (uint32_t) (reinterpret_cast<uintptr_t>(vg) & 15u);
+                        const uint32_t bulk_k = (lead_k + bytes) & ~15u;
+                        const uint32_t bulk_v = (lead_v + bytes) & ~15u;
+                        if ((uint32_t) lane < lead_k + bytes - bulk_k) {
+                            sK[bulk_k + lane] = (uint8_t) kg[(int) (bulk_k + lane) - (int) lead_k];
                         }
+                        if ((uint32_t) lane < lead_v + bytes - bulk_v) {
+                            sV[bulk_v + lane] = (uint8_t) vg[(int) (bulk_v + lane) - (int) lead_v];
+                        }
+                        const uint32_t mbytes = stage_mask(ti, n_ms, my_mr, mask_bulk, sK + 2 * Cfg::kTileBytes);
                         fence_proxy_async_smem();
                         __syncwarp();
+                        if (mbytes && lane < n_ms) {
+                            bulk_load(sK + 2 * Cfg::kTileBytes + lane * kDecBN * 2, my_mr + ti * kDecBN, kDecBN * 2,
+                                      &full_bar[stage]);
+                        }
                         if (lane == 0) {
-                            meta[stage] = make_int4(u, ti, kMetaData, 0);
-                            mbar_arrive_expect_tx(&full_bar[stage], 2 * bulk);
-                            bulk_load(sK, kg, bulk, &full_bar[stage]);
-                            bulk_load(sV, vg, bulk, &full_bar[stage]);
+                            meta[stage] = make_int4(u, ti, kMetaData, (int) (lead_k | (lead_v << 8)));
+                            mbar_arrive_expect_tx(&full_bar[stage], bulk_k + bulk_v + mbytes);
+                            if (bulk_k) {
+                                bulk_load(sK, kg - lead_k, bulk_k, &full_bar[stage]);
+                            }
+                            if (bulk_v) {
+                                bulk_load(sV, vg - lead_v, bulk_v, &full_bar[stage]);
+                            }
                         }
                     } else {
+                        const uint32_t mbytes = stage_mask(ti, n_ms, my_mr, mask_bulk, sK + 2 * Cfg::kTileBytes);
                         if (lane == 0) {
                             meta[stage] = make_int4(u, ti, kMetaData, 0);
-                            mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) Cfg::kStageBytes);
+                            mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) (2 * Cfg::kTmaBytes) + mbytes);
 #pragma unroll
                             for (int h = 0; h < D / 64; ++h) {
                                 tma_load_4d(sK + h * kDecBN * 128, &kmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
@@ -284,6 +362,11 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                                 tma_load_4d(sV + h * kDecBN * 128, &vmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
                                             &full_bar[stage]);
                             }
+                        }
+                        __syncwarp();
+                        if (mbytes && lane < n_ms) {
+                            bulk_load(sK + 2 * Cfg::kTileBytes + lane * kDecBN * 2, my_mr + ti * kDecBN, kDecBN * 2,
+                                      &full_bar[stage]);
                         }
                     }
                     pend[stage] = (int) phase;
@@ -344,7 +427,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     float     m_run[2], l_run[2];
     float     oacc[NT][4];
     uint32_t  qa[KS][4];
-    const uint16_t *mrow[2];
+    // BF16 operands keep ~16 mantissa bits of Q and P by a hi + lo split
+    // (two MMAs each); the F16 and Q8_0 paths never touch qlo.
+    uint32_t  qlo[kBF16 ? KS : 1][4];
+    int       mslot[2];  // mask slot (staged row) of fragment rows g and g+8
     float     slope[2];
 
     auto setup_unit = [&](int u) {
@@ -367,7 +453,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             qrow[i]  = rr < uc.rows ? reinterpret_cast<const float *>(o.q + (int64_t) iq * o.q_nb1 +
                                                                      (int64_t) hq * o.q_nb2 + (int64_t) uc.b * o.q_nb3)
                                     : nullptr;
-            mrow[i]  = o.mask ? mask_row(o, iq, hq, uc.b) : nullptr;
+            mslot[i] = o.m_ne2 == 1 ? iq - (uc.rb * kDecRows) / o.G : (rr < uc.rows ? rr : 0);
             slope[i] = alibi_slope(o, hq);
         }
         auto qv = [&](int i, int d) -> float { return qrow[i] ? __ldg(qrow[i] + d) : 0.0f; };
@@ -381,11 +467,17 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                 qa[ks][2]    = pack2<false>(qv(0, d0 + 2), qv(0, d0 + 3));
                 qa[ks][3]    = pack2<false>(qv(1, d0 + 2), qv(1, d0 + 3));
             } else {
-                const int d0 = 16 * ks + 2 * c;
-                qa[ks][0]    = pack2<kBF16>(qv(0, d0), qv(0, d0 + 1));
-                qa[ks][1]    = pack2<kBF16>(qv(1, d0), qv(1, d0 + 1));
-                qa[ks][2]    = pack2<kBF16>(qv(0, d0 + 8), qv(0, d0 + 9));
-                qa[ks][3]    = pack2<kBF16>(qv(1, d0 + 8), qv(1, d0 + 9));
+                const int d0  = 16 * ks + 2 * c;
+                const int ii[4] = {0, 1, 0, 1};
+                const int dd[4] = {d0, d0, d0 + 8, d0 + 8};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const float x0 = qv(ii[r], dd[r]), x1 = qv(ii[r], dd[r] + 1);
+                    qa[ks][r]      = pack2<kBF16>(x0, x1);
+                    if constexpr (kBF16) {
+                        qlo[ks][r] = split_lo_bf16(x0, x1, qa[ks][r]);
+                    }
+                }
             }
         }
     };
@@ -399,7 +491,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         }
     };
 
-    auto process_tile = [&](const uint8_t *sK, const uint8_t *sV, int tile) {
+    auto process_tile = [&](const uint8_t *sK, const uint8_t *sV, const uint16_t *sM, int tile) {
         float s[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
@@ -431,6 +523,14 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             const int mi   = lane >> 3;
             const int r8   = lane & 7;
             const int krow = 16 * warp + (mi >> 1) * 8 + r8;
+            float s2[2][4];  // second accumulator chain (odd k-steps) for more MMA overlap
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    s2[nt][e] = 0.0f;
+                }
+            }
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
                 const int      dim  = 16 * ks + (mi & 1) * 8;
@@ -438,8 +538,20 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                                       ((((dim & 63) >> 3) ^ r8) << 4);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(addr, b0, b1, b2, b3);
-                mma_16816<kBF16>(s[0], qa[ks], b0, b1);
-                mma_16816<kBF16>(s[1], qa[ks], b2, b3);
+                float(&acc)[2][4] = (!kBF16 && (ks & 1)) ? s2 : s;  // BF16 already pairs hi+lo MMAs
+                mma_16816<kBF16>(acc[0], qa[ks], b0, b1);
+                mma_16816<kBF16>(acc[1], qa[ks], b2, b3);
+                if constexpr (kBF16) {
+                    mma_16816<true>(acc[0], qlo[ks], b0, b1);
+                    mma_16816<true>(acc[1], qlo[ks], b2, b3);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    s[nt][e] += s2[nt][e];
+                }
             }
         }
         // ---- scale, softcap, mask, bounds; to log2 units
@@ -454,9 +566,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     x = o.softcap * tanhf(x);
                 }
                 if (pos < o.n_kv) {
-                    if (mrow[i]) {
+                    if (o.mask) {
                         // a -inf entry removes the key outright, whatever K held there
-                        const float mv = slope[i] * __half2float(__ushort_as_half(__ldg(mrow[i] + pos)));
+                        const float mv = slope[i] * __half2float(__ushort_as_half(
+                                                        sM[mslot[i] * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1)]));
                         x              = mv == -INFINITY ? -INFINITY : x + mv;
                     }
                     x *= kLog2e;
@@ -502,6 +615,13 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         pa[1] = pack2<kPB>(s[0][2], s[0][3]);
         pa[2] = pack2<kPB>(s[1][0], s[1][1]);
         pa[3] = pack2<kPB>(s[1][2], s[1][3]);
+        uint32_t palo[4];
+        if constexpr (kBF16) {
+            palo[0] = split_lo_bf16(s[0][0], s[0][1], pa[0]);
+            palo[1] = split_lo_bf16(s[0][2], s[0][3], pa[1]);
+            palo[2] = split_lo_bf16(s[1][0], s[1][1], pa[2]);
+            palo[3] = split_lo_bf16(s[1][2], s[1][3], pa[3]);
+        }
         if constexpr (kQ8) {
             // this thread's B fragments: keys 2c,2c+1 (b0) and 2c+8,2c+9 (b1) of the
             // warp's 16, head dims (D/8)*g .. +D/8 (one contiguous byte run per key)
@@ -513,7 +633,9 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                 const int      key   = 16 * warp + 2 * c + (r & 1) + 8 * (r >> 1);
                 const uint32_t rbase = smem_u32(sV) + key * Cfg::kRowBytes + (dim0 / 32) * 34;
                 lds_bytes_unaligned<D / 32>(rbase + 2 + (dim0 % 32), qv[r]);
-                dv[r] = __ushort_as_half(lds16(rbase));
+                // rows past n_kv in the last tile hold stale bytes: a zero scale
+                // keeps them finite (their P is 0, but 0 * inf would be NaN)
+                dv[r] = tile * kDecBN + key < o.n_kv ? __ushort_as_half(lds16(rbase)) : __float2half(0.0f);
             }
             const __half2 d01 = __halves2half2(dv[0], dv[1]);
             const __half2 d89 = __halves2half2(dv[2], dv[3]);
@@ -539,6 +661,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                 ldsm_x4_t(addr, b0, b1, b2, b3);
                 mma_16816<kBF16>(oacc[2 * dn], pa, b0, b1);
                 mma_16816<kBF16>(oacc[2 * dn + 1], pa, b2, b3);
+                if constexpr (kBF16) {
+                    mma_16816<true>(oacc[2 * dn], palo, b0, b1);
+                    mma_16816<true>(oacc[2 * dn + 1], palo, b2, b3);
+                }
             }
         }
     };
@@ -627,6 +753,12 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         named_bar_sync(1, kDecWarps * 32);
     };
 
+    // The first unit is known from the tile range: fetch its Q while the
+    // producer scans the mask and issues the first copies.
+    if (t0 < t1) {
+        cur_unit = (int) (t0 / tpu);
+        setup_unit(cur_unit);
+    }
     while (true) {
         if (!mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err, DEVERR_TIMEOUT_FULL, P.wait_limit_ns)) {
             break;
@@ -641,7 +773,15 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         }
         if (md.z == kMetaData) {
             const uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
-            process_tile(sK, sK + Cfg::kTileBytes, md.y);
+            const uint8_t *sV = sK + Cfg::kTileBytes;
+            if constexpr (kQ8) {
+                sK += md.w & 0xff;
+                sV += (md.w >> 8) & 0xff;
+            }
+            process_tile(sK, sV,
+                         reinterpret_cast<const uint16_t *>(smem + Cfg::kOffStages + stage * Cfg::kStageBytes +
+                                                            2 * Cfg::kTileBytes),
+                         md.y);
         }
         __syncwarp();
         if (lane == 0) {
@@ -659,9 +799,14 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
 }
 
 // ---------------------------------------------------------------------------
-// Combine: merge the partials of every unit split across CTAs.
+// Combine: merge the partials of every unit split across CTAs.  One CTA per
+// unit; 16 threads per row, each owning D/16 contiguous head dims, so all rows
+// and parts are read in parallel (the kernel is latency bound).
+constexpr int kCombThreads = kDecRows * 16;
+
 template <int D>
-__global__ void __launch_bounds__(D) fa_decode_combine(const __grid_constant__ DecodeParams P) {
+__global__ void __launch_bounds__(kCombThreads) fa_decode_combine(const __grid_constant__ DecodeParams P) {
+    constexpr int DPT = D / 16;  // dims per thread
     pdl_wait_primary();
     const OpDesc &o   = P.op;
     const int     u   = blockIdx.x;
@@ -673,39 +818,65 @@ __global__ void __launch_bounds__(D) fa_decode_combine(const __grid_constant__ D
     if (cf == cl) {
         return;
     }
-    const UnitCoord uc = unit_coord(P, u);
-    const int       d  = threadIdx.x;
-    for (int row = 0; row < uc.rows; ++row) {
-        float mx = -INFINITY;
-        for (int64_t cta = cf; cta <= cl; ++cta) {
-            mx = fmaxf(mx, P.partials[(cta + u) * dec_slot_floats(D) + row]);
+    const UnitCoord uc  = unit_coord(P, u);
+    const int       row = threadIdx.x / 16;
+    const int       d0  = (threadIdx.x % 16) * DPT;
+    // rows past uc.rows still run (the shuffles below need full warps); they
+    // read their slot's unused rows and write nothing
+    const bool    active = row < uc.rows;
+    const int64_t stride = dec_slot_floats(D);
+    const float  *base   = P.partials + (cf + u) * stride;
+    const int     np     = (int) (cl - cf + 1);
+    const int     sub    = threadIdx.x % 16;
+    float         mx     = -INFINITY;
+    for (int p = sub; p < np; p += 16) {  // the row's 16 threads split the parts
+        mx = fmaxf(mx, __ldg(base + p * stride + row));
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+    float l = 0.0f, acc[DPT];
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) {
+        acc[i] = 0.0f;
+    }
+#pragma unroll 4
+    for (int p = 0; p < np; ++p) {
+        const float *slot = base + p * stride;
+        const float  mc   = __ldg(slot + row);
+        const float  f    = mc == -INFINITY ? 0.0f : fast_exp2(mc - mx);
+        l += f * __ldg(slot + kDecRows + row);
+        const float4 *op4 = reinterpret_cast<const float4 *>(slot + 2 * kDecRows + row * D + d0);
+#pragma unroll
+        for (int i = 0; i < DPT / 4; ++i) {
+            const float4 v = __ldg(op4 + i);
+            acc[4 * i + 0] += f * v.x;
+            acc[4 * i + 1] += f * v.y;
+            acc[4 * i + 2] += f * v.z;
+            acc[4 * i + 3] += f * v.w;
         }
-        float l = 0.0f, acc = 0.0f;
-        for (int64_t cta = cf; cta <= cl; ++cta) {
-            const float *slot = P.partials + (cta + u) * dec_slot_floats(D);
-            const float  mc   = slot[row];
-            if (mc == -INFINITY) {
-                continue;
-            }
-            const float f = fast_exp2(mc - mx);
-            l += f * slot[kDecRows + row];
-            acc += f * slot[2 * kDecRows + row * D + d];
+    }
+    if (!active) {
+        return;
+    }
+    int iq, hq;
+    row_coord(P, uc, row, iq, hq);
+    float fs = 1.0f;
+    if (o.sinks) {
+        const float ts = o.sinks[hq] * kLog2e;
+        if (ts > mx) {
+            fs = fast_exp2(mx - ts);
+            l  = l * fs + 1.0f;
+        } else {
+            l += fast_exp2(ts - mx);
         }
-        int iq, hq;
-        row_coord(P, uc, row, iq, hq);
-        if (o.sinks) {
-            const float ts = o.sinks[hq] * kLog2e;
-            if (ts > mx) {
-                const float f = fast_exp2(mx - ts);
-                acc *= f;
-                l = l * f + 1.0f;
-            } else {
-                l += fast_exp2(ts - mx);
-            }
-        }
-        const float out = l == 0.0f ? 0.0f : acc / l;
-        *reinterpret_cast<float *>(o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
-                                   (int64_t) uc.b * o.d_nb3) = out;
+    }
+    const float inv = l == 0.0f ? 0.0f : fs / l;
+    char       *out = o.dst + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 + (int64_t) uc.b * o.d_nb3;
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) {
+        *reinterpret_cast<float *>(out + (int64_t) (d0 + i) * o.d_nb0) = acc[i] * inv;
     }
 }
 
@@ -747,7 +918,7 @@ cudaError_t launch_impl(const DecodeLaunch &L, cudaStream_t s, int *launches) {
     if (decode_needs_combine(L.p)) {
         cudaLaunchConfig_t c2 = cfg;
         c2.gridDim            = dim3((unsigned) L.p.units);
-        c2.blockDim           = dim3(D);
+        c2.blockDim           = dim3(kCombThreads);
         c2.dynamicSmemBytes   = 0;
         e                     = cudaLaunchKernelEx(&c2, fa_decode_combine<D>, L.p);
         if (e != cudaSuccess) {

@@ -24,7 +24,7 @@ struct OpDesc {
     // mask [>=n_kv, >=n_q, m_ne2, m_ne3] f16 (nullptr = none)
     const char *mask;
     int64_t     m_nb1, m_nb2, m_nb3;
-    int         m_ne2, m_ne3;
+    int         m_ne0, m_ne2, m_ne3;
     // sinks [Hq] f32 (nullptr = none)
     const float *sinks;
     // dst [D, Hq, n_q, B] f32
@@ -61,6 +61,7 @@ constexpr int kDecBN      = 64;  // keys per pipeline stage
 constexpr int kDecWarps   = 4;   // consumer warps (16 keys each per stage)
 constexpr int kDecStages  = 3;   // pipeline depth
 constexpr int kDecRows    = 16;  // rows per unit (one m16 MMA tile)
+constexpr int kDecMaxParts = 15; // cap on CTAs sharing one unit (bounds the combine)
 
 struct DecodeParams {
     OpDesc  op;

@@ -133,7 +133,7 @@ def cpu_baseline(budget_s=12.0, threads=None):
         oracle.flash_attn_ext(q, k, v, m, scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=threads)
         n += 1
         dt = time.perf_counter() - t0
-        if dt >= budget_s or n >= 200:
+        if dt >= budget_s or n >= 5000:
             break
     gbs = n * algo_bytes_per_op() / dt / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -183,10 +183,13 @@ def run_reference(args):
 
 
 def config_dict(args, note=None):
-    c = {"workload": "qwen3-4b decode attention stack (BASELINE config 2): 36 layers x ggml_flash_attn_ext, "
-                     "8 requests x CFG = 16 KV sets, Hq 32 / Hkv 8, D 128, KV 8192, F16 KV, mask [8192,1,1,16]",
-         "layers": LAYERS, "kv_sets_per_gpu": SETS, "kv_len": KV_LEN, "head_dim": D, "q_heads": HQ,
-         "kv_heads": HKV, "kv_type": "f16", "l2": "inputs larger than L2 (537 MB of KV per op); no flush",
+    layers = getattr(args, "layers", LAYERS)
+    kv = getattr(args, "kv", "f16")
+    c = {"workload": f"qwen3-4b decode attention stack (BASELINE config 2): {layers} layers x ggml_flash_attn_ext, "
+                     f"8 requests x CFG = 16 KV sets, Hq 32 / Hkv 8, D 128, KV 8192, {kv.upper()} KV, "
+                     "mask [8192,1,1,16]",
+         "layers": layers, "kv_sets_per_gpu": SETS, "kv_len": KV_LEN, "head_dim": D, "q_heads": HQ,
+         "kv_heads": HKV, "kv_type": kv, "l2": "inputs larger than L2 (537 MB of KV per op); no flush",
          "parallelism": f"requests sharded one batch per GPU x{args.gpus}, no collective"}
     if note:
         c["note"] = note
@@ -232,8 +235,9 @@ def time_graph(ops, steps, warmup, stream):
     with torch.cuda.graph(graph, stream=stream):
         for op in ops:
             op(stream=stream)
-    for _ in range(warmup):
-        graph.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
     torch.cuda.synchronize()
     return graph
 
@@ -255,9 +259,10 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
     stream = torch.cuda.Stream(device=device)
-    per_op = algo_bytes_per_op()
+    row_bytes = D // 32 * 34 if args.kv == "q8_0" else 2 * D
+    per_op = algo_bytes_per_op(kv_bytes_per_row=row_bytes)
     with torch.cuda.stream(stream):
-        ops, mask = build_stack(device, seed=SEED + 7919 * rank)
+        ops, mask = build_stack(device, kv=args.kv, layers=args.layers, seed=SEED + 7919 * rank)
         launches_per_op = 0
         ops[0](stream=stream)
         launches_per_op = acefa.last_launch_count()
@@ -268,10 +273,10 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk, torch.cuda.stream(stream):
         start.record(stream)
         for _ in range(args.steps):
-            graph.replay()
+            graph.replay()  # replays on the current stream
         end.record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -282,7 +287,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_step = ms_max / args.steps
-    step_bytes = per_op * LAYERS
+    step_bytes = per_op * args.layers
     value = world * step_bytes * args.steps / (ms_max / 1e3) / 1e9
     assert acefa.device_error(stream) == 0
 
@@ -326,22 +331,22 @@ def run_ours(args):
     out = None
     if rank == 0:
         peak, peak_kind = read_peaks()
-        per_launch_s = (ms_step / 1e3) / LAYERS
+        per_launch_s = (ms_step / 1e3) / args.layers
         achieved = per_op / per_launch_s / 1e9
         out = {
             "metric": "decode_attention_hbm_gbs", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.kv,
             "data": "synthetic N(0,1) K/V/Q, seeded (2042 + 7919*rank); random values, zero mask",
             "config": config_dict(args),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": read_traffic("fa_decode_kernel_f16_d128"),
-                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "fa_decode_kernel<F16,128> (+combine)",
+                         "frac": round(achieved / peak, 4), "traffic": read_traffic(f"fa_decode_kernel_{args.kv}_d128"),
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": f"fa_decode_kernel<{args.kv},128> (+combine)",
                          "algo_bytes_per_launch": per_op},
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h),
                     "how": "pinned H2D of mask + 36 Q, 36 C-ABI calls, D2H of 36 outputs, CUDA events"},
-            "gpu_launches": int(launches_per_op * LAYERS * args.steps),
+            "gpu_launches": int(launches_per_op * args.layers * args.steps),
             "clocks": clk.summary(),
         }
     # free the F16 stack before optional extras
@@ -415,6 +420,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (36 = the headline stack)")
+    ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
