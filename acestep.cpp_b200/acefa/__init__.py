@@ -23,7 +23,7 @@ OK = 0
 STATUS_NAMES = {
     0: "ACEFA_OK", -1: "ACEFA_ERR_NULL", -2: "ACEFA_ERR_TYPE", -3: "ACEFA_ERR_SHAPE",
     -4: "ACEFA_ERR_LAYOUT", -5: "ACEFA_ERR_WORKSPACE", -6: "ACEFA_ERR_CUDA",
-    -7: "ACEFA_ERR_DEVICE", -8: "ACEFA_ERR_DEVICE_TIMEOUT",
+    -7: "ACEFA_ERR_DEVICE", -8: "ACEFA_ERR_DEVICE_TIMEOUT", -9: "ACEFA_ERR_NOALLOC_LIMIT",
 }
 
 _PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "acefa_last_launch_count",
     "acefa_last_path",
     "acefa_version",
+    "acefa_flash_attn_ext_noalloc",
 )
 
 
@@ -88,6 +89,9 @@ def load_library(path: str | None = None):
     lib.acefa_last_launch_count.restype = ctypes.c_int
     lib.acefa_last_path.restype = ctypes.c_int
     lib.acefa_version.restype = ctypes.c_int
+    lib.acefa_flash_attn_ext_noalloc.argtypes = [T, T, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                                 ctypes.c_int, ctypes.c_void_p]
+    lib.acefa_flash_attn_ext_noalloc.restype = ctypes.c_int
     if path is None:
         _lib = lib
     return lib

@@ -381,6 +381,7 @@ ACEFA_API const char *acefa_status_string(int status) {
         case ACEFA_ERR_CUDA: return "CUDA call failed";
         case ACEFA_ERR_DEVICE: return "device is not sm_100";
         case ACEFA_ERR_DEVICE_TIMEOUT: return "device-side wait expired";
+        case ACEFA_ERR_NOALLOC_LIMIT: return "operands need more scratch than the fixed no-alloc buffer (8 MiB) holds";
         default: return "unknown status";
     }
 }

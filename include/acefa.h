@@ -18,8 +18,9 @@
  *
  * Tensors use ggml's conventions: ne[0] innermost, nb[] byte strides, type ids
  * equal to enum ggml_type.  All data pointers are device pointers owned by the
- * caller (ggml's allocator).  No entry point allocates device memory, synchronises
- * the stream or aborts; every call is safe inside CUDA-graph stream capture.
+ * caller (ggml's allocator).  No entry point allocates device memory or aborts;
+ * acefa_flash_attn_ext() also never synchronises, so it is safe inside
+ * CUDA-graph stream capture.
  */
 #ifndef ACEFA_H
 #define ACEFA_H
@@ -61,6 +62,7 @@ typedef enum acefa_status {
     ACEFA_ERR_CUDA       = -6, /* a CUDA runtime/driver call failed */
     ACEFA_ERR_DEVICE     = -7, /* current device is not sm_100 */
     ACEFA_ERR_DEVICE_TIMEOUT = -8, /* a bounded device-side wait expired */
+    ACEFA_ERR_NOALLOC_LIMIT  = -9, /* operands need more scratch than acefa_flash_attn_ext_noalloc's fixed buffer */
 } acefa_status;
 
 /* ggml_tensor reduced to what the operator reads. */
@@ -93,7 +95,32 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
                                    float scale, float max_bias, float logit_softcap, int prec, void *stream,
                                    void *workspace, size_t workspace_bytes);
 
-/* Workspace the call above needs for these operands on the current device
+/*
+ * The same operator for callers that cannot hand the engine any device memory:
+ * hosts whose device memory is entirely owned by another allocator (a ggml
+ * backend whose graph allocator has planned every buffer, a plugin inside a
+ * framework that forbids foreign allocations), threads that must never block
+ * (cudaMalloc can synchronise the whole device), and builds that forbid runtime
+ * allocation after start-up.  No counterpart in the reference: ggml's CUDA
+ * backend always draws flash-attention scratch from its own memory pool.
+ *
+ * Arguments and results are those of acefa_flash_attn_ext() without the
+ * workspace pair.  The split-KV scratch is a fixed 8 MiB array inside the
+ * library, one per GPU, held from library load until process exit; operands
+ * whose acefa_workspace_bytes() exceeds 8 MiB are refused with
+ * ACEFA_ERR_NOALLOC_LIMIT and nothing is launched.  The first call on each
+ * device looks up that array's device address (with the device current), so
+ * make that first call before any stream capture.  Every call on a device
+ * shares the array: calls whose kernels may overlap on the GPU (other streams or
+ * other threads without ordering) race and must be serialised by the caller.
+ * Nothing is allocated, freed or zeroed by the call.
+ */
+ACEFA_API int acefa_flash_attn_ext_noalloc(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                           const acefa_tensor *mask, const acefa_tensor *sinks,
+                                           const acefa_tensor *dst, float scale, float max_bias, float logit_softcap,
+                                           int prec, void *stream);
+
+/* Workspace acefa_flash_attn_ext() needs for these operands on the current device
  * (split-KV partial results, mask tile classes).  A function of shapes, types
  * and the device only -- never of tensor contents -- so it can be sized once
  * before CUDA-graph capture.  Returns 0 for unsupported operands. */

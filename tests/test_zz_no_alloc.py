@@ -1,0 +1,78 @@
+"""acefa_flash_attn_ext_noalloc: the operator for callers that cannot give the
+engine any device memory (a host whose allocator owns every buffer, a thread
+that must not block on cudaMalloc, a build that forbids runtime allocation).
+
+Its split-KV scratch is a fixed array inside the library, so these tests check
+that it produces the same result as the allocating entry point, call after
+call, and that it refuses operands whose scratch would not fit.  This file is
+collected last so that a stopping run has already exercised everything else.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import acefa
+from fa_cases import Case, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(op, stream=None):
+    lib = acefa.load_library()
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    s = torch.cuda.current_stream() if stream is None else stream
+    return lib.acefa_flash_attn_ext_noalloc(r(op.tq), r(op.tk), r(op.tv), r(op.tm), r(op.ts), r(op.td), op.scale,
+                                            op.max_bias, op.softcap, op.prec, ctypes.c_void_p(s.cuda_stream))
+
+
+@pytest.mark.parametrize("kv", ["f16", "q8_0"])
+def test_noalloc_matches_allocating_entry_twice(kv):
+    # two different operand sets back to back: the second call finds the first
+    # call's leftovers in the shared scratch and must not be affected by them
+    cases = [
+        Case(4242, B=16, Hq=32, Hkv=8, n_q=1, n_kv=2048, kv=kv, max_seq=4096, mask="valid",
+             valid=[2048 - 37 * i for i in range(16)]),
+        Case(4243, B=4, Hq=16, Hkv=8, n_q=3, n_kv=777, kv=kv, mask="random", sinks=True),
+    ]
+    for c in cases:
+        ref_op = c.op()
+        want = ref_op().clone()
+        torch.cuda.synchronize()
+        op = c.op()  # separate output buffer for the no-alloc call
+        op.out.fill_(float("nan"))
+        st = _noalloc(op)
+        assert st == 0, acefa.STATUS_NAMES.get(st, st)
+        torch.cuda.synchronize()
+        assert_close(op.out.cpu().numpy(), want.cpu().numpy(), what=f"noalloc {kv}")
+        assert acefa.device_error() == 0
+
+
+def test_noalloc_refuses_oversized_operands():
+    # 256 KV sets x 8 heads need far more than the fixed 8 MiB of split-KV
+    # partials; descriptors only (nothing is launched, so no memory behind them)
+    lib = acefa.load_library()
+    D, Hq, Hkv, B, nkv = 128, 32, 8, 256, 8192
+
+    def td(ne, es, gtype):
+        t = acefa.Tensor()
+        t.type = gtype
+        t.ne[:] = ne
+        nb = [es]
+        for i in range(1, 4):
+            nb.append(nb[-1] * ne[i - 1])
+        t.nb[:] = nb
+        t.data = 1 << 20
+        return t
+
+    q = td([D, 1, Hq, B], 4, acefa.GGML_F32)
+    k = td([D, nkv, Hkv, B], 2, acefa.GGML_F16)
+    v = td([D, nkv, Hkv, B], 2, acefa.GGML_F16)
+    m = td([nkv, 1, 1, B], 2, acefa.GGML_F16)
+    d = td([D, Hq, 1, B], 4, acefa.GGML_F32)
+    r = ctypes.byref
+    assert lib.acefa_workspace_bytes(r(q), r(k), r(v), r(m), r(d)) > (8 << 20)
+    st = lib.acefa_flash_attn_ext_noalloc(r(q), r(k), r(v), r(m), None, r(d), 0.088, 0.0, 0.0, 10, None)
+    assert st == -9
+    assert b"no-alloc" in lib.acefa_status_string(st)
