@@ -251,7 +251,40 @@ DecodePlan plan_decode(const OpDesc &o, int sm_count) {
     return p;
 }
 
-int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D) {
+// ------------------------------------------------------------------ dense plan
+// The dense tcgen05 kernel serves F16 K/V with D = 128 when a K/V head has
+// more than 64 rows of queries (G * n_q) -- prefill, encoders, DiT.  A function
+// of shapes only, so the choice (and the workspace) is fixed before capture.
+bool use_dense(const OpDesc &o) {
+    const int64_t rows = (int64_t) o.G * o.n_q;
+    const int64_t n_kt = ((int64_t) o.n_kv + kDenseBN - 1) / kDenseBN;
+    return o.kv_type == ACEFA_TYPE_F16 && o.D == 128 && rows > 64 && n_kt <= kDenseMaxKT && o.B <= 65535 &&
+           o.Hkv <= 65535;
+}
+
+struct DensePlan {
+    int    rows_total, n_rt, n_pairs, n_kt;
+    bool   classify;
+    size_t ws_bytes;
+};
+
+DensePlan plan_dense(const OpDesc &o) {
+    DensePlan p;
+    p.rows_total = o.G * o.n_q;
+    p.n_rt       = (p.rows_total + kDenseBM - 1) / kDenseBM;
+    p.n_pairs    = (p.n_rt + 1) / 2;
+    p.n_kt       = (o.n_kv + kDenseBN - 1) / kDenseBN;
+    // per-tile classes need one mask row per query: a mask shared by all heads
+    p.classify = o.mask != nullptr && o.m_ne2 == 1;
+    size_t b   = p.classify ? (size_t) o.m_ne3 * p.n_rt * p.n_kt : 0;
+    p.ws_bytes = (b + 255) / 256 * 256;
+    if (p.ws_bytes == 0) {
+        p.ws_bytes = 256;
+    }
+    return p;
+}
+
+int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D, int box_rows) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) {
         return ACEFA_ERR_CUDA;
@@ -261,7 +294,7 @@ int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D) {
     cuuint64_t s2         = t->ne[2] > 1 ? t->nb[2] : s1 * (cuuint64_t) t->ne[1];
     cuuint64_t s3         = t->ne[3] > 1 ? t->nb[3] : s2 * (cuuint64_t) t->ne[2];
     cuuint64_t strides[3] = {s1, s2, s3};
-    cuuint32_t box[4]     = {64, (cuuint32_t) kDecBN, 1, 1};
+    cuuint32_t box[4]     = {64, (cuuint32_t) box_rows, 1, 1};
     cuuint32_t estr[4]    = {1, 1, 1, 1};
     CUresult   rc = enc(map, t->type == ACEFA_TYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                         4, t->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -296,6 +329,9 @@ ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor
     if (dev_info(&di) != ACEFA_OK) {
         return 0;
     }
+    if (use_dense(c.op)) {
+        return plan_dense(c.op).ws_bytes;
+    }
     return plan_decode(c.op, di->sm_count).ws_bytes;
 }
 
@@ -319,6 +355,36 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
     set_scalars(c.op, scale, max_bias, logit_softcap);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
+    if (use_dense(c.op)) {
+        const DensePlan dp = plan_dense(c.op);
+        if (workspace_bytes < dp.ws_bytes || !workspace || !aligned(workspace, 256)) {
+            return ACEFA_ERR_WORKSPACE;
+        }
+        DenseLaunch L;
+        std::memset(&L, 0, sizeof(L));
+        L.p.op            = c.op;
+        L.p.rows_total    = dp.rows_total;
+        L.p.n_rt          = dp.n_rt;
+        L.p.n_pairs       = dp.n_pairs;
+        L.p.n_kt          = dp.n_kt;
+        L.p.cls           = dp.classify ? static_cast<const uint8_t *>(workspace) : nullptr;
+        L.p.cls_out       = dp.classify ? static_cast<uint8_t *>(workspace) : nullptr;
+        L.p.dev_err       = di->err_ptr;
+        L.p.wait_limit_ns = wait_limit_ns();
+        L.classify        = dp.classify;
+        if ((rc = encode_kv_map(&L.kmap, k, c.op.D, kDenseBN)) != ACEFA_OK ||
+            (rc = encode_kv_map(&L.vmap, v, c.op.D, kDenseBN)) != ACEFA_OK) {
+            return rc;
+        }
+        int launches = 0;
+        if (launch_dense(L, s, &launches) != cudaSuccess) {
+            return ACEFA_ERR_CUDA;
+        }
+        t_last_launches = launches;
+        t_last_path     = 2;
+        return ACEFA_OK;
+    }
+
     DecodePlan plan = plan_decode(c.op, di->sm_count);
     if (workspace_bytes < plan.ws_bytes || (plan.ws_bytes && (!workspace || !aligned(workspace, 256)))) {
         return ACEFA_ERR_WORKSPACE;
@@ -335,7 +401,8 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
     L.p.dev_err        = di->err_ptr;
     L.p.wait_limit_ns  = wait_limit_ns();
     if (c.op.kv_type != ACEFA_TYPE_Q8_0) {
-        if ((rc = encode_kv_map(&L.kmap, k, c.op.D)) != ACEFA_OK || (rc = encode_kv_map(&L.vmap, v, c.op.D)) != ACEFA_OK) {
+        if ((rc = encode_kv_map(&L.kmap, k, c.op.D, kDecBN)) != ACEFA_OK ||
+            (rc = encode_kv_map(&L.vmap, v, c.op.D, kDecBN)) != ACEFA_OK) {
             return rc;
         }
     }

@@ -1,0 +1,591 @@
+// fa_dense.cu -- tcgen05/TMEM flash attention for query-heavy ggml_flash_attn_ext
+// nodes: LM causal prefill (src/qwen3-lm.h:465-469, n_tokens > 1), the Qwen3
+// encoders (src/qwen3-enc.h:195-199) and DiT self/cross attention
+// (src/dit-graph.h:227-231, :348-352).
+//
+// One CTA owns two 128-row tiles of a (batch, kv head) unit -- the rows are
+// the unit's (query, q head) pairs, so GQA heads that share K/V share the
+// stream -- and walks the unit's 128-key tiles:
+//   warp 0      TMA producer: K_j and V_j into a 4 x 32 KB shared ring (128-B
+//               swizzle, two 64-dim boxes per tile), skipping key tiles that
+//               no row of either tile can see.
+//   warp 1      owns 512 TMEM columns (O0 | O1 | S0 | S1) and issues the MMAs
+//               from one thread: S_i = Q_i K_j^T (SS form, K-major operands)
+//               and O_i += P_i V_j (TS form: P read from TMEM, V MN-major).
+//   warps 4-7   softmax for row tile 0, warps 8-11 for row tile 1: one thread
+//               per row reads S with tcgen05.ld, applies scale / softcap /
+//               mask / ALiBi in log2 units, keeps a running max that only
+//               moves (and rescales O in TMEM) when it grows by more than 2^8,
+//               and writes P as f16 over the S columns it just read.
+// The two row tiles ping-pong: while one warpgroup exponentiates, the tensor
+// core runs the other tile's PV and next S.  A pre-pass classifies each
+// (row tile, key tile) of the mask as dead / all-zero / mixed so that causal
+// and window masks never load or multiply their dead tiles.
+// Every wait is bounded (error word + drain on expiry).
+#include "fa_internal.h"
+#include "ptx.cuh"
+
+namespace acefa {
+namespace {
+
+constexpr int      kThreads    = 384;
+constexpr int      kRing       = 4;
+constexpr int      kTileBytes  = kDenseBN * 128 * 2;  // 32 KB: 128 keys x 128 dims f16
+constexpr int      kQBytes     = kDenseBM * 128 * 2;  // 32 KB
+constexpr int      kOffQ       = 0;
+constexpr int      kOffRing    = kOffQ + 2 * kQBytes;
+constexpr int      kOffBars    = kOffRing + kRing * kTileBytes;
+constexpr int      kNumBars    = 2 * kRing + 2 * 3 + 1;
+constexpr int      kOffCls     = kOffBars + kNumBars * 8;
+constexpr int      kOffMisc    = kOffCls + 2 * kDenseMaxKT;
+constexpr int      kSmemBytes  = kOffMisc + 16 + 1024;
+constexpr uint32_t kTmemCols   = 512;
+constexpr float    kRescaleLog2 = 8.0f;  // O is rescaled only when the max grows by > 2^8
+
+constexpr uint16_t kHalfNegInf = 0xFC00u;
+
+__device__ __forceinline__ void row_to_query(int gr, int G, int hk, int &iq, int &hq) {
+    iq = gr / G;
+    hq = hk * G + gr % G;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Mask classification: one CTA per (key tile, row tile, mask batch).
+__global__ void __launch_bounds__(256) fa_mask_classify(const __grid_constant__ DenseParams P) {
+    const OpDesc &o   = P.op;
+    const int     kt  = blockIdx.x;
+    const int     t   = blockIdx.y;
+    const int     bm  = blockIdx.z;
+    const int     G   = o.G;
+    const int     gr0 = t * kDenseBM;
+    const int     gr1 = min(P.rows_total, gr0 + kDenseBM) - 1;
+    const int     iq0 = gr0 / G, iq1 = gr1 / G;
+    const int     j0 = kt * kDenseBN, j1 = min(o.n_kv, j0 + kDenseBN);
+    const int     nj = j1 - j0;
+    int           live = 0, nonzero = 0;
+    pdl_wait_primary();
+    const char *mbase = o.mask + (int64_t) bm * o.m_nb3;
+    for (int idx = threadIdx.x; idx < (iq1 - iq0 + 1) * nj; idx += blockDim.x) {
+        const int       iq = iq0 + idx / nj;
+        const int       j  = j0 + idx % nj;
+        const uint16_t  h  = __ldg(reinterpret_cast<const uint16_t *>(mbase + (int64_t) iq * o.m_nb1) + j);
+        live |= h != kHalfNegInf;
+        nonzero |= (h & 0x7FFFu) != 0;
+    }
+    live    = __syncthreads_or(live);
+    nonzero = __syncthreads_or(nonzero);
+    if (threadIdx.x == 0) {
+        P.cls_out[((int64_t) bm * P.n_rt + t) * P.n_kt + kt] =
+            (uint8_t) ((live ? kClsLive : 0) | (live && nonzero ? kClsMask : 0));
+    }
+    pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
+                    const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    uint64_t     *bars    = reinterpret_cast<uint64_t *>(smem + kOffBars);
+    uint64_t     *full    = bars;
+    uint64_t     *empty   = bars + kRing;
+    uint64_t     *s_ready = bars + 2 * kRing;
+    uint64_t     *p_ready = s_ready + 2;
+    uint64_t     *o_done  = p_ready + 2;
+    uint64_t     *fin     = o_done + 2;
+    uint8_t      *s_cls   = smem + kOffCls;  // [2][kDenseMaxKT]
+    uint32_t     *s_tmem  = reinterpret_cast<uint32_t *>(smem + kOffMisc);
+    volatile int *abort_f = reinterpret_cast<volatile int *>(smem + kOffMisc + 4);
+
+    const OpDesc &o    = P.op;
+    const int     warp = threadIdx.x >> 5;
+    const int     lane = threadIdx.x & 31;
+    const int     pair = P.n_pairs - 1 - (int) blockIdx.x;  // heavy (late, causal) tiles first
+    const int     hk   = blockIdx.y;
+    const int     b    = blockIdx.z;
+    const int     bk   = b / o.rk3;
+    const int     t0   = 2 * pair;
+    const bool    has_tile[2] = {t0 < P.n_rt, t0 + 1 < P.n_rt};
+
+    if (warp == 1) {
+        tmem_alloc(s_tmem, kTmemCols);
+        tmem_relinquish();
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRing; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_ready[i], 1);
+            mbar_init(&p_ready[i], 128);
+            mbar_init(&o_done[i], 1);
+        }
+        mbar_init(fin, 1);
+        *abort_f = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&kmap);
+        prefetch_tensormap(&vmap);
+    }
+    pdl_wait_primary();
+
+    // ---- key-tile classes of both row tiles
+    for (int j = threadIdx.x; j < P.n_kt; j += kThreads) {
+        for (int i = 0; i < 2; ++i) {
+            uint8_t c = 0;
+            if (has_tile[i]) {
+                if (P.cls) {
+                    c = P.cls[((int64_t) (b % o.m_ne3) * P.n_rt + t0 + i) * P.n_kt + j];
+                } else {
+                    c = kClsLive | (o.mask ? kClsMask : 0);
+                }
+                if ((c & kClsLive) && j == P.n_kt - 1 && (o.n_kv % kDenseBN) != 0) {
+                    c |= kClsBounds;
+                }
+            }
+            s_cls[i * kDenseMaxKT + j] = c;
+        }
+    }
+
+    // ---- Q: f32 rows -> f16, 128-B swizzled K-major tiles [128 rows][2 x 64 dims]
+    for (int rr = warp; rr < 2 * kDenseBM; rr += kThreads / 32) {
+        const int i  = rr / kDenseBM;
+        const int r  = rr % kDenseBM;
+        const int gr = (t0 + i) * kDenseBM + r;
+        float4    v  = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_tile[i] && gr < P.rows_total) {
+            int iq, hq;
+            row_to_query(gr, o.G, hk, iq, hq);
+            const char *qrow = o.q + (int64_t) iq * o.q_nb1 + (int64_t) hq * o.q_nb2 + (int64_t) b * o.q_nb3;
+            const float *qf  = reinterpret_cast<const float *>(qrow) + 4 * lane;
+            if ((reinterpret_cast<uintptr_t>(qf) & 15u) == 0) {
+                v = __ldg(reinterpret_cast<const float4 *>(qf));
+            } else {
+                v = make_float4(__ldg(qf), __ldg(qf + 1), __ldg(qf + 2), __ldg(qf + 3));
+            }
+        }
+        const uint32_t lo = pack2<false>(v.x, v.y), hi = pack2<false>(v.z, v.w);
+        const int      d  = 4 * lane;
+        uint8_t *dst = smem + kOffQ + i * kQBytes + (d >> 6) * (kDenseBM * 128) + r * 128 +
+                       ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+    }
+    fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+
+    auto live_of = [&](int i, int j) -> bool { return (s_cls[i * kDenseMaxKT + j] & kClsLive) != 0; };
+    auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };
+
+    if (warp == 0) {
+        // ============================ TMA producer ============================
+        if (lane == 0) {
+            int pend[kRing];
+            for (int i = 0; i < kRing; ++i) {
+                pend[i] = -1;
+            }
+            int  use = 0;
+            bool ok  = true;
+            for (int j = 0; j < P.n_kt && ok; ++j) {
+                if (!any_live(j)) {
+                    continue;
+                }
+                for (int h = 0; h < 2 && ok; ++h) {
+                    const int seq = 2 * use + h;
+                    const int buf = seq % kRing;
+                    const int u   = seq / kRing;
+                    ok = mbar_wait_bounded(&empty[buf], (uint32_t) ((u & 1) ^ 1), abort_f, P.dev_err,
+                                           DEVERR_TIMEOUT_EMPTY, P.wait_limit_ns);
+                    if (!ok) {
+                        break;
+                    }
+                    uint8_t           *dst = smem + kOffRing + buf * kTileBytes;
+                    const CUtensorMap *map = h == 0 ? &kmap : &vmap;
+                    mbar_arrive_expect_tx(&full[buf], kTileBytes);
+                    tma_load_4d(dst, map, 0, j * kDenseBN, hk, bk, &full[buf]);
+                    tma_load_4d(dst + kDenseBN * 128, map, 64, j * kDenseBN, hk, bk, &full[buf]);
+                    pend[buf] = u & 1;
+                }
+                ++use;
+            }
+            if (!ok) {
+                for (int i = 0; i < kRing; ++i) {
+                    if (pend[i] < 0) {
+                        continue;
+                    }
+                    const uint64_t ts = globaltimer_ns();
+                    while (!mbar_try_wait(&full[i], (uint32_t) pend[i])) {
+                        if (globaltimer_ns() - ts > P.wait_limit_ns) {
+                            atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_DRAIN);
+                            break;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ============================ MMA issuer ==============================
+        if (lane == 0) {
+            constexpr uint32_t idS = umma_idesc_f16(128, 128, false, false, false);
+            constexpr uint32_t idO = umma_idesc_f16(128, 128, false, true, false);
+            const uint32_t     q_s[2] = {smem_u32(smem + kOffQ), smem_u32(smem + kOffQ + kQBytes)};
+            const uint32_t     ring   = smem_u32(smem + kOffRing);
+            const uint32_t     tO[2]  = {tmem + 0, tmem + 128};
+            const uint32_t     tS[2]  = {tmem + 256, tmem + 384};
+            uint32_t           p_ph[2] = {0, 0};
+            uint32_t           has_o[2] = {0, 0};
+            bool               ok = true;
+
+            auto wait_full = [&](int seq) -> bool {
+                return mbar_wait_bounded(&full[seq % kRing], (uint32_t) ((seq / kRing) & 1), abort_f, P.dev_err,
+                                         DEVERR_TIMEOUT_FULL, P.wait_limit_ns);
+            };
+            auto issue_s = [&](int i, int kbuf) {
+                const uint32_t kb = ring + kbuf * kTileBytes;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t off = (ks >> 2) * (kDenseBM * 128) + (ks & 3) * 32;
+                    umma_ss(tS[i], umma_desc_sw128(q_s[i] + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024), idS,
+                            ks > 0 ? 1u : 0u);
+                }
+                tc_commit(&s_ready[i]);
+            };
+            auto issue_pv = [&](int i, int vbuf) {
+                const uint32_t vb = ring + vbuf * kTileBytes;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    umma_ts(tO[i], tS[i] + ks * 8, umma_desc_sw128(vb + ks * 2048, kDenseBN * 128, 1024), idO,
+                            (ks > 0 || has_o[i]) ? 1u : 0u);
+                }
+                has_o[i] = 1;
+                tc_commit(&o_done[i]);
+            };
+            auto next_live = [&](int j) {
+                while (j < P.n_kt && !any_live(j)) {
+                    ++j;
+                }
+                return j;
+            };
+
+            int use = 0;
+            int j   = next_live(0);
+            if (j < P.n_kt) {
+                ok = wait_full(2 * use);
+                if (ok) {
+                    tc_fence_after();
+                    for (int i = 0; i < 2; ++i) {
+                        if (live_of(i, j)) {
+                            issue_s(i, (2 * use) % kRing);
+                        }
+                    }
+                    tc_commit(&empty[(2 * use) % kRing]);
+                }
+            }
+            while (ok && j < P.n_kt) {
+                const int jn   = next_live(j + 1);
+                const int vseq = 2 * use + 1;
+                ok             = wait_full(vseq);
+                if (!ok) {
+                    break;
+                }
+                tc_fence_after();
+                const bool nxt = jn < P.n_kt;
+                const int  kseq = 2 * (use + 1);
+                bool       kready = false;
+                for (int i = 0; i < 2 && ok; ++i) {
+                    if (live_of(i, j)) {
+                        ok = mbar_wait_bounded(&p_ready[i], p_ph[i], abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
+                                               P.wait_limit_ns);
+                        if (!ok) {
+                            break;
+                        }
+                        p_ph[i] ^= 1u;
+                        tc_fence_after();
+                        issue_pv(i, vseq % kRing);
+                    }
+                    if (nxt && live_of(i, jn)) {
+                        if (!kready) {
+                            ok = wait_full(kseq);
+                            if (!ok) {
+                                break;
+                            }
+                            tc_fence_after();
+                            kready = true;
+                        }
+                        issue_s(i, kseq % kRing);
+                    }
+                }
+                if (!ok) {
+                    break;
+                }
+                tc_commit(&empty[vseq % kRing]);
+                if (nxt) {
+                    if (!kready) {  // neither tile needs jn's K here: never happens (jn is live)
+                        ok = wait_full(kseq);
+                    }
+                    tc_commit(&empty[kseq % kRing]);
+                }
+                ++use;
+                j = jn;
+            }
+            // every MMA issued by this thread completes before TMEM is released
+            tc_commit(fin);
+            const uint64_t ts = globaltimer_ns();
+            while (!mbar_try_wait(fin, 0)) {
+                if (globaltimer_ns() - ts > P.wait_limit_ns) {
+                    atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_MMA);
+                    break;
+                }
+            }
+        }
+    } else if (warp >= 4) {
+        // ============================ softmax =================================
+        const int      i     = (warp - 4) >> 2;  // row tile
+        const int      wq    = warp & 3;         // TMEM lane quarter
+        const int      r     = wq * 32 + lane;
+        const int      gr    = (t0 + i) * kDenseBM + r;
+        const bool     vrow  = has_tile[i] && gr < P.rows_total;
+        const uint32_t lanes = (uint32_t) (wq * 32) << 16;
+        const uint32_t tS    = tmem + lanes + 256 + 128 * i;
+        const uint32_t tO    = tmem + lanes + 128 * i;
+        int            iq = 0, hq = 0;
+        if (vrow) {
+            row_to_query(gr, o.G, hk, iq, hq);
+        }
+        const uint16_t *mrow = nullptr;
+        if (o.mask) {
+            mrow = reinterpret_cast<const uint16_t *>(o.mask + (int64_t) iq * o.m_nb1 +
+                                                      (int64_t) (hq % o.m_ne2) * o.m_nb2 +
+                                                      (int64_t) (b % o.m_ne3) * o.m_nb3);
+        }
+        const float slope = alibi_slope(o, hq);
+        float       m_run = -INFINITY;  // log2 units
+        float       l_run = 0.0f;
+        int         cnt   = 0;
+        bool        ok    = true;
+
+        for (int j = 0; j < P.n_kt && ok; ++j) {
+            const uint8_t c = s_cls[i * kDenseMaxKT + j];
+            if (!(c & kClsLive)) {
+                continue;
+            }
+            const int j0 = j * kDenseBN;
+            ok = mbar_wait_bounded(&s_ready[i], (uint32_t) (cnt & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
+                                   P.wait_limit_ns);
+            if (!ok) {
+                break;
+            }
+            tc_fence_after();
+            // ---- pass 1: logits in log2 units (written back), tile max
+            float tmax = -INFINITY;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t x[32];
+                tmem_ld32(tS + 32 * ch, x);
+                tmem_ld_wait32(x);
+                uint16_t mk[32];
+                if (c & kClsMask) {
+                    const uint16_t *mp = mrow + j0 + 32 * ch;
+                    if ((reinterpret_cast<uintptr_t>(mp) & 15u) == 0 && j0 + 32 * ch + 32 <= o.m_ne0) {
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            const uint4 w = __ldg(reinterpret_cast<const uint4 *>(mp) + q4);
+                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                mk[8 * q4 + 2 * e]     = (uint16_t) (ws[e] & 0xFFFFu);
+                                mk[8 * q4 + 2 * e + 1] = (uint16_t) (ws[e] >> 16);
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            mk[e] = j0 + 32 * ch + e < o.m_ne0 ? __ldg(mp + e) : kHalfNegInf;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    float v = __uint_as_float(x[e]) * o.scale_eff;
+                    if (o.softcap != 0.0f) {
+                        v = o.softcap * tanhf(v);
+                    }
+                    if (c & kClsMask) {
+                        const float mv = slope * __half2float(__ushort_as_half(mk[e]));
+                        v              = mv == -INFINITY ? -INFINITY : v + mv;
+                    }
+                    if ((c & kClsBounds) && j0 + 32 * ch + e >= o.n_kv) {
+                        v = -INFINITY;
+                    }
+                    v *= kLog2e;
+                    tmax = fmaxf(tmax, v);
+                    x[e] = __float_as_uint(v);
+                }
+                tmem_st32(tS + 32 * ch, x);
+            }
+            tmem_st_wait();
+            // ---- previous PV must be done before O is touched or P overwrites S
+            if (cnt > 0) {
+                ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
+                                       P.wait_limit_ns);
+                if (!ok) {
+                    break;
+                }
+                tc_fence_after();
+            }
+            const float m_new = fmaxf(m_run, tmax);
+            if (m_run == -INFINITY) {
+                m_run = m_new;  // nothing accumulated yet for this row
+            } else if (m_new > m_run + kRescaleLog2) {
+                const float f = fast_exp2(m_run - m_new);
+                l_run *= f;
+#pragma unroll 1
+                for (int ch = 0; ch < 4; ++ch) {
+                    uint32_t x[32];
+                    tmem_ld32(tO + 32 * ch, x);
+                    tmem_ld_wait32(x);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        x[e] = __float_as_uint(__uint_as_float(x[e]) * f);
+                    }
+                    tmem_st32(tO + 32 * ch, x);
+                }
+                m_run = m_new;
+            }
+            // ---- pass 2: P = exp2(x - m) as f16 pairs over the S columns
+            const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t x[32];
+                tmem_ld32(tS + 32 * ch, x);
+                tmem_ld_wait32(x);
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float p0 = fast_exp2(__uint_as_float(x[2 * e]) - m_use);
+                    const float p1 = fast_exp2(__uint_as_float(x[2 * e + 1]) - m_use);
+                    l_run += p0 + p1;
+                    pk[e] = pack2<false>(p0, p1);
+                }
+                tmem_st16(tS + 16 * ch, pk);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&p_ready[i]);
+            ++cnt;
+        }
+        // ---- epilogue: O / l
+        if (ok && cnt > 0) {
+            ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
+                                   P.wait_limit_ns);
+            tc_fence_after();
+        }
+        float fs = 1.0f;
+        if (o.sinks && vrow) {
+            const float ts = o.sinks[hq] * kLog2e;
+            if (ts > m_run) {
+                fs    = m_run == -INFINITY ? 0.0f : fast_exp2(m_run - ts);
+                l_run = l_run * fs + 1.0f;
+            } else {
+                l_run += fast_exp2(ts - m_run);
+            }
+        }
+        const float inv = l_run > 0.0f ? fs / l_run : 0.0f;
+        float      *orow = vrow ? reinterpret_cast<float *>(o.dst + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
+                                                            (int64_t) b * o.d_nb3)
+                                : nullptr;
+        const bool  al16 = (reinterpret_cast<uintptr_t>(orow) & 15u) == 0;
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+            uint32_t x[32];
+            if (ok && cnt > 0) {
+                tmem_ld32(tO + 32 * ch, x);
+                tmem_ld_wait32(x);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    x[e] = 0u;
+                }
+            }
+            if (vrow) {
+                float *op = orow + 32 * ch;
+                if (al16) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        *reinterpret_cast<float4 *>(op + e) =
+                            make_float4(__uint_as_float(x[e]) * inv, __uint_as_float(x[e + 1]) * inv,
+                                        __uint_as_float(x[e + 2]) * inv, __uint_as_float(x[e + 3]) * inv);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        op[e] = __uint_as_float(x[e]) * inv;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
+    static thread_local int configured_dev = -1;
+    int                     dev            = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(fa_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) {
+            return e;
+        }
+        configured_dev = dev;
+    }
+    int                 n = 0;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (L.classify) {
+        cudaLaunchConfig_t c = {};
+        c.gridDim            = dim3((unsigned) L.p.n_kt, (unsigned) L.p.n_rt, (unsigned) L.p.op.m_ne3);
+        c.blockDim           = dim3(256);
+        c.stream             = s;
+        c.attrs              = attr;
+        c.numAttrs           = 1;
+        cudaError_t e        = cudaLaunchKernelEx(&c, fa_mask_classify, L.p);
+        if (e != cudaSuccess) {
+            return e;
+        }
+        ++n;
+    }
+    cudaLaunchConfig_t c = {};
+    c.gridDim            = dim3((unsigned) L.p.n_pairs, (unsigned) L.p.op.Hkv, (unsigned) L.p.op.B);
+    c.blockDim           = dim3(kThreads);
+    c.dynamicSmemBytes   = kSmemBytes;
+    c.stream             = s;
+    c.attrs              = attr;
+    c.numAttrs           = 1;
+    cudaError_t e        = cudaLaunchKernelEx(&c, fa_dense_kernel, L.p, L.kmap, L.vmap);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    if (launches) {
+        *launches = n + 1;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace acefa

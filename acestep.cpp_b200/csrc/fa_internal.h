@@ -89,6 +89,36 @@ int         decode_ctas_per_sm(int kv_type, int D);
 size_t      decode_smem_bytes(int kv_type, int D);
 
 // ------------------------------------------------------------------ dense
-struct DenseParams;  // defined in fa_dense.cu
+// tcgen05 kernel for query-heavy nodes (LM prefill, DiT self/cross, encoders):
+// a CTA owns two 128-row tiles of one (batch, kv head) unit and streams the
+// unit's 128-key tiles through tensor memory.
+constexpr int kDenseBM    = 128;  // rows per row tile (MMA M)
+constexpr int kDenseBN    = 128;  // keys per key tile (MMA N of S)
+constexpr int kDenseMaxKT = 512;  // key tiles the class table holds (n_kv <= 65536)
+
+// mask tile classes
+constexpr uint8_t kClsLive   = 1;  // some key of the tile is visible to some row
+constexpr uint8_t kClsMask   = 2;  // entries other than 0 present: read the mask
+constexpr uint8_t kClsBounds = 4;  // tile runs past n_kv
+
+struct DenseParams {
+    OpDesc         op;
+    int            rows_total;  // G * n_q rows per (b, hk) unit
+    int            n_rt;        // 128-row tiles per unit
+    int            n_pairs;     // CTAs per unit
+    int            n_kt;        // key tiles
+    const uint8_t *cls;         // [m_ne3][n_rt][n_kt] classes, or nullptr (no per-tile info)
+    uint8_t       *cls_out;     // same buffer, written by the classify pre-pass
+    int           *dev_err;
+    uint64_t       wait_limit_ns;
+};
+
+struct DenseLaunch {
+    DenseParams p;
+    CUtensorMap kmap, vmap;  // box {64, 128, 1, 1}, 128-B swizzle
+    bool        classify;    // run the mask-classification pre-pass
+};
+
+cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches);
 
 }  // namespace acefa

@@ -1,0 +1,171 @@
+"""GPU parity of the dense tcgen05 path (LM prefill, encoders, DiT self/cross)
+against the CPU oracle, through the C ABI.  Same tolerance as the decode path:
+max-abs 2e-3, cosine >= 0.99995 vs the FP32 oracle; mask indexing bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+import acefa
+import oracle
+from fa_cases import Case, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def run_case(case, rows=None, **kw):
+    got = case.gpu(**kw)
+    assert acefa.last_path() == 2, "expected the dense tcgen05 path"
+    if rows is None:
+        want = case.oracle(**kw)
+    else:
+        want = oracle_rows(case, rows, **kw)
+        got = got[:, rows]
+    assert_close(got, want, what=str(kw))
+    assert acefa.device_error() == 0
+    return got, want
+
+
+def oracle_rows(case, rows, scale=None, max_bias=0.0, softcap=0.0):
+    """Oracle on a subset of query rows (mask rows follow), full K/V."""
+    scale = case.D ** -0.5 if scale is None else scale
+    kt = {"f16": oracle.GGML_F16}[case.kv]
+    q = case.q_cpu.numpy()[:, :, rows]
+    kc = case.k_cache_cpu.numpy()[case.s0:case.s0 + case.Bk, :, :case.n_kv]
+    vc = case.v_cache_cpu.numpy()[case.s0:case.s0 + case.Bk, :, :case.n_kv]
+    m = None if case.mask_cpu is None else np.ascontiguousarray(case.mask_cpu.numpy()[:, :, rows])
+    s = None if case.sinks_cpu is None else case.sinks_cpu.numpy()
+    return oracle.flash_attn_ext(np.ascontiguousarray(q), kc, vc, m, s, scale=scale, max_bias=max_bias,
+                                 softcap=softcap, k_type=kt, v_type=kt, d=case.D, dv=case.D)
+
+
+def pad256(x):
+    return (x + 255) // 256 * 256
+
+
+@pytest.mark.parametrize("S", [100, 257, 1024])
+def test_lm_causal_prefill_cache_view(S):
+    """qwen3-lm.h prefill: Q [128,S,16], K/V views [128,PAD(S,256),8] of a
+    [128,max_seq,8] cache, causal mask [PAD(S,256), S] with -inf past each row."""
+    n_kv = pad256(S)
+    c = Case(42 + 1000 * 3 + S, B=1, Hq=16, Hkv=8, n_q=S, n_kv=n_kv, max_seq=4096,
+             mask=lambda m: causal_mask(m, S))
+    run_case(c)
+
+
+def causal_mask(m, S):
+    # query i (absolute position i, kv_pos = 0) sees keys 0..i
+    n = m.shape[-1]
+    j = torch.arange(n)
+    for i in range(S):
+        m[..., i, :] = torch.where(j <= i, 0.0, float("-inf"))
+    return m
+
+
+@pytest.mark.parametrize("S,H,Hkv", [(300, 16, 16), (600, 16, 8), (1500, 16, 16)])
+def test_dit_self_attention_unmasked(S, H, Hkv):
+    c = Case(42 + 1000 * 4 + S, B=2, Hq=H, Hkv=Hkv, n_q=S, n_kv=S, mask=None)
+    run_case(c)
+
+
+def window_mask(m, win):
+    S_q, S_k = m.shape[-2], m.shape[-1]
+    qi = torch.arange(S_q)[:, None]
+    kj = torch.arange(S_k)[None, :]
+    m[...] = torch.where((qi - kj).abs() <= win, 0.0, float("-inf"))
+    return m
+
+
+@pytest.mark.parametrize("S,win", [(700, 64), (1000, 128)])
+def test_dit_self_attention_window(S, win):
+    c = Case(42 + 1000 * 4 + 7 * S + win, B=2, Hq=16, Hkv=16, n_q=S, n_kv=S, mask=lambda m: window_mask(m, win),
+             m_batch=2)
+    run_case(c)
+
+
+def padding_mask(valid):
+    def f(m):
+        for b in range(m.shape[0]):
+            m[b, :, :, valid[b]:] = float("-inf")
+        return m
+    return f
+
+
+@pytest.mark.parametrize("S,enc,valid", [(1000, 512, (461, 400)), (300, 238, (238, 200))])
+def test_dit_cross_attention_padding(S, enc, valid):
+    c = Case(42 + 1000 * 5 + S, B=2, Hq=16, Hkv=16, n_q=S, n_kv=enc, mask=padding_mask(valid), m_batch=2)
+    run_case(c)
+
+
+@pytest.mark.parametrize("n_q,n_kv", [(65, 1), (129, 130), (250, 127), (333, 1000)])
+def test_ragged_shapes(n_q, n_kv):
+    c = Case(42 + n_q * 7 + n_kv, B=1, Hq=4, Hkv=2, n_q=n_q, n_kv=n_kv, mask="random")
+    run_case(c)
+
+
+def test_sinks_softcap_alibi_dense():
+    c = Case(4500, B=2, Hq=8, Hkv=4, n_q=200, n_kv=300, mask="random", sinks=True)
+    run_case(c, max_bias=8.0, softcap=20.0)
+
+
+def test_per_head_mask_without_classes():
+    c = Case(4600, B=2, Hq=8, Hkv=2, n_q=100, n_kv=400, mask="random", m_heads=8, m_batch=1, mask_pad=9)
+    run_case(c)
+
+
+def test_fully_masked_rows_dense():
+    def mk(m):
+        m[:, :, 5, :] = float("-inf")
+        m[:, :, 150:, :] = float("-inf")
+        m[:, :, 10, 300:] = float("-inf")
+        return m
+
+    c = Case(4700, B=1, Hq=4, Hkv=4, n_q=200, n_kv=333, mask=mk)
+    got, _ = run_case(c)
+    assert np.all(got[:, 5] == 0.0) and np.all(got[:, 150:] == 0.0)
+
+
+def test_mask_indexing_bit_exact_dense():
+    n_kv, D = 128, 128
+    c = Case(4800, B=2, Hq=4, Hkv=2, n_q=100, n_kv=n_kv, D=D, mask="random", m_heads=1, m_batch=2)
+    c.q_cpu.zero_()
+    c.q.zero_()
+    c.v_cache_cpu[:] = torch.eye(n_kv, D).half()
+    c.v_cache.copy_(c.v_cache_cpu)
+    got = c.gpu()
+    assert acefa.last_path() == 2
+    m = c.mask_cpu.float().numpy()
+    for b in range(2):
+        for h in range(4):
+            vis = np.isfinite(m[b, 0, :100, :n_kv])
+            nz = got[b, :, h, :n_kv] != 0.0
+            assert np.array_equal(vis, nz), (b, h)
+
+
+@pytest.mark.parametrize("S", [6000])
+def test_full_size_dit_config4_sampled_rows(S):
+    """BASELINE config 4 at full size (S=6000, B=2, 16x128, window and padding
+    variants): every output row is computed, a seeded sample is checked."""
+    rng = np.random.default_rng(42 + 1000 * 4)
+    rows = np.sort(rng.choice(S, 48, replace=False))
+    rows = np.unique(np.concatenate([rows, [0, 127, 128, S - 1]]))
+    c = Case(42 + 1000 * 4 + 1, B=2, Hq=16, Hkv=16, n_q=S, n_kv=S, mask=None)
+    run_case(c, rows=rows)
+    cw = Case(42 + 1000 * 4 + 2, B=2, Hq=16, Hkv=16, n_q=S, n_kv=S, mask=lambda m: window_mask(m, 128), m_batch=1)
+    run_case(cw, rows=rows)
+    cx = Case(42 + 1000 * 4 + 3, B=2, Hq=16, Hkv=16, n_q=S, n_kv=512, mask=padding_mask((461, 461)), m_batch=2)
+    run_case(cx, rows=rows)
+
+
+def test_full_size_prefill_config3_sampled_rows():
+    """Qwen3-1.7B causal prefill, 16/8 heads, S=4096, batch 2
+    (the two CFG sequences in one call), unit-RMS Q/K rows."""
+    S = 4096
+    rng = np.random.default_rng(42 + 1000 * 3)
+    rows = np.unique(np.concatenate([np.sort(rng.choice(S, 40, replace=False)), [0, 1, 255, 256, S - 1]]))
+    c = Case(42 + 1000 * 3 + 9, B=2, Hq=16, Hkv=8, n_q=S, n_kv=S, mask=lambda m: causal_mask(m, S), m_batch=1)
+    # QK-norm: unit-RMS rows
+    c.q_cpu = c.q_cpu / c.q_cpu.pow(2).mean(-1, keepdim=True).sqrt()
+    kf = c.k_cache_cpu.float()
+    c.k_cache_cpu = (kf / kf.pow(2).mean(-1, keepdim=True).sqrt()).half()
+    c.to("cuda")
+    run_case(c, rows=rows)
