@@ -240,8 +240,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             }
         };
         auto acquire = [&]() -> bool {
-            return mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_f, P.dev_err, DEVERR_TIMEOUT_EMPTY,
-                                     P.wait_limit_ns);
+            // all lanes poll; the outcome is made warp-uniform because the
+            // ballots and shuffles after it need the whole warp
+            return __all_sync(0xffffffffu, mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_f, P.dev_err,
+                                                             DEVERR_TIMEOUT_EMPTY, P.wait_limit_ns));
         };
         // Stage the mask segment [64*ti, 64*ti + 64) of every slot row.  Returns
         // the bytes the caller must add to the barrier's transaction count (the
@@ -760,7 +762,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         setup_unit(cur_unit);
     }
     while (true) {
-        if (!mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err, DEVERR_TIMEOUT_FULL, P.wait_limit_ns)) {
+        const bool got =
+            mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err, DEVERR_TIMEOUT_FULL, P.wait_limit_ns);
+        // ldmatrix / mma.sync / shuffles below are warp-collective: leave together
+        if (!__all_sync(0xffffffffu, got)) {
             break;
         }
         const int4 md = meta[stage];

@@ -380,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int j0 = j * kDenseBN;
             ok = mbar_wait_bounded(&s_ready[i], (uint32_t) (cnt & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
                                    P.wait_limit_ns);
+            ok = __all_sync(0xffffffffu, ok);  // the collectives below need the whole warp
             if (!ok) {
                 break;
             }
@@ -436,17 +437,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (cnt > 0) {
                 ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
                                        P.wait_limit_ns);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) {
                     break;
                 }
                 tc_fence_after();
             }
             const float m_new = fmaxf(m_run, tmax);
+            // Rows whose max grew by more than 2^8 rescale O and l.  tcgen05.ld/st
+            // are warp-collective, so the whole warp walks O when any row needs
+            // it; the other rows multiply by 1.
+            const bool need = m_run != -INFINITY && m_new > m_run + kRescaleLog2;
+            float      f    = 1.0f;
+            if (need) {
+                f = fast_exp2(m_run - m_new);
+                l_run *= f;
+                m_run = m_new;
+            }
             if (m_run == -INFINITY) {
                 m_run = m_new;  // nothing accumulated yet for this row
-            } else if (m_new > m_run + kRescaleLog2) {
-                const float f = fast_exp2(m_run - m_new);
-                l_run *= f;
+            }
+            if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
                 for (int ch = 0; ch < 4; ++ch) {
                     uint32_t x[32];
@@ -458,7 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tmem_st32(tO + 32 * ch, x);
                 }
-                m_run = m_new;
             }
             // ---- pass 2: P = exp2(x - m) as f16 pairs over the S columns
             const float m_use = m_run == -INFINITY ? 0.0f : m_run;
@@ -488,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    P.wait_limit_ns);
             tc_fence_after();
         }
+        ok = __all_sync(0xffffffffu, ok);
         float fs = 1.0f;
         if (o.sinks && vrow) {
             const float ts = o.sinks[hq] * kLog2e;
