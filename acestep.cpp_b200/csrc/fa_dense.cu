@@ -367,6 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                       (int64_t) (b % o.m_ne3) * o.m_nb3);
         }
         const float slope = alibi_slope(o, hq);
+        // softcap or a non-positive scale take the general path on every tile
+        const bool  general    = o.softcap != 0.0f || !(o.scale_eff > 0.0f);
+        const float scale_log2 = o.scale_eff * kLog2e;
         float       m_run = -INFINITY;  // log2 units
         float       l_run = 0.0f;
         int         cnt   = 0;
@@ -385,54 +388,77 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            // ---- pass 1: logits in log2 units (written back), tile max
-            float tmax = -INFINITY;
+            // Fast tiles (no mask values, no bounds, no softcap, positive scale)
+            // only need max(S) now and exp2(S*c - m) later; the rest rewrite S
+            // as finished log2-unit logits first.
+            const bool fast = !(c & (kClsMask | kClsBounds)) && !general;
+            float      tmax = -INFINITY;
+            if (fast) {
+                // ---- pass 1 (fast): max of raw scores, two chunks in flight
+                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t x[32];
-                tmem_ld32(tS + 32 * ch, x);
-                tmem_ld_wait32(x);
-                uint16_t mk[32];
-                if (c & kClsMask) {
-                    const uint16_t *mp = mrow + j0 + 32 * ch;
-                    if ((reinterpret_cast<uintptr_t>(mp) & 15u) == 0 && j0 + 32 * ch + 32 <= o.m_ne0) {
+                for (int ch = 0; ch < 4; ch += 2) {
+                    uint32_t x[32], y[32];
+                    tmem_ld32(tS + 32 * ch, x);
+                    tmem_ld32(tS + 32 * ch + 32, y);
+                    tmem_ld_wait32(x);
+                    tmem_ld_wait32(y);
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            const uint4 w = __ldg(reinterpret_cast<const uint4 *>(mp) + q4);
-                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                    for (int e = 0; e < 32; e += 2) {
+                        mx[(e >> 1) & 3] = fmaxf(mx[(e >> 1) & 3], fmaxf(__uint_as_float(x[e]), __uint_as_float(x[e + 1])));
+                        mx[(e >> 1) & 3] = fmaxf(mx[(e >> 1) & 3], fmaxf(__uint_as_float(y[e]), __uint_as_float(y[e + 1])));
+                    }
+                }
+                tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+            } else {
+                // ---- pass 1 (general): logits in log2 units, written back
+#pragma unroll 1
+                for (int ch = 0; ch < 4; ++ch) {
+                    uint32_t x[32];
+                    tmem_ld32(tS + 32 * ch, x);
+                    tmem_ld_wait32(x);
+                    uint16_t mk[32];
+                    if (c & kClsMask) {
+                        const uint16_t *mp = mrow + j0 + 32 * ch;
+                        if ((reinterpret_cast<uintptr_t>(mp) & 15u) == 0 && j0 + 32 * ch + 32 <= o.m_ne0) {
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                mk[8 * q4 + 2 * e]     = (uint16_t) (ws[e] & 0xFFFFu);
-                                mk[8 * q4 + 2 * e + 1] = (uint16_t) (ws[e] >> 16);
+                            for (int q4 = 0; q4 < 4; ++q4) {
+                                const uint4    w     = __ldg(reinterpret_cast<const uint4 *>(mp) + q4);
+                                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    mk[8 * q4 + 2 * e]     = (uint16_t) (ws[e] & 0xFFFFu);
+                                    mk[8 * q4 + 2 * e + 1] = (uint16_t) (ws[e] >> 16);
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                mk[e] = j0 + 32 * ch + e < o.m_ne0 ? __ldg(mp + e) : kHalfNegInf;
                             }
                         }
-                    } else {
+                    }
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            mk[e] = j0 + 32 * ch + e < o.m_ne0 ? __ldg(mp + e) : kHalfNegInf;
+                    for (int e = 0; e < 32; ++e) {
+                        float v = __uint_as_float(x[e]) * o.scale_eff;
+                        if (o.softcap != 0.0f) {
+                            v = o.softcap * tanhf(v);
                         }
+                        if (c & kClsMask) {
+                            const float mv = slope * __half2float(__ushort_as_half(mk[e]));
+                            v              = mv == -INFINITY ? -INFINITY : v + mv;
+                        }
+                        if ((c & kClsBounds) && j0 + 32 * ch + e >= o.n_kv) {
+                            v = -INFINITY;
+                        }
+                        v *= kLog2e;
+                        tmax = fmaxf(tmax, v);
+                        x[e] = __float_as_uint(v);
                     }
+                    tmem_st32(tS + 32 * ch, x);
                 }
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float v = __uint_as_float(x[e]) * o.scale_eff;
-                    if (o.softcap != 0.0f) {
-                        v = o.softcap * tanhf(v);
-                    }
-                    if (c & kClsMask) {
-                        const float mv = slope * __half2float(__ushort_as_half(mk[e]));
-                        v              = mv == -INFINITY ? -INFINITY : v + mv;
-                    }
-                    if ((c & kClsBounds) && j0 + 32 * ch + e >= o.n_kv) {
-                        v = -INFINITY;
-                    }
-                    v *= kLog2e;
-                    tmax = fmaxf(tmax, v);
-                    x[e] = __float_as_uint(v);
-                }
-                tmem_st32(tS + 32 * ch, x);
+                tmem_st_wait();
             }
-            tmem_st_wait();
             // ---- previous PV must be done before O is touched or P overwrites S
             if (cnt > 0) {
                 ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
@@ -472,21 +498,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // ---- pass 2: P = exp2(x - m) as f16 pairs over the S columns
             const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+            // fast tiles: x = s * c, so exp2(s * c - m) is one FMA before the ex2
+            const float mul = fast ? scale_log2 : 1.0f;
+            float       ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t x[32];
+            for (int ch = 0; ch < 4; ch += 2) {
+                uint32_t x[32], y[32];
                 tmem_ld32(tS + 32 * ch, x);
+                tmem_ld32(tS + 32 * ch + 32, y);
                 tmem_ld_wait32(x);
-                uint32_t pk[16];
+                tmem_ld_wait32(y);
+                uint32_t pk[16], pk2[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const float p0 = fast_exp2(__uint_as_float(x[2 * e]) - m_use);
-                    const float p1 = fast_exp2(__uint_as_float(x[2 * e + 1]) - m_use);
-                    l_run += p0 + p1;
-                    pk[e] = pack2<false>(p0, p1);
+                    const float p0 = fast_exp2(fmaf(__uint_as_float(x[2 * e]), mul, -m_use));
+                    const float p1 = fast_exp2(fmaf(__uint_as_float(x[2 * e + 1]), mul, -m_use));
+                    const float q0 = fast_exp2(fmaf(__uint_as_float(y[2 * e]), mul, -m_use));
+                    const float q1 = fast_exp2(fmaf(__uint_as_float(y[2 * e + 1]), mul, -m_use));
+                    ls[e & 3] += (p0 + p1) + (q0 + q1);
+                    pk[e]  = pack2<false>(p0, p1);
+                    pk2[e] = pack2<false>(q0, q1);
                 }
                 tmem_st16(tS + 16 * ch, pk);
+                tmem_st16(tS + 16 * ch + 16, pk2);
             }
+            l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_ready[i]);

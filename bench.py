@@ -355,6 +355,7 @@ def run_ours(args):
 
     if rank == 0 and not args.no_extras:
         out["extras"] = extras(device, stream, args)
+        out["extras"]["dense"] = dense_extras(device, stream)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -411,6 +412,110 @@ def extras(device, stream, args):
     return res
 
 
+# -------------------------------------------------------------------------
+# dense path (BASELINE configs 3 and 4): TFLOP/s over unmasked (q, k) pairs
+DENSE_WORKLOADS = {
+    # name: (B, Hq, Hkv, S_q, S_kv, mask kind, extra)
+    "prefill1024": (2, 16, 8, 1024, 1024, "causal", None),
+    "prefill4096": (2, 16, 8, 4096, 4096, "causal", None),
+    "dit1500": (2, 16, 16, 1500, 1500, None, None),
+    "dit6000": (2, 16, 16, 6000, 6000, None, None),
+    "dit6000_window128": (2, 16, 16, 6000, 6000, "window", 128),
+    "cross6000": (2, 16, 16, 6000, 512, "padding", 461),
+}
+
+
+def dense_pairs(S_q, S_kv, kind, extra):
+    if kind is None:
+        return S_q * S_kv
+    if kind == "causal":
+        return S_q * (S_q + 1) // 2
+    if kind == "padding":
+        return S_q * extra
+    if kind == "window":
+        i = __import__("numpy").arange(S_q)
+        return int((__import__("numpy").minimum(S_kv - 1, i + extra) - __import__("numpy").maximum(0, i - extra) + 1).sum())
+    raise ValueError(kind)
+
+
+def build_dense(device, name, seed=SEED + 3):
+    import torch
+
+    import acefa
+
+    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name]
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(B, Hq, S_q, D, device=device, generator=g)
+    k = torch.randn(B, Hkv, S_kv, D, device=device, generator=g, dtype=torch.float16)
+    v = torch.randn(B, Hkv, S_kv, D, device=device, generator=g, dtype=torch.float16)
+    mask = None
+    if kind is not None:
+        qi = torch.arange(S_q, device=device)[:, None]
+        kj = torch.arange(S_kv, device=device)[None, :]
+        if kind == "causal":
+            vis = kj <= qi
+        elif kind == "window":
+            vis = (qi - kj).abs() <= extra
+        else:
+            vis = (kj < extra).expand(S_q, S_kv)
+        mask = torch.where(vis, 0.0, float("-inf")).half().reshape(1, 1, S_q, S_kv).contiguous()
+    op = acefa.Op(q, k, v, mask=mask, scale=D ** -0.5)
+    flops = 4 * D * dense_pairs(S_q, S_kv, kind, extra) * Hq * B
+    return op, flops
+
+
+def time_dense(device, stream, name, iters=10, warmup=3):
+    import torch
+
+    import acefa
+
+    op, flops = build_dense(device, name)
+    with torch.cuda.stream(stream):
+        op(stream=stream)
+        path = acefa.last_path()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            op(stream=stream)
+        for _ in range(warmup):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    del graph, op
+    return {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1), "gflop": round(flops / 1e9, 2),
+            "path": "dense tcgen05" if path == 2 else "decode"}
+
+
+def dense_extras(device, stream):
+    peak = 1635.6
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        peak = float(json.load(open(p))["bf16_tflops"])
+    res = {"peak_tflops": peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; kernel timed alone)"}
+    for name in DENSE_WORKLOADS:
+        r = time_dense(device, stream, name)
+        r["frac_of_peak"] = round(r["tflops"] / peak, 4)
+        res[name] = r
+    return res
+
+
+def run_dense_workload(args):
+    """--workload <dense name>: time one dense op (also the ncu profiling case)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(device=device)
+    r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup)
+    print(json.dumps({"workload": args.workload, **r}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -422,11 +527,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (36 = the headline stack)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
+    ap.add_argument("--workload", default="decode4b",
+                    help="decode4b (headline) or one dense op: " + ", ".join(DENSE_WORKLOADS))
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "decode4b":
+        return run_dense_workload(args)
     return run_ours(args)
 
 
