@@ -27,7 +27,9 @@ STATUS_NAMES = {
 }
 
 _PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(_PKG_DIR, "libacefa.so")
+# ACEFA_LIBRARY selects another build of the same ABI (e.g. a variant compiled
+# with different tuning macros); by default the in-tree library is used.
+LIB_PATH = os.environ.get("ACEFA_LIBRARY") or os.path.join(_PKG_DIR, "libacefa.so")
 
 EXPORTED_SYMBOLS = (
     "acefa_flash_attn_ext",

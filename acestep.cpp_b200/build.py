@@ -38,14 +38,20 @@ def _newest_input() -> float:
     return max(os.path.getmtime(p) for p in paths)
 
 
-def build(force: bool = False, ptxas_verbose: bool = False, jobs: int = 4) -> str:
-    if not force and os.path.exists(OUT) and os.path.getmtime(OUT) >= _newest_input():
-        return OUT
-    os.makedirs(BUILD, exist_ok=True)
+def build(force: bool = False, ptxas_verbose: bool = False, jobs: int = 4, out: str | None = None,
+          defines: list[str] | None = None, build_dir: str | None = None) -> str:
+    """Compile and link.  `out`, `defines` (-D macros) and `build_dir` build a
+    variant library elsewhere; the defaults build the in-tree libacefa.so."""
+    target = out or OUT
+    bdir = build_dir or BUILD
+    if not force and os.path.exists(target) and os.path.getmtime(target) >= _newest_input():
+        return target
+    os.makedirs(bdir, exist_ok=True)
     objs, procs = [], []
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    extra += [f"-D{d}" for d in (defines or [])]
     for src in _sources():
-        obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+        obj = os.path.join(bdir, src.replace(".cu", ".o"))
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-I", os.path.join(ROOT, "include"), "-c",
                os.path.join(CSRC, src), "-o", obj]
         procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
@@ -59,10 +65,10 @@ def build(force: bool = False, ptxas_verbose: bool = False, jobs: int = 4) -> st
             failed = True
     if failed:
         raise RuntimeError("nvcc failed")
-    tmp = OUT + ".tmp"
+    tmp = target + ".tmp"
     subprocess.check_call([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"])
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":

@@ -258,8 +258,9 @@ DecodePlan plan_decode(const OpDesc &o, int sm_count) {
 bool use_dense(const OpDesc &o) {
     const int64_t rows = (int64_t) o.G * o.n_q;
     const int64_t n_kt = ((int64_t) o.n_kv + kDenseBN - 1) / kDenseBN;
-    return o.kv_type == ACEFA_TYPE_F16 && o.D == 128 && rows > 64 && n_kt <= kDenseMaxKT && o.B <= 65535 &&
-           o.Hkv <= 65535;
+    const int64_t n_pairs = ((rows + kDenseBM - 1) / kDenseBM + 1) / 2;
+    return o.kv_type == ACEFA_TYPE_F16 && o.D == 128 && rows > 64 && n_kt <= kDenseMaxKT &&
+           n_pairs * o.Hkv * o.B < (1ll << 31);
 }
 
 struct DensePlan {

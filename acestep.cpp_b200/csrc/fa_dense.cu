@@ -28,7 +28,7 @@
 namespace acefa {
 namespace {
 
-constexpr int      kThreads    = 384;
+constexpr int      kThreads    = 384;  // warp 0 TMA, warp 1 MMA, 2-3 spare, 4-7 / 8-11 softmax
 constexpr int      kRing       = 4;
 constexpr int      kTileBytes  = kDenseBN * 128 * 2;  // 32 KB: 128 keys x 128 dims f16
 constexpr int      kQBytes     = kDenseBM * 128 * 2;  // 32 KB
@@ -42,7 +42,14 @@ constexpr int      kSmemBytes  = kOffMisc + 16 + 1024;
 constexpr uint32_t kTmemCols   = 512;
 constexpr float    kRescaleLog2 = 8.0f;  // O is rescaled only when the max grows by > 2^8
 
+
 constexpr uint16_t kHalfNegInf = 0xFC00u;
+
+// Share of softmax exponentials computed by poly_exp2 on the FMA pipe instead of
+// ex2 on the MUFU unit: 0 = none, 1 = one in four, 2 = one in two.
+#ifndef ACEFA_POLY_EXP
+#define ACEFA_POLY_EXP 0
+#endif
 
 __device__ __forceinline__ void row_to_query(int gr, int G, int hk, int &iq, int &hq) {
     iq = gr / G;
@@ -64,7 +71,7 @@ __global__ void __launch_bounds__(256) fa_mask_classify(const __grid_constant__ 
     const int     iq0 = gr0 / G, iq1 = gr1 / G;
     const int     j0 = kt * kDenseBN, j1 = min(o.n_kv, j0 + kDenseBN);
     const int     nj = j1 - j0;
-    int           live = 0, nonzero = 0;
+    int           live = 0, nonzero = 0, nonbinary = 0;
     pdl_wait_primary();
     const char *mbase = o.mask + (int64_t) bm * o.m_nb3;
     for (int idx = threadIdx.x; idx < (iq1 - iq0 + 1) * nj; idx += blockDim.x) {
@@ -73,14 +80,127 @@ __global__ void __launch_bounds__(256) fa_mask_classify(const __grid_constant__ 
         const uint16_t  h  = __ldg(reinterpret_cast<const uint16_t *>(mbase + (int64_t) iq * o.m_nb1) + j);
         live |= h != kHalfNegInf;
         nonzero |= (h & 0x7FFFu) != 0;
+        nonbinary |= (h & 0x7FFFu) != 0 && h != kHalfNegInf;
     }
-    live    = __syncthreads_or(live);
-    nonzero = __syncthreads_or(nonzero);
+    live      = __syncthreads_or(live);
+    nonzero   = __syncthreads_or(nonzero);
+    nonbinary = __syncthreads_or(nonbinary);
     if (threadIdx.x == 0) {
         P.cls_out[((int64_t) bm * P.n_rt + t) * P.n_kt + kt] =
-            (uint8_t) ((live ? kClsLive : 0) | (live && nonzero ? kClsMask : 0));
+            (uint8_t) ((live ? kClsLive : 0) | (live && nonzero ? kClsMask : 0) |
+                       (live && nonzero && !nonbinary ? kClsBinary : 0));
     }
     pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+// Softmax helpers of one row (thread) over one 128-key tile held in TMEM.
+
+// Bit k of vis[k/32] = key j0+k visible: inside n_kv and (for binary-mask
+// tiles) a mask entry that is not -inf.
+__device__ __forceinline__ void build_visibility(uint32_t (&vis)[4], uint8_t c, const uint16_t *mrow, int j0,
+                                                 int n_kv, int m_ne0) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        uint32_t bits = ~0u;
+        if (c & kClsBounds) {
+            const int room = n_kv - (j0 + 32 * w);
+            bits           = room >= 32 ? ~0u : (room <= 0 ? 0u : ((1u << room) - 1u));
+        }
+        if (c & kClsMask) {
+            const uint16_t *mp = mrow + j0 + 32 * w;
+            uint32_t        mb = 0;
+            if ((reinterpret_cast<uintptr_t>(mp) & 15u) == 0 && j0 + 32 * w + 32 <= m_ne0) {
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const uint4    v     = __ldg(reinterpret_cast<const uint4 *>(mp) + q4);
+                    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        mb |= (uint32_t) ((ws[e] & 0xFFFFu) != kHalfNegInf) << (8 * q4 + 2 * e);
+                        mb |= (uint32_t) ((ws[e] >> 16) != kHalfNegInf) << (8 * q4 + 2 * e + 1);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const bool in = j0 + 32 * w + e < m_ne0 && __ldg(mp + e) != kHalfNegInf;
+                    mb |= (uint32_t) in << e;
+                }
+            }
+            bits &= mb;
+        }
+        vis[w] = bits;
+    }
+}
+
+template <bool VIS>
+__device__ __forceinline__ float pass1_max(uint32_t tS, const uint32_t (&vis)[4]) {
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ch += 2) {
+        uint32_t x[32], y[32];
+        tmem_ld32(tS + 32 * ch, x);
+        tmem_ld32(tS + 32 * ch + 32, y);
+        tmem_ld_wait32(x);
+        tmem_ld_wait32(y);
+        const uint32_t va = ch == 0 ? vis[0] : vis[2];  // keep vis in registers
+        const uint32_t vb = ch == 0 ? vis[1] : vis[3];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            float a = __uint_as_float(x[e]), b = __uint_as_float(y[e]);
+            if constexpr (VIS) {
+                a = (va >> e) & 1u ? a : -INFINITY;
+                b = (vb >> e) & 1u ? b : -INFINITY;
+            }
+            mx[e & 3] = fmaxf(mx[e & 3], fmaxf(a, b));
+        }
+    }
+    return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// P = exp2(x * mul - m) as f16 pairs written over the first 64 S columns;
+// row sums accumulate into ls[4].
+template <bool VIS>
+__device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4], float mul, float m_use,
+                                          float (&ls)[4]) {
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ch += 2) {
+        uint32_t x[32], y[32];
+        tmem_ld32(tS + 32 * ch, x);
+        tmem_ld32(tS + 32 * ch + 32, y);
+        tmem_ld_wait32(x);
+        tmem_ld_wait32(y);
+        uint32_t       pk[16], pk2[16];
+        const uint32_t va = ch == 0 ? vis[0] : vis[2];
+        const uint32_t vb = ch == 0 ? vis[1] : vis[3];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            float p0 = fast_exp2(fmaf(__uint_as_float(x[2 * e]), mul, -m_use));
+            float p1 = fast_exp2(fmaf(__uint_as_float(x[2 * e + 1]), mul, -m_use));
+#if ACEFA_POLY_EXP >= 2
+            float q0 = poly_exp2(fmaf(__uint_as_float(y[2 * e]), mul, -m_use));
+#else
+            float q0 = fast_exp2(fmaf(__uint_as_float(y[2 * e]), mul, -m_use));
+#endif
+#if ACEFA_POLY_EXP >= 1
+            float q1 = poly_exp2(fmaf(__uint_as_float(y[2 * e + 1]), mul, -m_use));
+#else
+            float q1 = fast_exp2(fmaf(__uint_as_float(y[2 * e + 1]), mul, -m_use));
+#endif
+            if constexpr (VIS) {
+                p0 = (va >> (2 * e)) & 1u ? p0 : 0.0f;
+                p1 = (va >> (2 * e + 1)) & 1u ? p1 : 0.0f;
+                q0 = (vb >> (2 * e)) & 1u ? q0 : 0.0f;
+                q1 = (vb >> (2 * e + 1)) & 1u ? q1 : 0.0f;
+            }
+            ls[e & 3] += (p0 + p1) + (q0 + q1);
+            pk[e]  = pack2<false>(p0, p1);
+            pk2[e] = pack2<false>(q0, q1);
+        }
+        tmem_st16(tS + 16 * ch, pk);
+        tmem_st16(tS + 16 * ch + 16, pk2);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -104,9 +224,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const OpDesc &o    = P.op;
     const int     warp = threadIdx.x >> 5;
     const int     lane = threadIdx.x & 31;
-    const int     pair = P.n_pairs - 1 - (int) blockIdx.x;  // heavy (late, causal) tiles first
-    const int     hk   = blockIdx.y;
-    const int     b    = blockIdx.z;
+    // 1-D grid, pair index slowest and descending: every (batch, head) unit's
+    // late (for causal masks, heaviest) row tiles are scheduled first
+    const int     units = o.B * o.Hkv;
+    const int     pair  = P.n_pairs - 1 - (int) (blockIdx.x / units);
+    const int     hk    = (int) (blockIdx.x % units) % o.Hkv;
+    const int     b     = (int) (blockIdx.x % units) / o.Hkv;
     const int     bk   = b / o.rk3;
     const int     t0   = 2 * pair;
     const bool    has_tile[2] = {t0 < P.n_rt, t0 + 1 < P.n_rt};
@@ -185,7 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto live_of = [&](int i, int j) -> bool { return (s_cls[i * kDenseMaxKT + j] & kClsLive) != 0; };
     auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };
 
-    if (warp == 0) {
+    if (warp < 4) {
+      if (warp == 0) {
         // ============================ TMA producer ============================
         if (lane == 0) {
             int pend[kRing];
@@ -231,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ============================ MMA issuer ==============================
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_f16(128, 128, false, false, false);
@@ -346,8 +470,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp >= 4) {
+      }
+    } else {
         // ============================ softmax =================================
+        // warps 4-7 own row tile 0 and warps 8-11 row tile 1; a warp may only
+        // touch TMEM lanes 32*(warp%4) .. +31
         const int      i     = (warp - 4) >> 2;  // row tile
         const int      wq    = warp & 3;         // TMEM lane quarter
         const int      r     = wq * 32 + lane;
@@ -375,6 +502,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         int         cnt   = 0;
         bool        ok    = true;
 
+        // Waits for the previous PV (O and the P columns are then free), folds
+        // the tile max into the running max and rescales O and l when it grew
+        // by more than 2^8.  tcgen05.ld/st are warp-collective, so the whole warp
+        // walks O when any of its rows needs it (the others multiply by 1).
+        auto update_max = [&](float tmax) -> bool {
+            if (cnt > 0) {
+                ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
+                                       P.wait_limit_ns);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) {
+                    return false;
+                }
+                tc_fence_after();
+            }
+            const float m_new = fmaxf(m_run, tmax);
+            const bool  need  = m_run != -INFINITY && m_new > m_run + kRescaleLog2;
+            float       f     = 1.0f;
+            if (need) {
+                f = fast_exp2(m_run - m_new);
+                l_run *= f;
+                m_run = m_new;
+            }
+            if (m_run == -INFINITY) {
+                m_run = m_new;  // nothing accumulated yet for this row
+            }
+            if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint32_t x[16];
+                    tmem_ld16(tO + 16 * ch, x);
+                    tmem_ld_wait16(x);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        x[e] = __float_as_uint(__uint_as_float(x[e]) * f);
+                    }
+                    tmem_st16(tO + 16 * ch, x);
+                }
+            }
+            return true;
+        };
+
         for (int j = 0; j < P.n_kt && ok; ++j) {
             const uint8_t c = s_cls[i * kDenseMaxKT + j];
             if (!(c & kClsLive)) {
@@ -388,30 +556,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            // Fast tiles (no mask values, no bounds, no softcap, positive scale)
-            // only need max(S) now and exp2(S*c - m) later; the rest rewrite S
-            // as finished log2-unit logits first.
-            const bool fast = !(c & (kClsMask | kClsBounds)) && !general;
-            float      tmax = -INFINITY;
+            // Fast tiles (no mask values other than 0 / -inf, no softcap,
+            // positive scale): max of the raw scores, then exp2(s * c - m) in
+            // one FMA + ex2 per score.  Binary-mask and ragged tiles use a
+            // 128-bit visibility mask per row.  Other tiles rewrite S as
+            // finished log2-unit logits in TMEM first.
+            const bool fast = (!(c & kClsMask) || (c & kClsBinary)) && !general;
             if (fast) {
-                // ---- pass 1 (fast): max of raw scores, two chunks in flight
-                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-                for (int ch = 0; ch < 4; ch += 2) {
-                    uint32_t x[32], y[32];
-                    tmem_ld32(tS + 32 * ch, x);
-                    tmem_ld32(tS + 32 * ch + 32, y);
-                    tmem_ld_wait32(x);
-                    tmem_ld_wait32(y);
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        mx[(e >> 1) & 3] = fmaxf(mx[(e >> 1) & 3], fmaxf(__uint_as_float(x[e]), __uint_as_float(x[e + 1])));
-                        mx[(e >> 1) & 3] = fmaxf(mx[(e >> 1) & 3], fmaxf(__uint_as_float(y[e]), __uint_as_float(y[e + 1])));
-                    }
+                const bool use_vis = (c & (kClsMask | kClsBounds)) != 0;
+                uint32_t   vis[4]  = {~0u, ~0u, ~0u, ~0u};
+                if (use_vis) {
+                    build_visibility(vis, c, mrow, j0, o.n_kv, o.m_ne0);
                 }
-                tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+                const float tmax = (use_vis ? pass1_max<true>(tS, vis) : pass1_max<false>(tS, vis)) * scale_log2;
+                if (!update_max(tmax)) {
+                    break;
+                }
+                const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+                float       ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (use_vis) {
+                    pass2_exp<true>(tS, vis, scale_log2, m_use, ls);
+                } else {
+                    pass2_exp<false>(tS, vis, scale_log2, m_use, ls);
+                }
+                l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             } else {
                 // ---- pass 1 (general): logits in log2 units, written back
+                float tmax = -INFINITY;
 #pragma unroll 1
                 for (int ch = 0; ch < 4; ++ch) {
                     uint32_t x[32];
@@ -458,71 +629,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(tS + 32 * ch, x);
                 }
                 tmem_st_wait();
-            }
-            // ---- previous PV must be done before O is touched or P overwrites S
-            if (cnt > 0) {
-                ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
-                                       P.wait_limit_ns);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) {
+                if (!update_max(tmax)) {
                     break;
                 }
-                tc_fence_after();
+                // ---- pass 2 (general): P = exp2(x - m) over the S columns
+                const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+                float       ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const uint32_t all[4] = {~0u, ~0u, ~0u, ~0u};
+                pass2_exp<false>(tS, all, 1.0f, m_use, ls);
+                l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             }
-            const float m_new = fmaxf(m_run, tmax);
-            // Rows whose max grew by more than 2^8 rescale O and l.  tcgen05.ld/st
-            // are warp-collective, so the whole warp walks O when any row needs
-            // it; the other rows multiply by 1.
-            const bool need = m_run != -INFINITY && m_new > m_run + kRescaleLog2;
-            float      f    = 1.0f;
-            if (need) {
-                f = fast_exp2(m_run - m_new);
-                l_run *= f;
-                m_run = m_new;
-            }
-            if (m_run == -INFINITY) {
-                m_run = m_new;  // nothing accumulated yet for this row
-            }
-            if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-                for (int ch = 0; ch < 4; ++ch) {
-                    uint32_t x[32];
-                    tmem_ld32(tO + 32 * ch, x);
-                    tmem_ld_wait32(x);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        x[e] = __float_as_uint(__uint_as_float(x[e]) * f);
-                    }
-                    tmem_st32(tO + 32 * ch, x);
-                }
-            }
-            // ---- pass 2: P = exp2(x - m) as f16 pairs over the S columns
-            const float m_use = m_run == -INFINITY ? 0.0f : m_run;
-            // fast tiles: x = s * c, so exp2(s * c - m) is one FMA before the ex2
-            const float mul = fast ? scale_log2 : 1.0f;
-            float       ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-            for (int ch = 0; ch < 4; ch += 2) {
-                uint32_t x[32], y[32];
-                tmem_ld32(tS + 32 * ch, x);
-                tmem_ld32(tS + 32 * ch + 32, y);
-                tmem_ld_wait32(x);
-                tmem_ld_wait32(y);
-                uint32_t pk[16], pk2[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float p0 = fast_exp2(fmaf(__uint_as_float(x[2 * e]), mul, -m_use));
-                    const float p1 = fast_exp2(fmaf(__uint_as_float(x[2 * e + 1]), mul, -m_use));
-                    const float q0 = fast_exp2(fmaf(__uint_as_float(y[2 * e]), mul, -m_use));
-                    const float q1 = fast_exp2(fmaf(__uint_as_float(y[2 * e + 1]), mul, -m_use));
-                    ls[e & 3] += (p0 + p1) + (q0 + q1);
-                    pk[e]  = pack2<false>(p0, p1);
-                    pk2[e] = pack2<false>(q0, q1);
-                }
-                tmem_st16(tS + 16 * ch, pk);
-                tmem_st16(tS + 16 * ch + 16, pk2);
-            }
-            l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_ready[i]);
@@ -619,7 +735,7 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
         ++n;
     }
     cudaLaunchConfig_t c = {};
-    c.gridDim            = dim3((unsigned) L.p.n_pairs, (unsigned) L.p.op.Hkv, (unsigned) L.p.op.B);
+    c.gridDim            = dim3((unsigned) ((int64_t) L.p.n_pairs * L.p.op.Hkv * L.p.op.B));
     c.blockDim           = dim3(kThreads);
     c.dynamicSmemBytes   = kSmemBytes;
     c.stream             = s;

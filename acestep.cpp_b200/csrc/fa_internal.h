@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/acefa.h"
+#include "acefa.h"  // include/ is on the compiler include path
 
 namespace acefa {
 
@@ -100,6 +100,7 @@ constexpr int kDenseMaxKT = 512;  // key tiles the class table holds (n_kv <= 65
 constexpr uint8_t kClsLive   = 1;  // some key of the tile is visible to some row
 constexpr uint8_t kClsMask   = 2;  // entries other than 0 present: read the mask
 constexpr uint8_t kClsBounds = 4;  // tile runs past n_kv
+constexpr uint8_t kClsBinary = 8;  // every mask entry of the tile is 0 or -inf
 
 struct DenseParams {
     OpDesc         op;
