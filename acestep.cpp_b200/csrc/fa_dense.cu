@@ -153,10 +153,100 @@ __device__ __forceinline__ float pass1_max(uint32_t tS, const uint32_t (&vis)[4]
                 a = (va >> e) & 1u ? a : -INFINITY;
                 b = (vb >> e) & 1u ? b : -INFINITY;
             }
-            mx[e & 3] = fmaxf(mx[e & 3], fmaxf(a, b));
+            mx[e & 3] = fmax3(mx[e & 3], a, b);
         }
     }
     return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// Fast-tile P: t = s * c - m by packed FMA (two scores per instruction),
+// rounded to f16x2 and exponentiated by ex2.approx.f16x2 (two results per MUFU
+// op), which is already P's storage format.  Masked keys get t = -inf, so
+// P = 0 exactly.  Row sums add the f16 pairs in groups of four and fold them into
+// f32 once per 32 keys.
+template <bool VIS>
+__device__ __forceinline__ void pass2_exp_packed(uint32_t tS, const uint32_t (&vis)[4], float mul, float m_use,
+                                                 float (&ls)[4]) {
+    const uint64_t c2 = f32x2(mul, mul);
+    const uint64_t m2 = f32x2(-m_use, -m_use);
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ch += 2) {
+        uint32_t x[32], y[32];
+        tmem_ld32(tS + 32 * ch, x);
+        tmem_ld32(tS + 32 * ch + 32, y);
+        tmem_ld_wait32(x);
+        tmem_ld_wait32(y);
+        const uint32_t va = ch == 0 ? vis[0] : vis[2];
+        const uint32_t vb = ch == 0 ? vis[1] : vis[3];
+        uint32_t       pk[16], pk2[16];
+        uint32_t       ha[4], hb[4];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            float a0, a1, b0, b1;
+            f32x2_split(ffma2(f32x2(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1])), c2, m2), a0, a1);
+            f32x2_split(ffma2(f32x2(__uint_as_float(y[2 * e]), __uint_as_float(y[2 * e + 1])), c2, m2), b0, b1);
+            if constexpr (VIS) {
+                a0 = (va >> (2 * e)) & 1u ? a0 : -INFINITY;
+                a1 = (va >> (2 * e + 1)) & 1u ? a1 : -INFINITY;
+                b0 = (vb >> (2 * e)) & 1u ? b0 : -INFINITY;
+                b1 = (vb >> (2 * e + 1)) & 1u ? b1 : -INFINITY;
+            }
+            pk[e]  = ex2_f16x2(cvt_f16x2(a0, a1));
+            pk2[e] = ex2_f16x2(cvt_f16x2(b0, b1));
+            if (e < 4) {
+                ha[e] = pk[e];
+                hb[e] = pk2[e];
+            } else {
+                ha[e & 3] = hadd2_u(ha[e & 3], pk[e]);
+                hb[e & 3] = hadd2_u(hb[e & 3], pk2[e]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half2 s2 = __hadd2(*reinterpret_cast<const __half2 *>(&ha[k]),
+                                       *reinterpret_cast<const __half2 *>(&hb[k]));
+            const float2  f  = __half22float2(s2);
+            ls[k] += f.x + f.y;
+        }
+        tmem_st16(tS + 16 * ch, pk);
+        tmem_st16(tS + 16 * ch + 16, pk2);
+    }
+}
+
+// Steady-state fast tile: P = exp2(s * c - m) for all 128 keys into pk (f16
+// pairs, not yet stored), row sums into ls, and the raw (unscaled) max of the
+// visible scores returned, all from one read of S.
+template <bool VIS>
+__device__ __forceinline__ float exp_tile_regs(uint32_t tS, const uint32_t (&vis)[4], float c, float m,
+                                               float (&ls)[4], uint32_t (&pk)[64]) {
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int ch = 0; ch < 4; ch += 2) {
+        uint32_t x[32], y[32];
+        tmem_ld32(tS + 32 * ch, x);
+        tmem_ld32(tS + 32 * ch + 32, y);
+        tmem_ld_wait32(x);
+        tmem_ld_wait32(y);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            float a0 = __uint_as_float(x[2 * e]), a1 = __uint_as_float(x[2 * e + 1]);
+            float b0 = __uint_as_float(y[2 * e]), b1 = __uint_as_float(y[2 * e + 1]);
+            if constexpr (VIS) {
+                a0 = (vis[ch] >> (2 * e)) & 1u ? a0 : -INFINITY;
+                a1 = (vis[ch] >> (2 * e + 1)) & 1u ? a1 : -INFINITY;
+                b0 = (vis[ch + 1] >> (2 * e)) & 1u ? b0 : -INFINITY;
+                b1 = (vis[ch + 1] >> (2 * e + 1)) & 1u ? b1 : -INFINITY;
+            }
+            mx[0] = fmax3(mx[0], a0, a1);
+            mx[1] = fmax3(mx[1], b0, b1);
+            const float p0 = fast_exp2(fmaf(a0, c, -m)), p1 = fast_exp2(fmaf(a1, c, -m));
+            const float q0 = fast_exp2(fmaf(b0, c, -m)), q1 = fast_exp2(fmaf(b1, c, -m));
+            ls[e & 3] += (p0 + p1) + (q0 + q1);
+            pk[16 * ch + e]      = pack2<false>(p0, p1);
+            pk[16 * ch + 16 + e] = pack2<false>(q0, q1);
+        }
+    }
+    return fmaxf(mx[0], mx[1]);
 }
 
 // P = exp2(x * mul - m) as f16 pairs written over the first 64 S columns;
@@ -360,37 +450,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_f16(128, 128, false, false, false);
             constexpr uint32_t idO = umma_idesc_f16(128, 128, false, true, false);
-            const uint32_t     q_s[2] = {smem_u32(smem + kOffQ), smem_u32(smem + kOffQ + kQBytes)};
-            const uint32_t     ring   = smem_u32(smem + kOffRing);
-            const uint32_t     tO[2]  = {tmem + 0, tmem + 128};
-            const uint32_t     tS[2]  = {tmem + 256, tmem + 384};
-            uint32_t           p_ph[2] = {0, 0};
-            uint32_t           has_o[2] = {0, 0};
-            bool               ok = true;
+            // Base descriptors, built once.  Advancing a descriptor is a 64-bit add
+            // to its start-address field (16-B units): k-step ks of a K-major
+            // operand sits at (ks/4)*16 KB + (ks%4)*32 B; of the MN-major V at
+            // ks*16 keys*128 B; ring slot s at s*32 KB.
+            const uint64_t qd0   = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+            const uint64_t qd1   = umma_desc_sw128(smem_u32(smem + kOffQ + kQBytes), 16, 1024);
+            const uint64_t kd0   = umma_desc_sw128(smem_u32(smem + kOffRing), 16, 1024);
+            const uint64_t vd0   = umma_desc_sw128(smem_u32(smem + kOffRing), kDenseBN * 128, 1024);
+            const uint32_t tO0   = tmem + 0, tO1 = tmem + 128, tS0 = tmem + 256, tS1 = tmem + 384;
+            uint32_t       p_ph0 = 0, p_ph1 = 0, has_o0 = 0, has_o1 = 0;
+            bool           ok    = true;
 
             auto wait_full = [&](int seq) -> bool {
                 return mbar_wait_bounded(&full[seq % kRing], (uint32_t) ((seq / kRing) & 1), abort_f, P.dev_err,
                                          DEVERR_TIMEOUT_FULL, P.wait_limit_ns);
             };
-            auto issue_s = [&](int i, int kbuf) {
-                const uint32_t kb = ring + kbuf * kTileBytes;
+            auto issue_s = [&](uint32_t tS, uint64_t qd, int slot) {
+                const uint64_t kd = kd0 + (uint64_t) (slot * (kTileBytes >> 4));
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
-                    const uint32_t off = (ks >> 2) * (kDenseBM * 128) + (ks & 3) * 32;
-                    umma_ss(tS[i], umma_desc_sw128(q_s[i] + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024), idS,
-                            ks > 0 ? 1u : 0u);
+                    const uint64_t off = (uint64_t) ((ks >> 2) * (kDenseBM * 128 >> 4) + (ks & 3) * 2);
+                    umma_ss(tS, qd + off, kd + off, idS, ks > 0 ? 1u : 0u);
                 }
-                tc_commit(&s_ready[i]);
             };
-            auto issue_pv = [&](int i, int vbuf) {
-                const uint32_t vb = ring + vbuf * kTileBytes;
+            auto issue_pv = [&](uint32_t tO, uint32_t tS, int slot, uint32_t acc) {
+                const uint64_t vd = vd0 + (uint64_t) (slot * (kTileBytes >> 4));
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
-                    umma_ts(tO[i], tS[i] + ks * 8, umma_desc_sw128(vb + ks * 2048, kDenseBN * 128, 1024), idO,
-                            (ks > 0 || has_o[i]) ? 1u : 0u);
+                    umma_ts(tO, tS + ks * 8, vd + (uint64_t) (ks * (16 * 128 >> 4)), idO, (ks > 0 || acc) ? 1u : 0u);
                 }
-                has_o[i] = 1;
-                tc_commit(&o_done[i]);
             };
             auto next_live = [&](int j) {
                 while (j < P.n_kt && !any_live(j)) {
@@ -405,57 +494,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = wait_full(2 * use);
                 if (ok) {
                     tc_fence_after();
-                    for (int i = 0; i < 2; ++i) {
-                        if (live_of(i, j)) {
-                            issue_s(i, (2 * use) % kRing);
-                        }
+                    const int ks0 = (2 * use) % kRing;
+                    if (live_of(0, j)) {
+                        issue_s(tS0, qd0, ks0);
+                        tc_commit(&s_ready[0]);
                     }
-                    tc_commit(&empty[(2 * use) % kRing]);
+                    if (live_of(1, j)) {
+                        issue_s(tS1, qd1, ks0);
+                        tc_commit(&s_ready[1]);
+                    }
+                    tc_commit(&empty[ks0]);
                 }
             }
             while (ok && j < P.n_kt) {
-                const int jn   = next_live(j + 1);
-                const int vseq = 2 * use + 1;
-                ok             = wait_full(vseq);
+                const int  jn    = next_live(j + 1);
+                const bool nxt   = jn < P.n_kt;
+                const int  vslot = (2 * use + 1) % kRing;
+                const int  kslot = (2 * (use + 1)) % kRing;
+                const bool l0 = live_of(0, j), l1 = live_of(1, j);
+                const bool n0 = nxt && live_of(0, jn), n1 = nxt && live_of(1, jn);
+                ok = wait_full(2 * use + 1);
                 if (!ok) {
                     break;
                 }
                 tc_fence_after();
-                const bool nxt = jn < P.n_kt;
-                const int  kseq = 2 * (use + 1);
-                bool       kready = false;
-                for (int i = 0; i < 2 && ok; ++i) {
-                    if (live_of(i, j)) {
-                        ok = mbar_wait_bounded(&p_ready[i], p_ph[i], abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
-                                               P.wait_limit_ns);
+                bool kready = false;
+                // row tile 0: O0 += P0 V_j, then S0 = Q0 K_jn
+                if (l0) {
+                    ok = mbar_wait_bounded(&p_ready[0], p_ph0, abort_f, P.dev_err, DEVERR_TIMEOUT_MMA, P.wait_limit_ns);
+                    if (!ok) {
+                        break;
+                    }
+                    p_ph0 ^= 1u;
+                    tc_fence_after();
+                    issue_pv(tO0, tS0, vslot, has_o0);
+                    has_o0 = 1;
+                    tc_commit(&o_done[0]);
+                }
+                if (n0) {
+                    ok = wait_full(2 * (use + 1));
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+                    kready = true;
+                    issue_s(tS0, qd0, kslot);
+                    tc_commit(&s_ready[0]);
+                }
+                // row tile 1
+                if (l1) {
+                    ok = mbar_wait_bounded(&p_ready[1], p_ph1, abort_f, P.dev_err, DEVERR_TIMEOUT_MMA, P.wait_limit_ns);
+                    if (!ok) {
+                        break;
+                    }
+                    p_ph1 ^= 1u;
+                    tc_fence_after();
+                    issue_pv(tO1, tS1, vslot, has_o1);
+                    has_o1 = 1;
+                    tc_commit(&o_done[1]);
+                }
+                tc_commit(&empty[vslot]);
+                if (nxt) {
+                    if (!kready) {
+                        ok = wait_full(2 * (use + 1));
                         if (!ok) {
                             break;
                         }
-                        p_ph[i] ^= 1u;
                         tc_fence_after();
-                        issue_pv(i, vseq % kRing);
                     }
-                    if (nxt && live_of(i, jn)) {
-                        if (!kready) {
-                            ok = wait_full(kseq);
-                            if (!ok) {
-                                break;
-                            }
-                            tc_fence_after();
-                            kready = true;
-                        }
-                        issue_s(i, kseq % kRing);
+                    if (n1) {
+                        issue_s(tS1, qd1, kslot);
+                        tc_commit(&s_ready[1]);
                     }
-                }
-                if (!ok) {
-                    break;
-                }
-                tc_commit(&empty[vseq % kRing]);
-                if (nxt) {
-                    if (!kready) {  // neither tile needs jn's K here: never happens (jn is live)
-                        ok = wait_full(kseq);
-                    }
-                    tc_commit(&empty[kseq % kRing]);
+                    tc_commit(&empty[kslot]);
                 }
                 ++use;
                 j = jn;
@@ -502,20 +613,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         int         cnt   = 0;
         bool        ok    = true;
 
-        // Waits for the previous PV (O and the P columns are then free), folds
-        // the tile max into the running max and rescales O and l when it grew
-        // by more than 2^8.  tcgen05.ld/st are warp-collective, so the whole warp
+        // Folds the tile max into the running max and rescales O and l when it
+        // grew by more than 2^8.  tcgen05.ld/st are warp-collective, so the whole warp
         // walks O when any of its rows needs it (the others multiply by 1).
+        // (No wait for the previous PV here: S of this tile was issued after it,
+        // and the s_ready commit only fires once every earlier MMA is done.)
         auto update_max = [&](float tmax) -> bool {
-            if (cnt > 0) {
-                ok = mbar_wait_bounded(&o_done[i], (uint32_t) ((cnt - 1) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
-                                       P.wait_limit_ns);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) {
-                    return false;
-                }
-                tc_fence_after();
-            }
             const float m_new = fmaxf(m_run, tmax);
             const bool  need  = m_run != -INFINITY && m_new > m_run + kRescaleLog2;
             float       f     = 1.0f;
@@ -568,16 +671,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (use_vis) {
                     build_visibility(vis, c, mrow, j0, o.n_kv, o.m_ne0);
                 }
-                const float tmax = (use_vis ? pass1_max<true>(tS, vis) : pass1_max<false>(tS, vis)) * scale_log2;
-                if (!update_max(tmax)) {
-                    break;
-                }
-                const float m_use = m_run == -INFINITY ? 0.0f : m_run;
-                float       ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                if (use_vis) {
-                    pass2_exp<true>(tS, vis, scale_log2, m_use, ls);
+                float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (__any_sync(0xffffffffu, m_run == -INFINITY)) {
+                    // some row has no max yet: classic max pass first
+                    const float tmax =
+                        (use_vis ? pass1_max<true>(tS, vis) : pass1_max<false>(tS, vis)) * scale_log2;
+                    update_max(tmax);
+                    const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+                    if (use_vis) {
+                        pass2_exp_packed<true>(tS, vis, scale_log2, m_use, ls);
+                    } else {
+                        pass2_exp_packed<false>(tS, vis, scale_log2, m_use, ls);
+                    }
                 } else {
-                    pass2_exp<false>(tS, vis, scale_log2, m_use, ls);
+                    // Steady state: exponentiate against the running max while
+                    // finding the tile max; P stays in registers until the max is
+                    // known to have grown by at most 2^8 (else redo with the new max).
+                    uint32_t    pk[64];
+                    const float tmax =
+                        (use_vis ? exp_tile_regs<true>(tS, vis, scale_log2, m_run, ls, pk)
+                                 : exp_tile_regs<false>(tS, vis, scale_log2, m_run, ls, pk)) *
+                        scale_log2;
+                    if (__any_sync(0xffffffffu, tmax > m_run + kRescaleLog2)) {
+                        update_max(tmax);
+                        ls[0] = ls[1] = ls[2] = ls[3] = 0.0f;
+                        if (use_vis) {
+                            exp_tile_regs<true>(tS, vis, scale_log2, m_run, ls, pk);
+                        } else {
+                            exp_tile_regs<false>(tS, vis, scale_log2, m_run, ls, pk);
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t part[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            part[e] = pk[16 * q + e];
+                        }
+                        tmem_st16(tS + 16 * q, part);
+                    }
                 }
                 l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             } else {
