@@ -42,7 +42,14 @@ EXPORTED_SYMBOLS = (
     "acefa_last_path",
     "acefa_version",
     "acefa_flash_attn_ext_noalloc",
+    "acefa_flash_attn_ext_mirrored",
+    "acefa_peer_export",
+    "acefa_peer_import",
+    "acefa_peer_release",
 )
+
+MAX_MIRRORS = 7
+PEER_HANDLE_BYTES = 64
 
 
 class AcefaError(RuntimeError):
@@ -94,6 +101,16 @@ def load_library(path: str | None = None):
     lib.acefa_flash_attn_ext_noalloc.argtypes = [T, T, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_int, ctypes.c_void_p]
     lib.acefa_flash_attn_ext_noalloc.restype = ctypes.c_int
+    lib.acefa_flash_attn_ext_mirrored.argtypes = [T, T, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                                  ctypes.c_int, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+    lib.acefa_flash_attn_ext_mirrored.restype = ctypes.c_int
+    lib.acefa_peer_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
+    lib.acefa_peer_export.restype = ctypes.c_int
+    lib.acefa_peer_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
+    lib.acefa_peer_import.restype = ctypes.c_int
+    lib.acefa_peer_release.argtypes = [ctypes.c_void_p]
+    lib.acefa_peer_release.restype = ctypes.c_int
     if path is None:
         _lib = lib
     return lib
@@ -158,7 +175,7 @@ class Op:
     """One ggml_flash_attn_ext node's operands, described once, callable many times."""
 
     def __init__(self, q, k, v, mask=None, sinks=None, out=None, kv_type=None, scale=None,
-                 max_bias=0.0, softcap=0.0, prec=PREC_F32):
+                 max_bias=0.0, softcap=0.0, prec=PREC_F32, mirrors=()):
         self.lib = load_library()
         self.q, self.k, self.v, self.mask, self.sinks = q, k, v, mask, sinks
         D = q.shape[-1]
@@ -181,8 +198,20 @@ class Op:
         self.ws_bytes = int(self.lib.acefa_workspace_bytes(_ref(self.tq), _ref(self.tk), _ref(self.tv),
                                                            _ref(self.tm), _ref(self.td)))
         self.workspace = torch.empty(max(self.ws_bytes, 256), dtype=torch.uint8, device=q.device)
+        # mirrors: device addresses laid out like `out` (e.g. peer GPUs' buffers)
+        self.n_mirrors = len(mirrors)
+        self.mirrors = (ctypes.c_void_p * max(1, self.n_mirrors))(*[int(m) for m in mirrors])
 
     def __call__(self, stream=None):
+        if self.n_mirrors:
+            st = self.lib.acefa_flash_attn_ext_mirrored(
+                _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),
+                self.scale, self.max_bias, self.softcap, self.prec, self.mirrors, self.n_mirrors,
+                ctypes.c_void_p(_stream_ptr(stream)), ctypes.c_void_p(self.workspace.data_ptr()),
+                ctypes.c_size_t(self.workspace.numel()))
+            if st != OK:
+                raise AcefaError(st, "acefa_flash_attn_ext_mirrored")
+            return self.out
         st = self.lib.acefa_flash_attn_ext(
             _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),
             self.scale, self.max_bias, self.softcap, self.prec, ctypes.c_void_p(_stream_ptr(stream)),
@@ -214,6 +243,34 @@ def supports(q, k, v, mask=None, sinks=None, kv_type=None) -> bool:
                                    _ref(describe(mask, GGML_F16) if mask is not None else None),
                                    _ref(describe(sinks.reshape(-1), GGML_F32) if sinks is not None else None),
                                    ctypes.byref(td)))
+
+
+def peer_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """CUDA IPC handle of the allocation holding t, and t's byte offset in it."""
+    lib = load_library()
+    h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    off = ctypes.c_uint64(0)
+    st = lib.acefa_peer_export(ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off))
+    if st != OK:
+        raise AcefaError(st, "acefa_peer_export")
+    return h.raw, int(off.value)
+
+
+def peer_import(handle: bytes, offset: int) -> int:
+    """Map another process's exported buffer; returns its address here."""
+    lib = load_library()
+    p = ctypes.c_void_p(0)
+    st = lib.acefa_peer_import(ctypes.create_string_buffer(handle, PEER_HANDLE_BYTES), ctypes.c_uint64(offset),
+                               ctypes.byref(p))
+    if st != OK:
+        raise AcefaError(st, "acefa_peer_import")
+    return int(p.value)
+
+
+def peer_release(addr: int) -> None:
+    st = load_library().acefa_peer_release(ctypes.c_void_p(addr))
+    if st != OK:
+        raise AcefaError(st, "acefa_peer_release")
 
 
 def device_error(stream=None) -> int:

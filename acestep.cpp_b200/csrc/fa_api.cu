@@ -340,6 +340,15 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
                                    const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst,
                                    float scale, float max_bias, float logit_softcap, int prec, void *stream,
                                    void *workspace, size_t workspace_bytes) {
+    return acefa_flash_attn_ext_mirrored(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0,
+                                         stream, workspace, workspace_bytes);
+}
+
+ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                            const acefa_tensor *mask, const acefa_tensor *sinks,
+                                            const acefa_tensor *dst, float scale, float max_bias,
+                                            float logit_softcap, int prec, void *const *mirrors, int n_mirrors,
+                                            void *stream, void *workspace, size_t workspace_bytes) {
     (void) prec;  // accumulation is F32 for both GGML_PREC_DEFAULT and GGML_PREC_F32
     Checked c = check_operands(q, k, v, mask, sinks, dst);
     if (c.status != ACEFA_OK) {
@@ -348,6 +357,21 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
     if (!std::isfinite(scale) || !std::isfinite(max_bias) || !std::isfinite(logit_softcap) || max_bias < 0.0f) {
         return ACEFA_ERR_SHAPE;
     }
+    if (n_mirrors < 0 || n_mirrors > ACEFA_MAX_MIRRORS || (n_mirrors > 0 && !mirrors)) {
+        return n_mirrors > 0 && !mirrors ? ACEFA_ERR_NULL : ACEFA_ERR_SHAPE;
+    }
+    for (int i = 0; i < n_mirrors; ++i) {
+        if (!mirrors[i]) {
+            return ACEFA_ERR_NULL;
+        }
+        const int64_t delta = static_cast<int64_t>(reinterpret_cast<uintptr_t>(mirrors[i]) -
+                                                   reinterpret_cast<uintptr_t>(dst->data));
+        if (delta % 16 != 0 || delta == 0) {
+            return ACEFA_ERR_LAYOUT;
+        }
+        c.op.mirror_delta[i] = delta;
+    }
+    c.op.n_mirror = n_mirrors;
     DevInfo *di = nullptr;
     int      rc = dev_info(&di);
     if (rc != ACEFA_OK) {

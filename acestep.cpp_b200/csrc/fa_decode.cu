@@ -740,8 +740,15 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                         }
                     }
                     const float out = l == 0.0f ? 0.0f : acc / l;
-                    *reinterpret_cast<float *>(o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 +
-                                               (int64_t) iq * o.d_nb2 + (int64_t) uc.b * o.d_nb3) = out;
+                    char       *dp  = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
+                               (int64_t) uc.b * o.d_nb3;
+                    *reinterpret_cast<float *>(dp) = out;
+                    for (int mi = 0; mi < o.n_mirror; ++mi) {
+                        *reinterpret_cast<float *>(dp + o.mirror_delta[mi]) = out;
+                    }
+                    if (o.n_mirror) {
+                        __threadfence_system();
+                    }
                 } else {
                     if (d == 0) {
                         slot[row]            = mx;
@@ -881,7 +888,14 @@ __global__ void __launch_bounds__(kCombThreads) fa_decode_combine(const __grid_c
     char       *out = o.dst + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 + (int64_t) uc.b * o.d_nb3;
 #pragma unroll
     for (int i = 0; i < DPT; ++i) {
-        *reinterpret_cast<float *>(out + (int64_t) (d0 + i) * o.d_nb0) = acc[i] * inv;
+        char *dp = out + (int64_t) (d0 + i) * o.d_nb0;
+        *reinterpret_cast<float *>(dp) = acc[i] * inv;
+        for (int mi = 0; mi < o.n_mirror; ++mi) {
+            *reinterpret_cast<float *>(dp + o.mirror_delta[mi]) = acc[i] * inv;
+        }
+    }
+    if (o.n_mirror) {
+        __threadfence_system();
     }
 }
 

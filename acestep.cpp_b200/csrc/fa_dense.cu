@@ -797,7 +797,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         float      *orow = vrow ? reinterpret_cast<float *>(o.dst + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
                                                             (int64_t) b * o.d_nb3)
                                 : nullptr;
-        const bool  al16 = (reinterpret_cast<uintptr_t>(orow) & 15u) == 0;
+        // Rows leave through a per-warp staging slab in this row tile's Q
+        // buffer (idle once its last MMA has completed): each lane parks its
+        // row's 32-float chunk, then every store instruction of the warp writes
+        // four rows x 128 B, i.e. whole lines -- for the NVLink stores to the
+        // mirrors as much as for HBM.  16-B chunk j of row r sits at slot
+        // j ^ (r & 7), so both the parking and the read-back are conflict-free.
+        const bool al16 = __all_sync(0xffffffffu, (reinterpret_cast<uintptr_t>(orow) & 15u) == 0);
+        uint8_t   *stage = smem + kOffQ + i * kQBytes + wq * 8192;
+        char      *rowp[8];
+#pragma unroll
+        for (int st = 0; st < 8; ++st) {
+            rowp[st] = reinterpret_cast<char *>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(orow),
+                                                            4 * st + (lane >> 3)));
+        }
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
             uint32_t x[32];
@@ -810,22 +823,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     x[e] = 0u;
                 }
             }
-            if (vrow) {
-                float *op = orow + 32 * ch;
-                if (al16) {
+            if (al16) {
+                __syncwarp();  // the previous chunk's read-back is done
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4) {
-                        *reinterpret_cast<float4 *>(op + e) =
-                            make_float4(__uint_as_float(x[e]) * inv, __uint_as_float(x[e + 1]) * inv,
-                                        __uint_as_float(x[e + 2]) * inv, __uint_as_float(x[e + 3]) * inv);
+                for (int j = 0; j < 8; ++j) {
+                    *reinterpret_cast<float4 *>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_float4(__uint_as_float(x[4 * j]) * inv, __uint_as_float(x[4 * j + 1]) * inv,
+                                    __uint_as_float(x[4 * j + 2]) * inv, __uint_as_float(x[4 * j + 3]) * inv);
+                }
+                __syncwarp();
+                const int c = lane & 7;
+#pragma unroll
+                for (int st = 0; st < 8; ++st) {
+                    const int    rr = 4 * st + (lane >> 3);
+                    const float4 w4 = *reinterpret_cast<const float4 *>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+                    if (rowp[st]) {
+                        char *dp = rowp[st] + 128 * ch + 16 * c;
+                        *reinterpret_cast<float4 *>(dp) = w4;
+                        for (int mi = 0; mi < o.n_mirror; ++mi) {  // peers' outputs (NVLink stores)
+                            *reinterpret_cast<float4 *>(dp + o.mirror_delta[mi]) = w4;
+                        }
                     }
-                } else {
+                }
+            } else if (vrow) {
+                float *op = orow + 32 * ch;
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        op[e] = __uint_as_float(x[e]) * inv;
+                for (int e = 0; e < 32; ++e) {
+                    const float w1 = __uint_as_float(x[e]) * inv;
+                    op[e]          = w1;
+                    for (int mi = 0; mi < o.n_mirror; ++mi) {
+                        *reinterpret_cast<float *>(reinterpret_cast<char *>(op + e) + o.mirror_delta[mi]) = w1;
                     }
                 }
             }
+        }
+        if (o.n_mirror) {
+            __threadfence_system();  // peer stores performed before the kernel retires
         }
     }
 

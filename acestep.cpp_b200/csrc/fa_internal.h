@@ -30,6 +30,10 @@ struct OpDesc {
     // dst [D, Hq, n_q, B] f32
     char   *dst;
     int64_t d_nb0, d_nb1, d_nb2, d_nb3;
+    // Mirrors: the same output also stored at dst + mirror_delta[i] (peer GPUs'
+    // buffers mapped into this address space; plain stores over NVLink).
+    int     n_mirror;
+    int64_t mirror_delta[ACEFA_MAX_MIRRORS];
     // shapes
     int D, n_q, Hq, B, n_kv, Hkv, Bk;
     int G;    // Hq / Hkv

@@ -178,7 +178,7 @@ def run_reference(args):
                                    "(oracle/fa_oracle.c, ggml-cpu arithmetic) stands in"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -356,13 +356,17 @@ def run_ours(args):
     if rank == 0 and not args.no_extras:
         out["extras"] = extras(device, stream, args)
         out["extras"]["dense"] = dense_extras(device, stream)
+    if world > 1 and not args.no_extras:
+        sharded = sharded_dit(device, stream, world, rank)  # collective: every rank
+        if rank == 0:
+            out["extras"]["dit6000_heads_sharded"] = sharded
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
-        print(json.dumps(out), flush=True)
+        emit(out)
     return 0
 
 
@@ -504,6 +508,55 @@ def dense_extras(device, stream):
     return res
 
 
+def sharded_dit(device, stream, world, rank, iters=10, warmup=3):
+    """BASELINE config 4 (S=6000, B=2, 16 heads) with K/V head groups split over
+    the ranks and one NCCL all-gather of the outputs (strong scaling: the total
+    work is fixed).  Device time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from acefa.dist import MirroredShardedOp, ShardedOp, head_shard
+
+    B, Hq, Hkv, S = 2, 16, 16, 6000
+    g = torch.Generator(device=device).manual_seed(SEED + 11)
+    sh = head_shard(Hq, Hkv, world, rank)
+    hs, hks = sh.hq1 - sh.hq0, sh.hk1 - sh.hk0
+    q = torch.randn(B, hs, S, D, device=device, generator=g)
+    k = torch.randn(B, hks, S, D, device=device, generator=g, dtype=torch.float16)
+    v = torch.randn(B, hks, S, D, device=device, generator=g, dtype=torch.float16)
+    op = ShardedOp(q, k, v, None, world)
+    mop = MirroredShardedOp(q, k, v, None, world)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            op(stream)
+            mop(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev[0].record(stream)
+        for _ in range(iters):
+            op.op(stream)
+        ev[1].record(stream)
+        for _ in range(iters):
+            op(stream)
+        ev[2].record(stream)
+        for _ in range(iters):
+            mop(stream)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([ev[i].elapsed_time(ev[i + 1]) / iters for i in range(3)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    mop.close()
+    flops = 4 * D * S * S * Hq * B
+    tf = lambda ms: round(flops / (ms / 1e3) / 1e12, 1)  # noqa: E731
+    return {"gpus": world, "ms_attention_only": round(float(t[0]), 4),
+            "ms_with_nccl_allgather": round(float(t[1]), 4), "ms_p2p_mirrored": round(float(t[2]), 4),
+            "tflops_total_nccl_allgather": tf(float(t[1])), "tflops_total_p2p_mirrored": tf(float(t[2])),
+            "note": "heads sharded by K/V group; full output on every rank either by NCCL "
+                    "all_gather_into_tensor + permute, or by the kernel storing its rows into every "
+                    "rank's buffer over NVLink (one-element all-reduce as completion barrier)"}
+
+
 def run_dense_workload(args):
     """--workload <dense name>: time one dense op (also the ncu profiling case)."""
     import torch
@@ -512,11 +565,33 @@ def run_dense_workload(args):
     device = torch.device("cuda", 0)
     stream = torch.cuda.Stream(device=device)
     r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup)
-    print(json.dumps({"workload": args.workload, **r}), flush=True)
+    emit({"workload": args.workload, **r})
     return 0
 
 
+_JSON_FD = None
+
+
+def claim_stdout():
+    """Keep stdout for the one JSON line: libraries that print on fd 1 (NCCL's
+    version banner under torchrun, for one) are sent to stderr instead."""
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
+def emit(obj):
+    data = (json.dumps(obj) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 def main():
+    claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

@@ -120,6 +120,43 @@ ACEFA_API int acefa_flash_attn_ext_noalloc(const acefa_tensor *q, const acefa_te
                                            const acefa_tensor *dst, float scale, float max_bias, float logit_softcap,
                                            int prec, void *stream);
 
+/*
+ * Multi-GPU extension; no counterpart in the reference, which runs every module
+ * on one device.  The operator with its result also written to up to
+ * ACEFA_MAX_MIRRORS further buffers ("mirrors"), each laid out exactly like dst
+ * (same ne and nb) at another address: typically this rank's head slice of a
+ * peer GPU's full output, mapped with acefa_peer_import().  The kernels' output
+ * stage stores every row to dst and to each mirror (plain stores, over NVLink
+ * for peer memory), so a head-sharded attention layer assembles its full
+ * output on every GPU with no separate all-gather.  Each mirror must be
+ * congruent to dst modulo 16 bytes.  n_mirrors == 0 is acefa_flash_attn_ext().
+ * The call signals nothing to the peers: before a peer reads its output the
+ * caller orders it after this stream's work (a collective on this stream after
+ * the call, or an IPC event).  Returns ACEFA_ERR_NULL / ACEFA_ERR_LAYOUT for a
+ * NULL or misaligned mirror, ACEFA_ERR_SHAPE for n_mirrors out of range.
+ */
+#define ACEFA_MAX_MIRRORS 7
+ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                            const acefa_tensor *mask, const acefa_tensor *sinks,
+                                            const acefa_tensor *dst, float scale, float max_bias,
+                                            float logit_softcap, int prec, void *const *mirrors, int n_mirrors,
+                                            void *stream, void *workspace, size_t workspace_bytes);
+
+/*
+ * CUDA IPC through the ABI, so a host without CUDA bindings can map peer
+ * buffers.  acefa_peer_export: an opaque handle (ACEFA_PEER_HANDLE_BYTES bytes)
+ * for the allocation holding ptr, plus ptr's byte offset inside it.
+ * acefa_peer_import (another process of the same node, its own device current):
+ * maps that allocation with peer access enabled and returns the address that
+ * corresponds to the exported ptr.  acefa_peer_release: unmaps an address
+ * acefa_peer_import returned.  All three return ACEFA_OK or ACEFA_ERR_CUDA /
+ * ACEFA_ERR_NULL.
+ */
+#define ACEFA_PEER_HANDLE_BYTES 64
+ACEFA_API int acefa_peer_export(const void *ptr, void *handle, uint64_t *offset);
+ACEFA_API int acefa_peer_import(const void *handle, uint64_t offset, void **ptr);
+ACEFA_API int acefa_peer_release(void *ptr);
+
 /* Workspace acefa_flash_attn_ext() needs for these operands on the current device
  * (split-KV partial results, mask tile classes).  A function of shapes, types
  * and the device only -- never of tensor contents -- so it can be sized once

@@ -146,6 +146,34 @@ def test_flash_attn_without_gpu_fails_cleanly(lib):
     assert lib.acefa_workspace_bytes(r(q), r(k), r(v), r(m), r(d)) == 0
 
 
+def test_mirrored_entry_validates_mirrors_before_launch(lib):
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    q, k, v, m, d = _ops()
+    d.data = 4096
+
+    def call(ptrs, n):
+        arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs) if ptrs is not None else None
+        return lib.acefa_flash_attn_ext_mirrored(r(q), r(k), r(v), r(m), None, r(d), 0.088, 0.0, 0.0, 10,
+                                                 arr, n, None, None, 0)
+
+    assert call(None, 1) == -1                   # mirrors NULL
+    assert call([0], 1) == -1                    # a NULL mirror
+    assert call([(1 << 30) + 4100], 1) == -4  # not congruent to dst mod 16
+    assert call([4096], 1) == -4                 # the mirror is dst itself
+    assert call([1 << 30] * 8, 8) == -3          # more than ACEFA_MAX_MIRRORS
+    assert call([1 << 30], -1) == -3
+    # valid mirrors pass validation and fail only at the device step here
+    if not torch.cuda.is_available():
+        assert call([(1 << 30) + 4096, (1 << 31) + 4096], 2) in (-6, -7)
+
+
+def test_peer_entry_points_reject_null(lib):
+    assert lib.acefa_peer_export(None, None, None) == -1
+    assert lib.acefa_peer_import(None, 0, None) == -1
+    assert lib.acefa_peer_release(None) == -1
+    assert lib.acefa_peer_release(ctypes.c_void_p(4096)) == -1  # never imported
+
+
 def test_torch_q8_0_quantiser_bit_exact(oracle_mod):
     x = np.load(os.path.join(ROOT, "tests", "golden", "q8_0_input.npy"))
     want = np.load(os.path.join(ROOT, "tests", "golden", "q8_0_gguf.npy"))
