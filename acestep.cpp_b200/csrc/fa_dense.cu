@@ -41,6 +41,13 @@ constexpr int      kOffMisc    = kOffCls + 2 * kDenseMaxKT;
 constexpr int      kSmemBytes  = kOffMisc + 16 + 1024;
 constexpr uint32_t kTmemCols   = 512;
 constexpr float    kRescaleLog2 = 8.0f;  // O is rescaled only when the max grows by > 2^8
+// Register split between the warpgroups (setmaxnreg): warps 0-3 (TMA, MMA)
+// give registers to the two softmax warpgroups.  The sum must stay within
+// what the block was launched with (384 threads x 168 registers = 64512), or
+// setmaxnreg.inc would wait forever: 128 x 112 + 256 x 192 = 63488.
+constexpr uint32_t kRegsControl = 112;
+constexpr uint32_t kRegsSoftmax = 192;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= 384 * 168, "register split exceeds the launch pool");
 
 
 constexpr uint16_t kHalfNegInf = 0xFC00u;
@@ -216,36 +223,50 @@ __device__ __forceinline__ void pass2_exp_packed(uint32_t tS, const uint32_t (&v
 // Steady-state fast tile: P = exp2(s * c - m) for all 128 keys into pk (f16
 // pairs, not yet stored), row sums into ls, and the raw (unscaled) max of the
 // visible scores returned, all from one read of S.
+// 64 scores (two 32-column chunks) against the running max m: P into
+// pk[0..31] (f16 pairs, chunk x then chunk y), raw maxima into mx, sums into ls.
+template <bool VIS>
+__device__ __forceinline__ void exp_pair(const uint32_t (&x)[32], const uint32_t (&y)[32], uint32_t vx,
+                                         uint32_t vy, float c, float m, float (&mx)[2], float (&ls)[4],
+                                         uint32_t *pk) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        float a0 = __uint_as_float(x[2 * e]), a1 = __uint_as_float(x[2 * e + 1]);
+        float b0 = __uint_as_float(y[2 * e]), b1 = __uint_as_float(y[2 * e + 1]);
+        if constexpr (VIS) {
+            a0 = (vx >> (2 * e)) & 1u ? a0 : -INFINITY;
+            a1 = (vx >> (2 * e + 1)) & 1u ? a1 : -INFINITY;
+            b0 = (vy >> (2 * e)) & 1u ? b0 : -INFINITY;
+            b1 = (vy >> (2 * e + 1)) & 1u ? b1 : -INFINITY;
+        }
+        mx[0] = fmax3(mx[0], a0, a1);
+        mx[1] = fmax3(mx[1], b0, b1);
+        const float p0 = fast_exp2(fmaf(a0, c, -m)), p1 = fast_exp2(fmaf(a1, c, -m));
+        const float q0 = fast_exp2(fmaf(b0, c, -m)), q1 = fast_exp2(fmaf(b1, c, -m));
+        ls[e & 3] += (p0 + p1) + (q0 + q1);
+        pk[e]      = pack2<false>(p0, p1);
+        pk[16 + e] = pack2<false>(q0, q1);
+    }
+}
+
+// One tile row against the running max: the second half's TMEM loads are
+// issued before the first half is exponentiated, so their latency hides
+// behind it.  P stays in registers (pk) and the raw tile max is returned.
 template <bool VIS>
 __device__ __forceinline__ float exp_tile_regs(uint32_t tS, const uint32_t (&vis)[4], float c, float m,
                                                float (&ls)[4], uint32_t (&pk)[64]) {
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int ch = 0; ch < 4; ch += 2) {
-        uint32_t x[32], y[32];
-        tmem_ld32(tS + 32 * ch, x);
-        tmem_ld32(tS + 32 * ch + 32, y);
-        tmem_ld_wait32(x);
-        tmem_ld_wait32(y);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            float a0 = __uint_as_float(x[2 * e]), a1 = __uint_as_float(x[2 * e + 1]);
-            float b0 = __uint_as_float(y[2 * e]), b1 = __uint_as_float(y[2 * e + 1]);
-            if constexpr (VIS) {
-                a0 = (vis[ch] >> (2 * e)) & 1u ? a0 : -INFINITY;
-                a1 = (vis[ch] >> (2 * e + 1)) & 1u ? a1 : -INFINITY;
-                b0 = (vis[ch + 1] >> (2 * e)) & 1u ? b0 : -INFINITY;
-                b1 = (vis[ch + 1] >> (2 * e + 1)) & 1u ? b1 : -INFINITY;
-            }
-            mx[0] = fmax3(mx[0], a0, a1);
-            mx[1] = fmax3(mx[1], b0, b1);
-            const float p0 = fast_exp2(fmaf(a0, c, -m)), p1 = fast_exp2(fmaf(a1, c, -m));
-            const float q0 = fast_exp2(fmaf(b0, c, -m)), q1 = fast_exp2(fmaf(b1, c, -m));
-            ls[e & 3] += (p0 + p1) + (q0 + q1);
-            pk[16 * ch + e]      = pack2<false>(p0, p1);
-            pk[16 * ch + 16 + e] = pack2<false>(q0, q1);
-        }
-    }
+    float    mx[2] = {-INFINITY, -INFINITY};
+    uint32_t x0[32], x1[32], y0[32], y1[32];
+    tmem_ld32(tS, x0);
+    tmem_ld32(tS + 32, x1);
+    tmem_ld_wait32(x0);
+    tmem_ld_wait32(x1);
+    tmem_ld32(tS + 64, y0);
+    tmem_ld32(tS + 96, y1);
+    exp_pair<VIS>(x0, x1, vis[0], vis[1], c, m, mx, ls, pk);
+    tmem_ld_wait32(y0);
+    tmem_ld_wait32(y1);
+    exp_pair<VIS>(y0, y1, vis[2], vis[3], c, m, mx, ls, pk + 32);
     return fmaxf(mx[0], mx[1]);
 }
 
@@ -399,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };
 
     if (warp < 4) {
+      setmaxnreg_dec<kRegsControl>();
       if (warp == 0) {
         // ============================ TMA producer ============================
         if (lane == 0) {
@@ -584,6 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
         // ============================ softmax =================================
+        setmaxnreg_inc<kRegsSoftmax>();
         // warps 4-7 own row tile 0 and warps 8-11 row tile 1; a warp may only
         // touch TMEM lanes 32*(warp%4) .. +31
         const int      i     = (warp - 4) >> 2;  // row tile

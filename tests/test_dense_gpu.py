@@ -102,6 +102,25 @@ def test_ragged_shapes(n_q, n_kv):
     run_case(c)
 
 
+@pytest.mark.parametrize("lo,hi,scale", [(0.05, 1.0, 0.3), (1.0, 3.0, 0.5)])
+def test_running_max_jumps_inside_tiles(lo, hi, scale):
+    """Scores whose maximum jumps by more than 2^8 (log2 units) from the first
+    64-key half of a tile to the second, in nearly every row: the first half's
+    stored P, the row sum and O must all be rescaled.  Q is made exactly
+    representable in f16 so that the check isolates the softmax rescaling
+    from the Q -> f16 operand rounding, whose error grows with the score
+    magnitude (up to ~100 log2 units here) for every F16 K/V implementation."""
+    c = Case(61, B=1, Hq=8, Hkv=8, n_q=300, n_kv=700, mask=None)
+    c.q_cpu = c.q_cpu.half().float()
+    k = c.k_cache_cpu.float()
+    j = torch.arange(k.shape[2])
+    k[:, :, (j % 128) < 64] *= lo
+    k[:, :, (j % 128) >= 64] *= hi
+    c.k_cache_cpu = k.half()
+    c.to("cuda")
+    run_case(c, scale=scale)
+
+
 def test_sinks_softcap_alibi_dense():
     c = Case(4500, B=2, Hq=8, Hkv=4, n_q=200, n_kv=300, mask="random", sinks=True)
     run_case(c, max_bias=8.0, softcap=20.0)
