@@ -5,6 +5,7 @@
 // (supports_op check, then ggml_cuda_flash_attn_ext(ctx, dst) reading
 // dst->src[0..4] and dst->op_params {scale, max_bias, logit_softcap}) without any
 // ggml type in the signature.  Status codes replace ggml's GGML_ABORT.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -265,20 +266,44 @@ bool use_dense(const OpDesc &o) {
 
 struct DensePlan {
     int    rows_total, n_rt, n_pairs, n_kt;
+    int    n_full, n_tail, n_split;
     bool   classify;
+    size_t cls_bytes;  // class table at the start of the workspace (256-B aligned)
     size_t ws_bytes;
 };
 
-DensePlan plan_dense(const OpDesc &o) {
+// One CTA per SM at a time.  If the units do not fill the last wave, the
+// leftover units are cut into key ranges so that the last wave keeps nearly
+// every SM busy: only for unmasked nodes (every unit the same work; with a
+// causal mask the heavy-first order already packs the last wave) and only
+// when each range keeps at least 16 key tiles, so that a range outweighs its
+// fixed cost (Q conversion, partial write, merge).  At most 8 ranges.  A
+// function of shapes and the SM count only.
+DensePlan plan_dense(const OpDesc &o, int sm_count) {
     DensePlan p;
     p.rows_total = o.G * o.n_q;
     p.n_rt       = (p.rows_total + kDenseBM - 1) / kDenseBM;
     p.n_pairs    = (p.n_rt + 1) / 2;
     p.n_kt       = (o.n_kv + kDenseBN - 1) / kDenseBN;
     // per-tile classes need one mask row per query: a mask shared by all heads
-    p.classify = o.mask != nullptr && o.m_ne2 == 1;
-    size_t b   = p.classify ? (size_t) o.m_ne3 * p.n_rt * p.n_kt : 0;
-    p.ws_bytes = (b + 255) / 256 * 256;
+    p.classify          = o.mask != nullptr && o.m_ne2 == 1;
+    const int64_t units = (int64_t) p.n_pairs * o.B * o.Hkv;
+    const int64_t sms   = sm_count > 0 ? sm_count : 1;
+    const int64_t tail  = units % sms;
+    int64_t       split = 1;
+    if (o.mask == nullptr && units >= sms && tail > 0 && tail <= sms / 2) {
+        split = std::min<int64_t>(std::min<int64_t>(sms / tail, kDenseMaxSplit), p.n_kt / 16);
+        if (split < 2) {
+            split = 1;
+        }
+    }
+    p.n_split     = (int) split;
+    p.n_tail      = split > 1 ? (int) tail : 0;
+    p.n_full      = (int) (units - p.n_tail);
+    size_t b      = p.classify ? (size_t) o.m_ne3 * p.n_rt * p.n_kt : 0;
+    p.cls_bytes   = (b + 255) / 256 * 256;
+    size_t part   = (size_t) p.n_tail * p.n_split * 2 * dense_part_floats() * sizeof(float);
+    p.ws_bytes    = p.cls_bytes + part;
     if (p.ws_bytes == 0) {
         p.ws_bytes = 256;
     }
@@ -331,7 +356,7 @@ ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor
         return 0;
     }
     if (use_dense(c.op)) {
-        return plan_dense(c.op).ws_bytes;
+        return plan_dense(c.op, di->sm_count).ws_bytes;
     }
     return plan_decode(c.op, di->sm_count).ws_bytes;
 }
@@ -381,7 +406,7 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
     if (use_dense(c.op)) {
-        const DensePlan dp = plan_dense(c.op);
+        const DensePlan dp = plan_dense(c.op, di->sm_count);
         if (workspace_bytes < dp.ws_bytes || !workspace || !aligned(workspace, 256)) {
             return ACEFA_ERR_WORKSPACE;
         }
@@ -392,8 +417,13 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
         L.p.n_rt          = dp.n_rt;
         L.p.n_pairs       = dp.n_pairs;
         L.p.n_kt          = dp.n_kt;
+        L.p.n_full        = dp.n_full;
+        L.p.n_tail        = dp.n_tail;
+        L.p.n_split       = dp.n_split;
         L.p.cls           = dp.classify ? static_cast<const uint8_t *>(workspace) : nullptr;
         L.p.cls_out       = dp.classify ? static_cast<uint8_t *>(workspace) : nullptr;
+        L.p.part          = dp.n_tail ? reinterpret_cast<float *>(static_cast<char *>(workspace) + dp.cls_bytes)
+                                      : nullptr;
         L.p.dev_err       = di->err_ptr;
         L.p.wait_limit_ns = wait_limit_ns();
         L.classify        = dp.classify;

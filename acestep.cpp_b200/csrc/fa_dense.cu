@@ -18,7 +18,9 @@
 //               moves (and rescales O in TMEM) when it grows by more than 2^8,
 //               and writes P as f16 over the S columns it just read.
 // The two row tiles ping-pong: while one warpgroup exponentiates, the tensor
-// core runs the other tile's PV and next S.  A pre-pass classifies each
+// core runs the other tile's PV and next S.  When the work units leave the
+// last wave mostly idle, the leftover units are cut into key ranges whose
+// partial results fa_dense_combine merges.  A pre-pass classifies each
 // (row tile, key tile) of the mask as dead / all-zero / mixed so that causal
 // and window masks never load or multiply their dead tiles.
 // Every wait is bounded (error word + drain on expiry).
@@ -335,12 +337,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const OpDesc &o    = P.op;
     const int     warp = threadIdx.x >> 5;
     const int     lane = threadIdx.x & 31;
-    // 1-D grid, pair index slowest and descending: every (batch, head) unit's
-    // late (for causal masks, heaviest) row tiles are scheduled first
-    const int     units = o.B * o.Hkv;
-    const int     pair  = P.n_pairs - 1 - (int) (blockIdx.x / units);
-    const int     hk    = (int) (blockIdx.x % units) % o.Hkv;
-    const int     b     = (int) (blockIdx.x % units) / o.Hkv;
+    // 1-D grid of work units, pair index slowest and descending: every (batch,
+    // head) unit's late (for causal masks, heaviest) row tiles are scheduled
+    // first.  CTAs past n_full each take one key range of a split unit.
+    const int     units   = o.B * o.Hkv;
+    const bool    is_part = (int) blockIdx.x >= P.n_full;
+    const int     xs      = (int) blockIdx.x - P.n_full;
+    const int     unit_id = is_part ? P.n_full + xs / P.n_split : (int) blockIdx.x;
+    const int     sp      = is_part ? xs % P.n_split : 0;
+    const int     kt_lo   = is_part ? (int) ((int64_t) P.n_kt * sp / P.n_split) : 0;
+    const int     kt_hi   = is_part ? (int) ((int64_t) P.n_kt * (sp + 1) / P.n_split) : P.n_kt;
+    const int     pair    = P.n_pairs - 1 - unit_id / units;
+    const int     hk      = (unit_id % units) % o.Hkv;
+    const int     b       = (unit_id % units) / o.Hkv;
     const int     bk   = b / o.rk3;
     const int     t0   = 2 * pair;
     const bool    has_tile[2] = {t0 < P.n_rt, t0 + 1 < P.n_rt};
@@ -373,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = threadIdx.x; j < P.n_kt; j += kThreads) {
         for (int i = 0; i < 2; ++i) {
             uint8_t c = 0;
-            if (has_tile[i]) {
+            if (has_tile[i] && j >= kt_lo && j < kt_hi) {
                 if (P.cls) {
                     c = P.cls[((int64_t) (b % o.m_ne3) * P.n_rt + t0 + i) * P.n_kt + j];
                 } else {
@@ -387,28 +396,89 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
-    // ---- Q: f32 rows -> f16, 128-B swizzled K-major tiles [128 rows][2 x 64 dims]
-    for (int rr = warp; rr < 2 * kDenseBM; rr += kThreads / 32) {
-        const int i  = rr / kDenseBM;
-        const int r  = rr % kDenseBM;
-        const int gr = (t0 + i) * kDenseBM + r;
-        float4    v  = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has_tile[i] && gr < P.rows_total) {
-            int iq, hq;
-            row_to_query(gr, o.G, hk, iq, hq);
-            const char *qrow = o.q + (int64_t) iq * o.q_nb1 + (int64_t) hq * o.q_nb2 + (int64_t) b * o.q_nb3;
-            const float *qf  = reinterpret_cast<const float *>(qrow) + 4 * lane;
-            if ((reinterpret_cast<uintptr_t>(qf) & 15u) == 0) {
-                v = __ldg(reinterpret_cast<const float4 *>(qf));
-            } else {
-                v = make_float4(__ldg(qf), __ldg(qf + 1), __ldg(qf + 2), __ldg(qf + 3));
+    __syncthreads();  // barriers initialised, class table complete
+
+    auto live_of  = [&](int i, int j) -> bool { return (s_cls[i * kDenseMaxKT + j] & kClsLive) != 0; };
+    auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };
+
+    // TMA producer state (warp 0, lane 0).  (Issuing its first key steps
+    // before the Q conversion below measured slower: the K/V burst competes
+    // with the Q loads at every wave start.)
+    int  pend[kRing];
+    int  p_j = 0, p_use = 0;
+    bool p_ok = true;
+    auto produce = [&](int max_steps) {
+        for (int n = 0; p_j < P.n_kt && p_ok && n < max_steps; ++p_j) {
+            if (!any_live(p_j)) {
+                continue;
+            }
+            for (int h = 0; h < 2 && p_ok; ++h) {
+                const int seq = 2 * p_use + h;
+                const int buf = seq % kRing;
+                const int u   = seq / kRing;
+                p_ok = mbar_wait_bounded(&empty[buf], (uint32_t) ((u & 1) ^ 1), abort_f, P.dev_err,
+                                         DEVERR_TIMEOUT_EMPTY, P.wait_limit_ns);
+                if (!p_ok) {
+                    break;
+                }
+                uint8_t           *dst = smem + kOffRing + buf * kTileBytes;
+                const CUtensorMap *map = h == 0 ? &kmap : &vmap;
+                mbar_arrive_expect_tx(&full[buf], kTileBytes);
+                tma_load_4d(dst, map, 0, p_j * kDenseBN, hk, bk, &full[buf]);
+                tma_load_4d(dst + kDenseBN * 128, map, 64, p_j * kDenseBN, hk, bk, &full[buf]);
+                pend[buf] = u & 1;
+            }
+            ++p_use;
+            ++n;
+        }
+    };
+    if (warp == 0 && lane == 0) {
+        for (int k = 0; k < kRing; ++k) {
+            pend[k] = -1;
+        }
+    }
+
+    // ---- Q: f32 rows -> f16, 128-B swizzled K-major tiles [2 x 64 dims][128 rows].
+    // 16-B chunks, eight loads in flight per thread before any is converted.
+    {
+        constexpr int kChunks = 2 * kDenseBM * 32;
+        constexpr int kUnroll = 8;
+        for (int base = threadIdx.x; base < kChunks; base += kThreads * kUnroll) {
+            float4 v[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int ch = base + u * kThreads;
+                v[u]         = make_float4(0.f, 0.f, 0.f, 0.f);
+                const int rr = ch >> 5;
+                const int i  = rr / kDenseBM;
+                const int gr = (t0 + i) * kDenseBM + rr % kDenseBM;
+                if (ch < kChunks && has_tile[i] && gr < P.rows_total) {
+                    int iq, hq;
+                    row_to_query(gr, o.G, hk, iq, hq);
+                    const char  *qrow = o.q + (int64_t) iq * o.q_nb1 + (int64_t) hq * o.q_nb2 + (int64_t) b * o.q_nb3;
+                    const float *qf   = reinterpret_cast<const float *>(qrow) + 4 * (ch & 31);
+                    if ((reinterpret_cast<uintptr_t>(qf) & 15u) == 0) {
+                        v[u] = __ldg(reinterpret_cast<const float4 *>(qf));
+                    } else {
+                        v[u] = make_float4(__ldg(qf), __ldg(qf + 1), __ldg(qf + 2), __ldg(qf + 3));
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int ch = base + u * kThreads;
+                if (ch < kChunks) {
+                    const int      rr = ch >> 5;
+                    const int      i  = rr / kDenseBM;
+                    const int      r  = rr % kDenseBM;
+                    const int      d  = 4 * (ch & 31);
+                    const uint32_t lo = pack2<false>(v[u].x, v[u].y), hi = pack2<false>(v[u].z, v[u].w);
+                    uint8_t *dst = smem + kOffQ + i * kQBytes + (d >> 6) * (kDenseBM * 128) + r * 128 +
+                                   ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
+                    *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+                }
             }
         }
-        const uint32_t lo = pack2<false>(v.x, v.y), hi = pack2<false>(v.z, v.w);
-        const int      d  = 4 * lane;
-        uint8_t *dst = smem + kOffQ + i * kQBytes + (d >> 6) * (kDenseBM * 128) + r * 128 +
-                       ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
-        *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
     }
     fence_proxy_async_smem();  // Q is read by the tensor core (async proxy)
     tc_fence_before();
@@ -416,43 +486,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
 
-    auto live_of = [&](int i, int j) -> bool { return (s_cls[i * kDenseMaxKT + j] & kClsLive) != 0; };
-    auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };
-
     if (warp < 4) {
       setmaxnreg_dec<kRegsControl>();
       if (warp == 0) {
         // ============================ TMA producer ============================
         if (lane == 0) {
-            int pend[kRing];
-            for (int i = 0; i < kRing; ++i) {
-                pend[i] = -1;
-            }
-            int  use = 0;
-            bool ok  = true;
-            for (int j = 0; j < P.n_kt && ok; ++j) {
-                if (!any_live(j)) {
-                    continue;
-                }
-                for (int h = 0; h < 2 && ok; ++h) {
-                    const int seq = 2 * use + h;
-                    const int buf = seq % kRing;
-                    const int u   = seq / kRing;
-                    ok = mbar_wait_bounded(&empty[buf], (uint32_t) ((u & 1) ^ 1), abort_f, P.dev_err,
-                                           DEVERR_TIMEOUT_EMPTY, P.wait_limit_ns);
-                    if (!ok) {
-                        break;
-                    }
-                    uint8_t           *dst = smem + kOffRing + buf * kTileBytes;
-                    const CUtensorMap *map = h == 0 ? &kmap : &vmap;
-                    mbar_arrive_expect_tx(&full[buf], kTileBytes);
-                    tma_load_4d(dst, map, 0, j * kDenseBN, hk, bk, &full[buf]);
-                    tma_load_4d(dst + kDenseBN * 128, map, 64, j * kDenseBN, hk, bk, &full[buf]);
-                    pend[buf] = u & 1;
-                }
-                ++use;
-            }
-            if (!ok) {
+            produce(P.n_kt);
+            if (!p_ok) {
                 for (int i = 0; i < kRing; ++i) {
                     if (pend[i] < 0) {
                         continue;
@@ -806,6 +846,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
         }
         ok = __all_sync(0xffffffffu, ok);
+        if (is_part) {
+            // key range of a split unit: unnormalised O, running max and row
+            // sum to this range's slot; fa_dense_combine finishes the rows
+            float *slot = P.part + ((int64_t) ((unit_id - P.n_full) * P.n_split + sp) * 2 + i) * dense_part_floats();
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t xo[32];
+                if (ok && cnt > 0) {
+                    tmem_ld32(tO + 32 * ch, xo);
+                    tmem_ld_wait32(xo);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        xo[e] = 0u;
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    slot[(32 * ch + e) * kDenseBM + r] = __uint_as_float(xo[e]);
+                }
+            }
+            const bool has = ok && cnt > 0;
+            slot[128 * kDenseBM + r]            = has ? m_run : -INFINITY;
+            slot[128 * kDenseBM + kDenseBM + r] = has ? l_run : 0.0f;
+        } else {
         float fs = 1.0f;
         if (o.sinks && vrow) {
             const float ts = o.sinks[hq] * kLog2e;
@@ -883,6 +948,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (o.n_mirror) {
             __threadfence_system();  // peer stores performed before the kernel retires
         }
+        }
     }
 
     tc_fence_before();
@@ -890,6 +956,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Merge of the key ranges of split units: one CTA per (split unit, row tile,
+// 8-dim chunk), one thread per row, every load of the chunk independent.
+// O = sum_k 2^(m_k - M) O_k / (sum_k 2^(m_k - M) l_k [+ sink]).
+constexpr int kCombineDims = 8;
+
+__global__ void __launch_bounds__(kDenseBM) fa_dense_combine(const __grid_constant__ DenseParams P) {
+    const OpDesc &o     = P.op;
+    const int     t     = blockIdx.x;  // split unit
+    const int     i     = blockIdx.y;  // row tile of its pair
+    const int     d0    = blockIdx.z * kCombineDims;
+    const int     r     = threadIdx.x;
+    const int     units = o.B * o.Hkv;
+    const int     unit  = P.n_full + t;
+    const int     pair  = P.n_pairs - 1 - unit / units;
+    const int     hk    = (unit % units) % o.Hkv;
+    const int     b     = (unit % units) / o.Hkv;
+    const int     gr    = (2 * pair + i) * kDenseBM + r;
+    pdl_wait_primary();
+    if (2 * pair + i >= P.n_rt || gr >= P.rows_total) {
+        return;
+    }
+    int iq, hq;
+    row_to_query(gr, o.G, hk, iq, hq);
+    const float *base = P.part + (int64_t) t * P.n_split * 2 * dense_part_floats() + (int64_t) i * dense_part_floats();
+    const int64_t step = 2 * (int64_t) dense_part_floats();  // next key range of the same row tile
+    float         mk[kDenseMaxSplit], lk[kDenseMaxSplit];
+    float         M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kDenseMaxSplit; ++k) {
+        mk[k] = k < P.n_split ? __ldg(base + k * step + 128 * kDenseBM + r) : -INFINITY;
+        lk[k] = k < P.n_split ? __ldg(base + k * step + 128 * kDenseBM + kDenseBM + r) : 0.0f;
+        M     = fmaxf(M, mk[k]);
+    }
+    float L = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kDenseMaxSplit; ++k) {
+        L += mk[k] == -INFINITY ? 0.0f : lk[k] * fast_exp2(mk[k] - M);
+    }
+    float fs = 1.0f;
+    if (o.sinks) {
+        const float ts = o.sinks[hq] * kLog2e;
+        if (ts > M) {
+            fs = M == -INFINITY ? 0.0f : fast_exp2(M - ts);
+            L  = L * fs + 1.0f;
+        } else {
+            L += fast_exp2(ts - M);
+        }
+    }
+    const float inv = L > 0.0f ? fs / L : 0.0f;
+    float       acc[kCombineDims];
+#pragma unroll
+    for (int e = 0; e < kCombineDims; ++e) {
+        acc[e] = 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kDenseMaxSplit; ++k) {
+        if (k < P.n_split && mk[k] != -INFINITY) {
+            const float w = fast_exp2(mk[k] - M) * inv;
+#pragma unroll
+            for (int e = 0; e < kCombineDims; ++e) {
+                acc[e] += __ldg(base + k * step + (int64_t) (d0 + e) * kDenseBM + r) * w;
+            }
+        }
+    }
+    char *orow = o.dst + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 + (int64_t) b * o.d_nb3;
+#pragma unroll
+    for (int e = 0; e < kCombineDims; ++e) {
+        char *dp                        = orow + (int64_t) (d0 + e) * o.d_nb0;
+        *reinterpret_cast<float *>(dp) = acc[e];
+        for (int mi = 0; mi < o.n_mirror; ++mi) {
+            *reinterpret_cast<float *>(dp + o.mirror_delta[mi]) = acc[e];
+        }
+    }
+    if (o.n_mirror) {
+        __threadfence_system();
     }
 }
 
@@ -923,7 +1068,7 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
         ++n;
     }
     cudaLaunchConfig_t c = {};
-    c.gridDim            = dim3((unsigned) ((int64_t) L.p.n_pairs * L.p.op.Hkv * L.p.op.B));
+    c.gridDim            = dim3((unsigned) (L.p.n_full + (int64_t) L.p.n_tail * L.p.n_split));
     c.blockDim           = dim3(kThreads);
     c.dynamicSmemBytes   = kSmemBytes;
     c.stream             = s;
@@ -933,8 +1078,22 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     if (e != cudaSuccess) {
         return e;
     }
+    ++n;
+    if (L.p.n_tail > 0) {
+        cudaLaunchConfig_t cc = {};
+        cc.gridDim            = dim3((unsigned) L.p.n_tail, 2, 128 / kCombineDims);
+        cc.blockDim           = dim3(kDenseBM);
+        cc.stream             = s;
+        cc.attrs              = attr;
+        cc.numAttrs           = 1;
+        e                     = cudaLaunchKernelEx(&cc, fa_dense_combine, L.p);
+        if (e != cudaSuccess) {
+            return e;
+        }
+        ++n;
+    }
     if (launches) {
-        *launches = n + 1;
+        *launches = n;
     }
     return cudaSuccess;
 }

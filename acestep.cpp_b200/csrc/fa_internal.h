@@ -106,17 +106,31 @@ constexpr uint8_t kClsMask   = 2;  // entries other than 0 present: read the mas
 constexpr uint8_t kClsBounds = 4;  // tile runs past n_kv
 constexpr uint8_t kClsBinary = 8;  // every mask entry of the tile is 0 or -inf
 
+// Work units are (row-tile pair, batch, kv head), numbered pair-major from
+// the heaviest pair.  The first n_full units run whole, one CTA each; when the
+// last wave would leave most SMs idle, each of the n_tail remaining units is
+// cut into n_split key ranges run by separate CTAs, which write unnormalised
+// partial results (O, running max, row sum) that fa_dense_combine merges.
 struct DenseParams {
     OpDesc         op;
     int            rows_total;  // G * n_q rows per (b, hk) unit
     int            n_rt;        // 128-row tiles per unit
-    int            n_pairs;     // CTAs per unit
+    int            n_pairs;     // row-tile pairs per unit
     int            n_kt;        // key tiles
+    int            n_full;      // units run whole
+    int            n_tail;      // units split over key ranges
+    int            n_split;     // key ranges per split unit (1 = none)
     const uint8_t *cls;         // [m_ne3][n_rt][n_kt] classes, or nullptr (no per-tile info)
     uint8_t       *cls_out;     // same buffer, written by the classify pre-pass
+    float         *part;        // [n_tail][n_split][2 tiles] partial slots (dense_part_floats each)
     int           *dev_err;
     uint64_t       wait_limit_ns;
 };
+
+constexpr int kDenseMaxSplit = 8;  // key ranges per split unit
+
+// One partial slot: O [128 dims][128 rows] (row fastest), then m[128], l[128].
+constexpr int dense_part_floats() { return 128 * kDenseBM + 2 * kDenseBM; }
 
 struct DenseLaunch {
     DenseParams p;

@@ -121,6 +121,16 @@ def test_running_max_jumps_inside_tiles(lo, hi, scale):
     run_case(c, scale=scale)
 
 
+def test_tail_units_split_over_key_ranges():
+    """160 work units (16 row-tile pairs x 10 heads) on 148 SMs: the 12 of the
+    last wave are each cut into two key ranges of 16 key tiles whose partial
+    results a combine kernel merges, with the sink added once in the merge.
+    The split units are pair 0 (rows 0-255) of every head and pair 1 of two."""
+    c = Case(71, B=1, Hq=10, Hkv=10, n_q=4096, n_kv=4096, mask=None, sinks=True)
+    run_case(c, rows=[0, 1, 77, 128, 255, 256, 300, 511, 2048, 4095])
+    assert acefa.last_launch_count() == 2  # attention, combine
+
+
 def test_sinks_softcap_alibi_dense():
     c = Case(4500, B=2, Hq=8, Hkv=4, n_q=200, n_kv=300, mask="random", sinks=True)
     run_case(c, max_bias=8.0, softcap=20.0)

@@ -5,6 +5,7 @@ dst and to every mirror (bit for bit: the same value goes to every address),
 and dst must meet the parity tolerance like the unmirrored call.  (Two launches
 of the decode kernel can differ in the last bit: its four consumer warps merge
 their partial outputs with shared-memory float atomics in arrival order.)"""
+import numpy as np
 import pytest
 import torch
 
@@ -54,3 +55,17 @@ def test_mirrored_head_slices_assemble_full_output():
     torch.cuda.synchronize()
     for b in bufs:
         assert (b.cpu().numpy() == full).all()
+
+
+def test_mirrored_dense_split_units():
+    """Units split over key ranges: the combine kernel writes the mirrors."""
+    c = Case(34, B=1, Hq=10, Hkv=10, n_q=4096, n_kv=4096, mask=None)
+    out = torch.full((c.B, c.n_q, c.Hq, c.D), float("nan"), device="cuda")
+    mirrors = [torch.full_like(out, float("nan")) for _ in range(2)]
+    acefa.Op(c.q, c.k, c.v, out=out, mirrors=[m.data_ptr() for m in mirrors])()
+    assert acefa.last_launch_count() == 2  # attention, combine
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    for m in mirrors:
+        assert (m.cpu().numpy() == got).all()
