@@ -58,7 +58,8 @@ struct DecCfg {
     static constexpr int kOffStages = 0;
     static constexpr int kOffMerge  = kOffStages + kDecStages * kStageBytes;
     static constexpr int kOffStats  = kOffMerge + kDecRows * kMergeStride * 4;  // m,l per warp per row
-    static constexpr int kOffBars   = kOffStats + 2 * kDecWarps * kDecRows * 4;
+    static constexpr int kOffFin    = kOffStats + 2 * kDecWarps * kDecRows * 4;  // merged m,l per row
+    static constexpr int kOffBars   = kOffFin + 2 * kDecRows * 4;
     static constexpr int kOffMeta   = kOffBars + 2 * kDecStages * 8;
     static constexpr int kOffFlags  = kOffMeta + kDecStages * 16;
     static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
@@ -192,6 +193,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     float        *merge     = reinterpret_cast<float *>(smem + Cfg::kOffMerge);
     float        *s_m       = reinterpret_cast<float *>(smem + Cfg::kOffStats);
     float        *s_l       = s_m + kDecWarps * kDecRows;
+    float        *s_fin     = reinterpret_cast<float *>(smem + Cfg::kOffFin);  // [0,16) max, [16,32) sum
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -203,9 +205,6 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         }
         *abort_f = 0;
         fence_barrier_init();
-    }
-    for (int i = threadIdx.x; i < kDecRows * Cfg::kMergeStride; i += blockDim.x) {
-        merge[i] = 0.0f;
     }
     __syncthreads();
 
@@ -696,70 +695,85 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             }
             fac[i] = m_run[i] == -INFINITY ? 0.0f : fast_exp2(m_run[i] - mx);
         }
+        // The four warps' partial O, rescaled to the common row max, summed in
+        // shared memory one warp at a time (plain stores: each lane owns its
+        // elements within a warp), while threads 0-15 merge the row statistics.
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
+        for (int w = 0; w < kDecWarps; ++w) {
+            if (warp == w) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = g + 8 * (e >> 1);
-                atomicAdd(&merge[row * Cfg::kMergeStride + out_dim(j, e)], oacc[j][e] * fac[e >> 1]);
+                for (int j = 0; j < NT; ++j) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float      *mp = &merge[(g + 8 * (e >> 1)) * Cfg::kMergeStride + out_dim(j, e)];
+                        const float v  = oacc[j][e] * fac[e >> 1];
+                        *mp            = w == 0 ? v : *mp + v;
+                    }
+                }
             }
+            if (w == 0 && threadIdx.x < kDecRows) {
+                const int row = threadIdx.x;
+                float     mx  = -INFINITY;
+#pragma unroll
+                for (int ww = 0; ww < kDecWarps; ++ww) {
+                    mx = fmaxf(mx, s_m[ww * kDecRows + row]);
+                }
+                float l = 0.0f;
+#pragma unroll
+                for (int ww = 0; ww < kDecWarps; ++ww) {
+                    const float mw = s_m[ww * kDecRows + row];
+                    l += mw == -INFINITY ? 0.0f : s_l[ww * kDecRows + row] * fast_exp2(mw - mx);
+                }
+                s_fin[row]            = mx;
+                s_fin[kDecRows + row] = l;
+            }
+            named_bar_sync(1, kDecWarps * 32);
         }
-        named_bar_sync(1, kDecWarps * 32);
         const int64_t cf     = cta_of_tile((int64_t) u * tpu, T, C);
         const int64_t cl     = cta_of_tile((int64_t) (u + 1) * tpu - 1, T, C);
         const bool    direct = cf == cl;
         float        *slot   = P.partials + (int64_t) (blockIdx.x + u) * dec_slot_floats(D);
+        if (!direct && threadIdx.x < kDecRows && threadIdx.x < uc.rows) {
+            slot[threadIdx.x]            = s_fin[threadIdx.x];
+            slot[kDecRows + threadIdx.x] = s_fin[kDecRows + threadIdx.x];
+        }
         for (int idx = threadIdx.x; idx < kDecRows * D; idx += kDecWarps * 32) {
             const int row = idx / D;
             const int d   = idx % D;
-            float    *mp  = &merge[row * Cfg::kMergeStride + d];
-            if (row < uc.rows) {
-                float mx = -INFINITY;
-#pragma unroll
-                for (int w = 0; w < kDecWarps; ++w) {
-                    mx = fmaxf(mx, s_m[w * kDecRows + row]);
-                }
-                float l = 0.0f;
-#pragma unroll
-                for (int w = 0; w < kDecWarps; ++w) {
-                    const float mw = s_m[w * kDecRows + row];
-                    l += mw == -INFINITY ? 0.0f : s_l[w * kDecRows + row] * fast_exp2(mw - mx);
-                }
-                float acc = *mp;
-                if (direct) {
-                    int iq, hq;
-                    row_coord(P, uc, row, iq, hq);
-                    if (o.sinks) {
-                        const float ts = o.sinks[hq] * kLog2e;
-                        if (ts > mx) {
-                            const float f = fast_exp2(mx - ts);
-                            acc *= f;
-                            l = l * f + 1.0f;
-                        } else {
-                            l += fast_exp2(ts - mx);
-                        }
-                    }
-                    const float out = l == 0.0f ? 0.0f : acc / l;
-                    char       *dp  = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
-                               (int64_t) uc.b * o.d_nb3;
-                    *reinterpret_cast<float *>(dp) = out;
-                    for (int mi = 0; mi < o.n_mirror; ++mi) {
-                        *reinterpret_cast<float *>(dp + o.mirror_delta[mi]) = out;
-                    }
-                    if (o.n_mirror) {
-                        __threadfence_system();
-                    }
-                } else {
-                    if (d == 0) {
-                        slot[row]            = mx;
-                        slot[kDecRows + row] = l;
-                    }
-                    slot[2 * kDecRows + row * D + d] = acc;
-                }
+            if (row >= uc.rows) {
+                continue;
             }
-            *mp = 0.0f;
+            float acc = merge[row * Cfg::kMergeStride + d];
+            if (direct) {
+                const float mx = s_fin[row];
+                float       l  = s_fin[kDecRows + row];
+                int         iq, hq;
+                row_coord(P, uc, row, iq, hq);
+                if (o.sinks) {
+                    const float ts = o.sinks[hq] * kLog2e;
+                    if (ts > mx) {
+                        const float f = fast_exp2(mx - ts);
+                        acc *= f;
+                        l = l * f + 1.0f;
+                    } else {
+                        l += fast_exp2(ts - mx);
+                    }
+                }
+                const float out = l == 0.0f ? 0.0f : acc / l;
+                char       *dp  = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
+                           (int64_t) uc.b * o.d_nb3;
+                *reinterpret_cast<float *>(dp) = out;
+                for (int mi = 0; mi < o.n_mirror; ++mi) {
+                    *reinterpret_cast<float *>(dp + o.mirror_delta[mi]) = out;
+                }
+                if (o.n_mirror) {
+                    __threadfence_system();
+                }
+            } else {
+                slot[2 * kDecRows + row * D + d] = acc;
+            }
         }
-        named_bar_sync(1, kDecWarps * 32);
+        named_bar_sync(1, kDecWarps * 32);  // merge and s_fin are free for the next unit
     };
 
     // The first unit is known from the tile range: fetch its Q while the
@@ -838,35 +852,49 @@ __global__ void __launch_bounds__(kCombThreads) fa_decode_combine(const __grid_c
     const bool    active = row < uc.rows;
     const int64_t stride = dec_slot_floats(D);
     const float  *base   = P.partials + (cf + u) * stride;
-    const int     np     = (int) (cl - cf + 1);
+    const int     np     = (int) (cl - cf + 1);  // <= kDecMaxParts + 1
     const int     sub    = threadIdx.x % 16;
-    float         mx     = -INFINITY;
-    for (int p = sub; p < np; p += 16) {  // the row's 16 threads split the parts
-        mx = fmaxf(mx, __ldg(base + p * stride + row));
+    // Thread `sub` of a row reads part sub's max and sum (at most 16 parts), so
+    // the row statistics take one round of loads and two shuffle reductions;
+    // then every part's slice of O is requested before any is summed.
+    float m_p = -INFINITY, l_p = 0.0f;
+    if (sub < np) {
+        m_p = __ldg(base + sub * stride + row);
+        l_p = __ldg(base + sub * stride + kDecRows + row);
     }
+    float mx = m_p;
 #pragma unroll
     for (int off = 8; off > 0; off >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     }
-    float l = 0.0f, acc[DPT];
+    const float f_p = m_p == -INFINITY ? 0.0f : fast_exp2(m_p - mx);
+    float       l   = l_p * f_p;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) {
+        l += __shfl_xor_sync(0xffffffffu, l, off);
+    }
+    float acc[DPT];
 #pragma unroll
     for (int i = 0; i < DPT; ++i) {
         acc[i] = 0.0f;
     }
-#pragma unroll 4
-    for (int p = 0; p < np; ++p) {
-        const float *slot = base + p * stride;
-        const float  mc   = __ldg(slot + row);
-        const float  f    = mc == -INFINITY ? 0.0f : fast_exp2(mc - mx);
-        l += f * __ldg(slot + kDecRows + row);
-        const float4 *op4 = reinterpret_cast<const float4 *>(slot + 2 * kDecRows + row * D + d0);
+    const int grp = (threadIdx.x & 31) & ~15;  // first lane of this row's 16 in the warp
+    // a unit spans at most kDecMaxParts + 1 CTAs (its ends need not align with
+    // theirs): at most 16 parts, one per thread of the row
+    static_assert(kDecMaxParts + 1 <= 16, "one part per thread of a row");
 #pragma unroll
-        for (int i = 0; i < DPT / 4; ++i) {
-            const float4 v = __ldg(op4 + i);
-            acc[4 * i + 0] += f * v.x;
-            acc[4 * i + 1] += f * v.y;
-            acc[4 * i + 2] += f * v.z;
-            acc[4 * i + 3] += f * v.w;
+    for (int p = 0; p < 16; ++p) {
+        if (p < np) {  // uniform over the CTA
+            const float   f   = __shfl_sync(0xffffffffu, f_p, grp + p);
+            const float4 *op4 = reinterpret_cast<const float4 *>(base + p * stride + 2 * kDecRows + row * D + d0);
+#pragma unroll
+            for (int i = 0; i < DPT / 4; ++i) {
+                const float4 v = __ldg(op4 + i);
+                acc[4 * i + 0] += f * v.x;
+                acc[4 * i + 1] += f * v.y;
+                acc[4 * i + 2] += f * v.z;
+                acc[4 * i + 3] += f * v.w;
+            }
         }
     }
     if (!active) {

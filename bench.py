@@ -356,6 +356,7 @@ def run_ours(args):
     if rank == 0 and not args.no_extras:
         out["extras"] = extras(device, stream, args)
         out["extras"]["dense"] = dense_extras(device, stream)
+        out["extras"]["config2_sweep"] = decode_sweep(device, stream)
     if world > 1 and not args.no_extras:
         sharded = sharded_dit(device, stream, world, rank)  # collective: every rank
         if rank == 0:
@@ -413,6 +414,41 @@ def extras(device, stream, args):
         b1 = 8_409_088
         res["config1_single_op"] = {"us_per_op": round(us, 2), "gbs": round(b1 / (us / 1e6) / 1e9, 1),
                                     "note": "64 distinct ops back to back in one CUDA graph (8.4 MB each)"}
+    return res
+
+
+def decode_sweep(device, stream, layers=LAYERS):
+    """BASELINE config 2's sweep: KV length {512, 2048, 8192} x KV sets
+    {2, 8, 16} (1, 4, 8 requests x CFG) x F16 / Q8_0, each a stack of `layers`
+    distinct layers replayed in one CUDA graph (the (8192, 16) points are the
+    headline and the q8_0_stack figures)."""
+    import torch
+
+    peak, _ = read_peaks()
+    res = {}
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for kv in ("f16", "q8_0"):
+        row = 2 * D if kv == "f16" else D // 32 * 34
+        for kv_len in (512, 2048, 8192):
+            for sets in (2, 8, 16):
+                if kv_len == 8192 and sets == 16:
+                    continue
+                with torch.cuda.stream(stream):
+                    ops, _ = build_stack(device, kv=kv, layers=layers, sets=sets, kv_len=kv_len,
+                                         seed=SEED + 17 * kv_len + sets)
+                    graph = time_graph(ops, 5, 3, stream)
+                    s0.record(stream)
+                    for _ in range(5):
+                        graph.replay()
+                    s1.record(stream)
+                    torch.cuda.synchronize()
+                ms = s0.elapsed_time(s1) / 5
+                b = algo_bytes_per_op(sets=sets, kv_len=kv_len, kv_bytes_per_row=row) * layers
+                gbs = b / (ms / 1e3) / 1e9
+                res[f"L{kv_len}_N{sets}_{kv}"] = {"gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
+                                                  "us_per_op": round(ms * 1e3 / layers, 2)}
+                del graph, ops
+                torch.cuda.empty_cache()
     return res
 
 
