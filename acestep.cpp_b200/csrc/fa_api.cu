@@ -452,6 +452,7 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
     L.p.tiles_per_unit = plan.tpu;
     L.p.total_tiles    = plan.total_tiles;
     L.p.n_ctas         = plan.n_ctas;
+    L.p.div32          = (uint64_t) plan.total_tiles * (uint64_t) (plan.n_ctas + 1) < (1ull << 32) ? 1 : 0;
     L.p.partials       = static_cast<float *>(workspace);
     L.p.dev_err        = di->err_ptr;
     L.p.wait_limit_ns  = wait_limit_ns();

@@ -66,7 +66,14 @@ struct DecCfg {
     static constexpr int kThreads   = (kDecWarps + 1) * 32;
 };
 
-__device__ __forceinline__ int64_t cta_of_tile(int64_t t, int64_t T, int C) { return ((t + 1) * C - 1) / T; }
+// a * b / c, by 32-bit division when the plan says every such product fits
+// (a 64-bit division is a long emulated sequence on the critical path).
+__device__ __forceinline__ int64_t mul_div(int64_t a, int64_t b, int64_t c, int div32) {
+    return div32 ? (int64_t) ((uint32_t) (a * b) / (uint32_t) c) : a * b / c;
+}
+__device__ __forceinline__ int64_t cta_of_tile(int64_t t, int64_t T, int C, int div32) {
+    return div32 ? (int64_t) (((uint32_t) (t + 1) * (uint32_t) C - 1u) / (uint32_t) T) : ((t + 1) * C - 1) / T;
+}
 
 struct UnitCoord {
     int b, hk, rb, bk, rows;
@@ -215,8 +222,8 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     const OpDesc &o  = P.op;
     const int64_t T  = P.total_tiles;
     const int     C  = P.n_ctas;
-    const int64_t t0 = (int64_t) blockIdx.x * T / C;
-    const int64_t t1 = (int64_t) (blockIdx.x + 1) * T / C;
+    const int64_t t0 = mul_div(blockIdx.x, T, C, P.div32);
+    const int64_t t1 = mul_div(blockIdx.x + 1, T, C, P.div32);
     const int     tpu = P.tiles_per_unit;
 
     if (warp == kDecWarps) {
@@ -270,7 +277,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             return 0;
         };
         for (int64_t t = t0; t < t1 && ok;) {
-            const int       u   = (int) (t / tpu);
+            const int       u   = (int) mul_div(t, 1, tpu, P.div32);
             const int64_t   ue  = min(t1, (int64_t) (u + 1) * tpu);
             const int       tlo = (int) (t - (int64_t) u * tpu);
             const int       thi = (int) (ue - (int64_t) u * tpu);
@@ -696,22 +703,30 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             fac[i] = m_run[i] == -INFINITY ? 0.0f : fast_exp2(m_run[i] - mx);
         }
         // The four warps' partial O, rescaled to the common row max, summed in
-        // shared memory one warp at a time (plain stores: each lane owns its
-        // elements within a warp), while threads 0-15 merge the row statistics.
+        // shared memory in four turns; in turn t warp w adds its n8 tiles of
+        // column block (w + t) % 4, so every warp works in every turn and each
+        // element has one writer per turn (plain stores, no atomics).  Threads
+        // 0-15 also merge the row statistics.
+        constexpr int NTB = NT / 4;  // n8 tiles per column block
 #pragma unroll
-        for (int w = 0; w < kDecWarps; ++w) {
-            if (warp == w) {
+        for (int t = 0; t < 4; ++t) {
+            const int bsel = (warp + t) & 3;
 #pragma unroll
-                for (int j = 0; j < NT; ++j) {
+            for (int bb = 0; bb < 4; ++bb) {
+                if (bb == bsel) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float      *mp = &merge[(g + 8 * (e >> 1)) * Cfg::kMergeStride + out_dim(j, e)];
-                        const float v  = oacc[j][e] * fac[e >> 1];
-                        *mp            = w == 0 ? v : *mp + v;
+                    for (int jj = 0; jj < NTB; ++jj) {
+                        const int j = bb * NTB + jj;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            float      *mp = &merge[(g + 8 * (e >> 1)) * Cfg::kMergeStride + out_dim(j, e)];
+                            const float v  = oacc[j][e] * fac[e >> 1];
+                            *mp            = t == 0 ? v : *mp + v;
+                        }
                     }
                 }
             }
-            if (w == 0 && threadIdx.x < kDecRows) {
+            if (t == 0 && threadIdx.x < kDecRows) {
                 const int row = threadIdx.x;
                 float     mx  = -INFINITY;
 #pragma unroll
@@ -729,48 +744,62 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             }
             named_bar_sync(1, kDecWarps * 32);
         }
-        const int64_t cf     = cta_of_tile((int64_t) u * tpu, T, C);
-        const int64_t cl     = cta_of_tile((int64_t) (u + 1) * tpu - 1, T, C);
-        const bool    direct = cf == cl;
-        float        *slot   = P.partials + (int64_t) (blockIdx.x + u) * dec_slot_floats(D);
+        // this CTA holds every tile of the unit: write the output itself
+        const bool direct = t0 <= (int64_t) u * tpu && (int64_t) (u + 1) * tpu <= t1;
+        float     *slot   = P.partials + (int64_t) (blockIdx.x + u) * dec_slot_floats(D);
         if (!direct && threadIdx.x < kDecRows && threadIdx.x < uc.rows) {
             slot[threadIdx.x]            = s_fin[threadIdx.x];
             slot[kDecRows + threadIdx.x] = s_fin[kDecRows + threadIdx.x];
         }
-        for (int idx = threadIdx.x; idx < kDecRows * D; idx += kDecWarps * 32) {
-            const int row = idx / D;
-            const int d   = idx % D;
+        // four consecutive head dims per thread and step
+        for (int idx = threadIdx.x; idx < kDecRows * (D / 4); idx += kDecWarps * 32) {
+            const int row = idx / (D / 4);
+            const int d   = (idx % (D / 4)) * 4;
             if (row >= uc.rows) {
                 continue;
             }
-            float acc = merge[row * Cfg::kMergeStride + d];
+            float4 acc = *reinterpret_cast<const float4 *>(&merge[row * Cfg::kMergeStride + d]);
             if (direct) {
                 const float mx = s_fin[row];
                 float       l  = s_fin[kDecRows + row];
+                float       fs = 1.0f;
                 int         iq, hq;
                 row_coord(P, uc, row, iq, hq);
                 if (o.sinks) {
                     const float ts = o.sinks[hq] * kLog2e;
                     if (ts > mx) {
-                        const float f = fast_exp2(mx - ts);
-                        acc *= f;
-                        l = l * f + 1.0f;
+                        fs = fast_exp2(mx - ts);
+                        l  = l * fs + 1.0f;
                     } else {
                         l += fast_exp2(ts - mx);
                     }
                 }
-                const float out = l == 0.0f ? 0.0f : acc / l;
-                char       *dp  = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
+                const float inv = l == 0.0f ? 0.0f : fs / l;
+                acc             = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+                char *dp = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
                            (int64_t) uc.b * o.d_nb3;
-                *reinterpret_cast<float *>(dp) = out;
-                for (int mi = 0; mi < o.n_mirror; ++mi) {
-                    *reinterpret_cast<float *>(dp + o.mirror_delta[mi]) = out;
+                if (o.d_nb0 == 4 && (reinterpret_cast<uintptr_t>(dp) & 15u) == 0) {
+                    // mirrors are congruent to dst modulo 16 B
+                    *reinterpret_cast<float4 *>(dp) = acc;
+                    for (int mi = 0; mi < o.n_mirror; ++mi) {
+                        *reinterpret_cast<float4 *>(dp + o.mirror_delta[mi]) = acc;
+                    }
+                } else {
+                    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        char *dk = dp + (int64_t) k * o.d_nb0;
+                        *reinterpret_cast<float *>(dk) = a4[k];
+                        for (int mi = 0; mi < o.n_mirror; ++mi) {
+                            *reinterpret_cast<float *>(dk + o.mirror_delta[mi]) = a4[k];
+                        }
+                    }
                 }
                 if (o.n_mirror) {
                     __threadfence_system();
                 }
             } else {
-                slot[2 * kDecRows + row * D + d] = acc;
+                *reinterpret_cast<float4 *>(slot + 2 * kDecRows + row * D + d) = acc;
             }
         }
         named_bar_sync(1, kDecWarps * 32);  // merge and s_fin are free for the next unit
@@ -779,7 +808,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     // The first unit is known from the tile range: fetch its Q while the
     // producer scans the mask and issues the first copies.
     if (t0 < t1) {
-        cur_unit = (int) (t0 / tpu);
+        cur_unit = (int) mul_div(t0, 1, tpu, P.div32);
         setup_unit(cur_unit);
     }
     while (true) {
@@ -839,8 +868,8 @@ __global__ void __launch_bounds__(kCombThreads) fa_decode_combine(const __grid_c
     const int64_t T   = P.total_tiles;
     const int     C   = P.n_ctas;
     const int     tpu = P.tiles_per_unit;
-    const int64_t cf  = cta_of_tile((int64_t) u * tpu, T, C);
-    const int64_t cl  = cta_of_tile((int64_t) (u + 1) * tpu - 1, T, C);
+    const int64_t cf  = cta_of_tile((int64_t) u * tpu, T, C, P.div32);
+    const int64_t cl  = cta_of_tile((int64_t) (u + 1) * tpu - 1, T, C, P.div32);
     if (cf == cl) {
         return;
     }
@@ -880,12 +909,18 @@ __global__ void __launch_bounds__(kCombThreads) fa_decode_combine(const __grid_c
     }
     const int grp = (threadIdx.x & 31) & ~15;  // first lane of this row's 16 in the warp
     // a unit spans at most kDecMaxParts + 1 CTAs (its ends need not align with
-    // theirs): at most 16 parts, one per thread of the row
+    // theirs): at most 16 parts, one per thread of the row.  The weights are
+    // gathered first so that no shuffle sits between the loads below.
     static_assert(kDecMaxParts + 1 <= 16, "one part per thread of a row");
+    float fw[16];
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+        fw[p] = __shfl_sync(0xffffffffu, f_p, grp + p);
+    }
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
         if (p < np) {  // uniform over the CTA
-            const float   f   = __shfl_sync(0xffffffffu, f_p, grp + p);
+            const float   f   = fw[p];
             const float4 *op4 = reinterpret_cast<const float4 *>(base + p * stride + 2 * kDecRows + row * D + d0);
 #pragma unroll
             for (int i = 0; i < DPT / 4; ++i) {

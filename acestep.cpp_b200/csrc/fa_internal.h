@@ -74,6 +74,7 @@ struct DecodeParams {
     int     tiles_per_unit;  // ceil(n_kv / kDecBN)
     int64_t total_tiles;     // units * tiles_per_unit
     int     n_ctas;          // persistent CTAs
+    int     div32;           // total_tiles * (n_ctas + 1) < 2^32: tile/CTA arithmetic fits 32-bit division
     float  *partials;        // workspace: (n_ctas + units) slots
     int    *dev_err;
     uint64_t wait_limit_ns;
