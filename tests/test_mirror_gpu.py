@@ -2,9 +2,7 @@
 this device laid out like dst.  Every kernel family's output stage (decode
 direct write, split-KV combine, dense tcgen05) must store the identical rows to
 dst and to every mirror (bit for bit: the same value goes to every address),
-and dst must meet the parity tolerance like the unmirrored call.  (Two launches
-of the decode kernel can differ in the last bit: its four consumer warps merge
-their partial outputs with shared-memory float atomics in arrival order.)"""
+and dst must meet the parity tolerance like the unmirrored call."""
 import numpy as np
 import pytest
 import torch
