@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "acefa_peer_export",
     "acefa_peer_import",
     "acefa_peer_release",
+    "acefa_flash_attn_ext_append",
 )
 
 MAX_MIRRORS = 7
@@ -105,6 +106,10 @@ def load_library(path: str | None = None):
                                                   ctypes.c_int, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
                                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
     lib.acefa_flash_attn_ext_mirrored.restype = ctypes.c_int
+    lib.acefa_flash_attn_ext_append.argtypes = [T, T, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                                ctypes.c_int, T, T, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_size_t]
+    lib.acefa_flash_attn_ext_append.restype = ctypes.c_int
     lib.acefa_peer_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
     lib.acefa_peer_export.restype = ctypes.c_int
     lib.acefa_peer_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
@@ -175,7 +180,7 @@ class Op:
     """One ggml_flash_attn_ext node's operands, described once, callable many times."""
 
     def __init__(self, q, k, v, mask=None, sinks=None, out=None, kv_type=None, scale=None,
-                 max_bias=0.0, softcap=0.0, prec=PREC_F32, mirrors=()):
+                 max_bias=0.0, softcap=0.0, prec=PREC_F32, mirrors=(), k_new=None, v_new=None, pos=None):
         self.lib = load_library()
         self.q, self.k, self.v, self.mask, self.sinks = q, k, v, mask, sinks
         D = q.shape[-1]
@@ -198,11 +203,27 @@ class Op:
         self.ws_bytes = int(self.lib.acefa_workspace_bytes(_ref(self.tq), _ref(self.tk), _ref(self.tv),
                                                            _ref(self.tm), _ref(self.td)))
         self.workspace = torch.empty(max(self.ws_bytes, 256), dtype=torch.uint8, device=q.device)
+        # fused KV append: k_new / v_new (Bk, Hkv, 1, D) f32, pos (Bk,) int64 on the device
+        self.append = k_new is not None
+        if self.append:
+            if v_new is None or pos is None or pos.dtype != torch.int64 or not pos.is_cuda:
+                raise ValueError("append needs k_new, v_new and an int64 device tensor pos")
+            self.k_new, self.v_new, self.pos = k_new, v_new, pos
+            self.tkn, self.tvn = describe(k_new), describe(v_new)
         # mirrors: device addresses laid out like `out` (e.g. peer GPUs' buffers)
         self.n_mirrors = len(mirrors)
         self.mirrors = (ctypes.c_void_p * max(1, self.n_mirrors))(*[int(m) for m in mirrors])
 
     def __call__(self, stream=None):
+        if self.append:
+            st = self.lib.acefa_flash_attn_ext_append(
+                _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),
+                self.scale, self.max_bias, self.softcap, self.prec, _ref(self.tkn), _ref(self.tvn),
+                ctypes.c_void_p(self.pos.data_ptr()), ctypes.c_void_p(_stream_ptr(stream)),
+                ctypes.c_void_p(self.workspace.data_ptr()), ctypes.c_size_t(self.workspace.numel()))
+            if st != OK:
+                raise AcefaError(st, "acefa_flash_attn_ext_append")
+            return self.out
         if self.n_mirrors:
             st = self.lib.acefa_flash_attn_ext_mirrored(
                 _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),

@@ -333,47 +333,18 @@ int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D, int box_rows) 
 
 using namespace acefa;
 
-extern "C" {
+// The operator with optional mirrors (acefa_flash_attn_ext_mirrored) and an
+// optional fused KV-cache append (acefa_flash_attn_ext_append).
+struct AppendArgs {
+    const char    *k_new, *v_new;
+    int64_t        kn_nb2, kn_nb3, vn_nb2, vn_nb3;
+    const int64_t *pos;
+};
 
-ACEFA_API int acefa_check(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
-                          const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
-    return check_operands(q, k, v, mask, sinks, dst).status;
-}
-
-ACEFA_API int acefa_supports(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
-                             const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
-    return check_operands(q, k, v, mask, sinks, dst).status == ACEFA_OK ? 1 : 0;
-}
-
-ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
-                                       const acefa_tensor *mask, const acefa_tensor *dst) {
-    Checked c = check_operands(q, k, v, mask, nullptr, dst);
-    if (c.status != ACEFA_OK) {
-        return 0;
-    }
-    DevInfo *di = nullptr;
-    if (dev_info(&di) != ACEFA_OK) {
-        return 0;
-    }
-    if (use_dense(c.op)) {
-        return plan_dense(c.op, di->sm_count).ws_bytes;
-    }
-    return plan_decode(c.op, di->sm_count).ws_bytes;
-}
-
-ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
-                                   const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst,
-                                   float scale, float max_bias, float logit_softcap, int prec, void *stream,
-                                   void *workspace, size_t workspace_bytes) {
-    return acefa_flash_attn_ext_mirrored(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0,
-                                         stream, workspace, workspace_bytes);
-}
-
-ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
-                                            const acefa_tensor *mask, const acefa_tensor *sinks,
-                                            const acefa_tensor *dst, float scale, float max_bias,
-                                            float logit_softcap, int prec, void *const *mirrors, int n_mirrors,
-                                            void *stream, void *workspace, size_t workspace_bytes) {
+static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v, const acefa_tensor *mask,
+                  const acefa_tensor *sinks, const acefa_tensor *dst, float scale, float max_bias,
+                  float logit_softcap, int prec, void *const *mirrors, int n_mirrors, const AppendArgs *app,
+                  void *stream, void *workspace, size_t workspace_bytes) {
     (void) prec;  // accumulation is F32 for both GGML_PREC_DEFAULT and GGML_PREC_F32
     Checked c = check_operands(q, k, v, mask, sinks, dst);
     if (c.status != ACEFA_OK) {
@@ -406,6 +377,9 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
     if (use_dense(c.op)) {
+        if (app) {
+            return ACEFA_ERR_SHAPE;  // the fused append serves the decode path (one new row per set)
+        }
         const DensePlan dp = plan_dense(c.op, di->sm_count);
         if (workspace_bytes < dp.ws_bytes || !workspace || !aligned(workspace, 256)) {
             return ACEFA_ERR_WORKSPACE;
@@ -453,6 +427,15 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
     L.p.total_tiles    = plan.total_tiles;
     L.p.n_ctas         = plan.n_ctas;
     L.p.div32          = (uint64_t) plan.total_tiles * (uint64_t) (plan.n_ctas + 1) < (1ull << 32) ? 1 : 0;
+    if (app) {
+        L.p.k_new      = app->k_new;
+        L.p.v_new      = app->v_new;
+        L.p.kn_nb2     = app->kn_nb2;
+        L.p.kn_nb3     = app->kn_nb3;
+        L.p.vn_nb2     = app->vn_nb2;
+        L.p.vn_nb3     = app->vn_nb3;
+        L.p.append_pos = app->pos;
+    }
     L.p.partials       = static_cast<float *>(workspace);
     L.p.dev_err        = di->err_ptr;
     L.p.wait_limit_ns  = wait_limit_ns();
@@ -470,6 +453,77 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
     t_last_launches = launches;
     t_last_path     = 1;
     return ACEFA_OK;
+}
+
+extern "C" {
+
+ACEFA_API int acefa_check(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                          const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
+    return check_operands(q, k, v, mask, sinks, dst).status;
+}
+
+ACEFA_API int acefa_supports(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                             const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst) {
+    return check_operands(q, k, v, mask, sinks, dst).status == ACEFA_OK ? 1 : 0;
+}
+
+ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                       const acefa_tensor *mask, const acefa_tensor *dst) {
+    Checked c = check_operands(q, k, v, mask, nullptr, dst);
+    if (c.status != ACEFA_OK) {
+        return 0;
+    }
+    DevInfo *di = nullptr;
+    if (dev_info(&di) != ACEFA_OK) {
+        return 0;
+    }
+    if (use_dense(c.op)) {
+        return plan_dense(c.op, di->sm_count).ws_bytes;
+    }
+    return plan_decode(c.op, di->sm_count).ws_bytes;
+}
+
+ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                   const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst,
+                                   float scale, float max_bias, float logit_softcap, int prec, void *stream,
+                                   void *workspace, size_t workspace_bytes) {
+    return acefa_flash_attn_ext_mirrored(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0,
+                                         stream, workspace, workspace_bytes);
+}
+
+ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                            const acefa_tensor *mask, const acefa_tensor *sinks,
+                                            const acefa_tensor *dst, float scale, float max_bias,
+                                            float logit_softcap, int prec, void *const *mirrors, int n_mirrors,
+                                            void *stream, void *workspace, size_t workspace_bytes) {
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, mirrors, n_mirrors, nullptr,
+                  stream, workspace, workspace_bytes);
+}
+
+ACEFA_API int acefa_flash_attn_ext_append(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                          const acefa_tensor *mask, const acefa_tensor *sinks,
+                                          const acefa_tensor *dst, float scale, float max_bias, float logit_softcap,
+                                          int prec, const acefa_tensor *k_new, const acefa_tensor *v_new,
+                                          const int64_t *pos, void *stream, void *workspace,
+                                          size_t workspace_bytes) {
+    if (!k_new || !v_new || !pos || !k_new->data || !v_new->data || !k || !v) {
+        return ACEFA_ERR_NULL;
+    }
+    if (k_new->type != ACEFA_TYPE_F32 || v_new->type != ACEFA_TYPE_F32) {
+        return ACEFA_ERR_TYPE;
+    }
+    for (const acefa_tensor *t : {k_new, v_new}) {
+        if (t->ne[0] != k->ne[0] || t->ne[1] != 1 || t->ne[2] != k->ne[2] || t->ne[3] != k->ne[3]) {
+            return ACEFA_ERR_SHAPE;
+        }
+        if (t->nb[0] != 4 || t->nb[2] % 4 || t->nb[3] % 4 || !aligned(t->data, 4)) {
+            return ACEFA_ERR_LAYOUT;
+        }
+    }
+    AppendArgs a{static_cast<const char *>(k_new->data), static_cast<const char *>(v_new->data),
+                 (int64_t) k_new->nb[2], (int64_t) k_new->nb[3], (int64_t) v_new->nb[2], (int64_t) v_new->nb[3], pos};
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0, &a, stream, workspace,
+                  workspace_bytes);
 }
 
 ACEFA_API int acefa_device_error(void *stream) {

@@ -180,6 +180,87 @@ __device__ __forceinline__ void lds_bytes_unaligned(uint32_t addr, uint32_t (&ou
 
 }  // namespace
 
+// Fused KV-cache append, run by the producer warp of the CTA whose tile range
+// holds the new row's tile: the f32 row of K and of V for (kv head, set) is
+// converted to the cache type -- F16 / BF16 rounded to nearest even, Q8_0 by
+// ggml's reference quantiser (d = amax/127, q = roundf(x * (1/d)), d stored
+// as f16) -- and stored at cache row append_pos[set].  append_load fetches the
+// lane's four values of each row early (their latency overlaps the unit's
+// first copies); append_store writes them, and its proxy fence orders the
+// generic stores before the warp's later TMA / bulk-copy reads of that row.
+// Lane mapping: F16/BF16 dims lane + 32k; Q8_0 block lane/8, values 4*(lane%8)+k.
+template <int KV_TYPE, int D>
+__device__ __forceinline__ int append_index(int lane, int k) {
+    return KV_TYPE == ACEFA_TYPE_Q8_0 ? (lane >> 3) * 32 + (lane & 7) * 4 + k : lane + 32 * k;
+}
+
+template <int KV_TYPE, int D>
+__device__ __forceinline__ void append_load(const DecodeParams &P, int hk, int bk, int lane, float (&xk)[4],
+                                            float (&xv)[4]) {
+    const float *ks = reinterpret_cast<const float *>(P.k_new + (int64_t) hk * P.kn_nb2 + (int64_t) bk * P.kn_nb3);
+    const float *vs = reinterpret_cast<const float *>(P.v_new + (int64_t) hk * P.vn_nb2 + (int64_t) bk * P.vn_nb3);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int  i  = append_index<KV_TYPE, D>(lane, k);
+        const bool in = KV_TYPE == ACEFA_TYPE_Q8_0 ? (lane >> 3) < D / 32 : k < D / 32;
+        xk[k]         = in ? ks[i] : 0.0f;
+        xv[k]         = in ? vs[i] : 0.0f;
+    }
+}
+
+template <int KV_TYPE, int D>
+__device__ __forceinline__ void append_store(const DecodeParams &P, int64_t pr, int lane, const char *kbase,
+                                             const char *vbase, const float (&xk)[4], const float (&xv)[4]) {
+    const OpDesc &o = P.op;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+        const float(&x)[4] = which ? xv : xk;
+        char *dst          = const_cast<char *>(which ? vbase + pr * o.v_nb1 : kbase + pr * o.k_nb1);
+        if constexpr (KV_TYPE == ACEFA_TYPE_Q8_0) {
+            // 32-value blocks, eight lanes per block, four values per lane
+            constexpr int NB   = D / 32;
+            const int     blk  = lane >> 3;
+            const int     sub  = lane & 7;
+            float         amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                amax = fmaxf(amax, fabsf(x[k]));
+            }
+#pragma unroll
+            for (int off = 4; off > 0; off >>= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            }
+            const float d  = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            if (blk < NB) {
+                // rows and blocks start at even addresses (34-B blocks, rows of
+                // D/32 blocks, validated 2-B aligned): 16-bit stores throughout
+                uint16_t *bp = reinterpret_cast<uint16_t *>(dst + blk * 34);
+                if (sub == 0) {
+                    bp[0] = __half_as_ushort(__float2half_rn(d));
+                }
+#pragma unroll
+                for (int k = 0; k < 4; k += 2) {
+                    const uint32_t q0 = (uint32_t) (uint8_t) (int8_t) roundf(x[k] * id);
+                    const uint32_t q1 = (uint32_t) (uint8_t) (int8_t) roundf(x[k + 1] * id);
+                    bp[1 + sub * 2 + k / 2] = (uint16_t) (q0 | (q1 << 8));
+                }
+            }
+        } else {
+            uint16_t *dh = reinterpret_cast<uint16_t *>(dst);
+#pragma unroll
+            for (int k = 0; k < D / 32; ++k) {
+                const float v = x[k];
+                dh[append_index<KV_TYPE, D>(lane, k)] =
+                    KV_TYPE == ACEFA_TYPE_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                               : __half_as_ushort(__float2half_rn(v));
+            }
+        }
+    }
+    fence_proxy_async_global();
+    __syncwarp();
+}
+
 template <int KV_TYPE, int D>
 __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     fa_decode_kernel(const __grid_constant__ DecodeParams P, const __grid_constant__ CUtensorMap kmap,
@@ -284,6 +365,24 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             const UnitCoord uc  = unit_coord(P, u);
             const char *kbase = o.k + (int64_t) uc.hk * o.k_nb2 + (int64_t) uc.bk * o.k_nb3;
             const char *vbase = o.v + (int64_t) uc.hk * o.v_nb2 + (int64_t) uc.bk * o.v_nb3;
+            // Fused append: the row is written by the CTA whose range holds its
+            // tile, just before that tile's copy is issued (after the earlier
+            // tiles' copies, so its latency overlaps them), or after the unit's
+            // tiles when the mask makes that tile dead.
+            int64_t app_row  = -1;
+            int     app_tile = -1;
+            float   app_k[4], app_v[4];
+            if (P.append_pos) {
+                app_row = P.append_pos[uc.bk];
+                if (app_row < 0 || app_row >= o.n_kv) {
+                    if (lane == 0) {
+                        atomicCAS(P.dev_err, 0, DEVERR_APPEND_POS);
+                    }
+                } else if (app_row / kDecBN >= tlo && app_row / kDecBN < thi) {
+                    app_tile = (int) (app_row / kDecBN);
+                    append_load<KV_TYPE, D>(P, uc.hk, uc.bk, lane, app_k, app_v);
+                }
+            }
             // Mask slots: the distinct mask rows this unit reads (one per query
             // index when the mask is shared by all heads).  Lane s owns slot s and
             // stages its 64-key segment of every tile into shared memory.
@@ -315,6 +414,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     const int i = __ffs(bits) - 1;
                     bits &= bits - 1;
                     const int ti = tb + i;
+                    if (ti == app_tile) {
+                        append_store<KV_TYPE, D>(P, app_row, lane, kbase, vbase, app_k, app_v);
+                        app_tile = -1;
+                    }
                     ok           = acquire();
                     if (!ok) {
                         break;
@@ -381,6 +484,9 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     __syncwarp();
                     advance();
                 }
+            }
+            if (app_tile >= 0) {  // the row's tile is dead for this unit: no read to order
+                append_store<KV_TYPE, D>(P, app_row, lane, kbase, vbase, app_k, app_v);
             }
             if (!ok) {
                 break;

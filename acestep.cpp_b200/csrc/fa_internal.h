@@ -76,6 +76,12 @@ struct DecodeParams {
     int     n_ctas;          // persistent CTAs
     int     div32;           // total_tiles * (n_ctas + 1) < 2^32: tile/CTA arithmetic fits 32-bit division
     float  *partials;        // workspace: (n_ctas + units) slots
+    // Fused KV-cache append (acefa_flash_attn_ext_append), or all null: the
+    // new K/V row of (kv head h, set s) is f32 at k_new + h*kn_nb2 + s*kn_nb3
+    // and goes into cache row append_pos[s] before that row is read.
+    const char    *k_new, *v_new;
+    int64_t        kn_nb2, kn_nb3, vn_nb2, vn_nb3;
+    const int64_t *append_pos;
     int    *dev_err;
     uint64_t wait_limit_ns;
 };

@@ -19,6 +19,7 @@ enum : int {
     DEVERR_TIMEOUT_EMPTY = 2,  // producer waited too long for a free stage
     DEVERR_TIMEOUT_MMA   = 3,  // tensor-core completion never signalled
     DEVERR_TIMEOUT_DRAIN = 4,  // in-flight copies did not land while aborting
+    DEVERR_APPEND_POS    = 5,  // an append position outside [0, n_kv): row not written
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -40,6 +41,11 @@ __device__ __forceinline__ void fence_barrier_init() {
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Orders this thread's generic-proxy global stores before later async-proxy
+// (TMA / bulk copy) reads of the same addresses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)

@@ -414,7 +414,64 @@ def extras(device, stream, args):
         b1 = 8_409_088
         res["config1_single_op"] = {"us_per_op": round(us, 2), "gbs": round(b1 / (us / 1e6) / 1e9, 1),
                                     "note": "64 distinct ops back to back in one CUDA graph (8.4 MB each)"}
+        res["config1_append"] = append_step(device, stream)
     return res
+
+
+def append_step(device, stream, reps=64, kv_len=2048):
+    """A config-1 decode step with its KV-cache append: the new K and V rows
+    written by two separate row writes (standing in for ggml_set_rows) and then
+    the attention, against acefa_flash_attn_ext_append doing both in one
+    launch.  64 distinct layers back to back in one CUDA graph each."""
+    import torch
+
+    import acefa
+
+    g = torch.Generator(device=device).manual_seed(42 + 1000 + 7)
+    sep, fused = [], []
+    for _ in range(reps):
+        q = torch.randn(1, 16, 1, D, device=device, generator=g)
+        k = torch.randn(1, 8, kv_len, D, device=device, generator=g, dtype=torch.float16)
+        v = torch.randn(1, 8, kv_len, D, device=device, generator=g, dtype=torch.float16)
+        m = torch.zeros(1, 1, 1, kv_len, device=device, dtype=torch.float16)
+        kn = torch.randn(1, 8, 1, D, device=device, generator=g)
+        vn = torch.randn(1, 8, 1, D, device=device, generator=g)
+        pos = torch.tensor([kv_len - 1], dtype=torch.int64, device=device)
+        op = acefa.Op(q, k, v, mask=m, scale=D ** -0.5)
+        sep.append((op, k, v, kn, vn, pos))
+        fused.append(acefa.Op(q, k, v, mask=m, scale=D ** -0.5, k_new=kn, v_new=vn, pos=pos))
+
+    def run_sep():
+        for op, k, v, kn, vn, pos in sep:
+            k.index_copy_(2, pos, kn.half())
+            v.index_copy_(2, pos, vn.half())
+            op(stream=torch.cuda.current_stream())
+
+    def run_fused():
+        for op in fused:
+            op(stream=torch.cuda.current_stream())
+
+    out = {}
+    for name, fn in (("separate_us_per_step", run_sep), ("fused_us_per_step", run_fused)):
+        with torch.cuda.stream(stream):
+            fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                fn()
+            for _ in range(3):
+                graph.replay()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(10):
+                graph.replay()
+            s1.record(stream)
+            torch.cuda.synchronize()
+        out[name] = round(s0.elapsed_time(s1) * 1e3 / (10 * reps), 2)
+        del graph
+    out["note"] = ("config-1 shape, new row at the last position; separate = two row writes (torch index_copy, "
+                   "standing in for ggml_set_rows) + acefa_flash_attn_ext")
+    return out
 
 
 def decode_sweep(device, stream, layers=LAYERS):

@@ -143,6 +143,35 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
                                             void *stream, void *workspace, size_t workspace_bytes);
 
 /*
+ * The operator fused with the KV-cache append that precedes it in a decode
+ * step.  The reference writes the new row with two ggml_set_rows nodes (K and V
+ * at src/qwen3-lm.h:776-777, inside qw3lm_forward_batch) and then runs the
+ * attention node over the cache views; this entry does both in one launch.
+ *
+ *   k_new, v_new  [D, 1, Hkv, Bk] F32, nb[0] == 4: the new row of every
+ *                 (kv head, set), already projected, normed and rotated
+ *   pos           device array of Bk int64: the cache row (0 <= pos < n_kv of
+ *                 the k/v views) that receives set s's new row
+ *
+ * Row pos[s] of every head of set s in k and v is overwritten with k_new /
+ * v_new converted to the cache type (F16 / BF16 rounded to nearest even; Q8_0
+ * by ggml's reference quantiser: d = amax/127, q = roundf(x * (1/d)), d as f16), and
+ * the attention then reads the updated cache exactly as acefa_flash_attn_ext
+ * would have after the two set_rows.  The k and v views must be writable and
+ * each (head, set) row written once: sets whose views alias each other, or a
+ * mask that hides row pos[s], are the caller's concern.  Served by the decode
+ * path only (query rows per kv head <= 64, i.e. decode steps); other shapes
+ * return ACEFA_ERR_SHAPE.  A pos outside [0, n_kv) leaves that set's row
+ * unwritten and raises device error 5 (acefa_device_error()).  Other
+ * arguments and results are those of acefa_flash_attn_ext().
+ */
+ACEFA_API int acefa_flash_attn_ext_append(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                          const acefa_tensor *mask, const acefa_tensor *sinks,
+                                          const acefa_tensor *dst, float scale, float max_bias, float logit_softcap,
+                                          int prec, const acefa_tensor *k_new, const acefa_tensor *v_new,
+                                          const int64_t *pos, void *stream, void *workspace, size_t workspace_bytes);
+
+/*
  * CUDA IPC through the ABI, so a host without CUDA bindings can map peer
  * buffers.  acefa_peer_export: an opaque handle (ACEFA_PEER_HANDLE_BYTES bytes)
  * for the allocation holding ptr, plus ptr's byte offset inside it.

@@ -167,6 +167,26 @@ def test_mirrored_entry_validates_mirrors_before_launch(lib):
         assert call([(1 << 30) + 4096, (1 << 31) + 4096], 2) in (-6, -7)
 
 
+def test_append_entry_validates_before_launch(lib):
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    q, k, v, m, d = _ops(Hq=32, B=4, Bk=4, nkv=700)
+    kn = _td([128, 1, 8, 4], _contig([128, 1, 8, 4], 4), acefa.GGML_F32, ptr=8192)
+    vn = _td([128, 1, 8, 4], _contig([128, 1, 8, 4], 4), acefa.GGML_F32, ptr=16384)
+
+    def call(kn_, vn_, pos):
+        return lib.acefa_flash_attn_ext_append(r(q), r(k), r(v), r(m), None, r(d), 0.088, 0.0, 0.0, 10,
+                                               r(kn_), r(vn_), pos, None, None, 0)
+
+    assert call(kn, vn, None) == -1                   # no positions
+    assert call(None, vn, 4096) == -1                 # no new K row
+    bad_t = _td([128, 1, 8, 4], _contig([128, 1, 8, 4], 2), acefa.GGML_F16, ptr=8192)
+    assert call(bad_t, vn, 4096) == -2                # new rows are f32
+    bad_s = _td([128, 2, 8, 4], _contig([128, 2, 8, 4], 4), acefa.GGML_F32, ptr=8192)
+    assert call(bad_s, vn, 4096) == -3                # one row per (head, set)
+    if not torch.cuda.is_available():
+        assert call(kn, vn, 4096) in (-6, -7)         # valid: fails only at the device step
+
+
 def test_peer_entry_points_reject_null(lib):
     assert lib.acefa_peer_export(None, None, None) == -1
     assert lib.acefa_peer_import(None, 0, None) == -1
