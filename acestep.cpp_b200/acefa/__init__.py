@@ -47,10 +47,50 @@ EXPORTED_SYMBOLS = (
     "acefa_peer_import",
     "acefa_peer_release",
     "acefa_flash_attn_ext_append",
+    "acefa_flash_attn_ext_gen",
 )
 
 MAX_MIRRORS = 7
 PEER_HANDLE_BYTES = 64
+
+# mask rules (acefa_mask_gen)
+MASK_CAUSAL, MASK_WINDOW, MASK_PADDING = 1, 2, 3
+MASK_GEN_MAX_BATCH = 32
+
+
+class MaskGen(ctypes.Structure):
+    """acefa_mask_gen: a 0 / -inf mask given by its rule."""
+    _fields_ = [("kind", ctypes.c_int32), ("window", ctypes.c_int32),
+                ("pos0", ctypes.c_int64 * MASK_GEN_MAX_BATCH), ("len", ctypes.c_int64 * MASK_GEN_MAX_BATCH)]
+
+
+def mask_gen(kind: int, window: int = 0, pos0=(), lens=()) -> MaskGen:
+    m = MaskGen()
+    m.kind, m.window = int(kind), int(window)
+    for i, p in enumerate(pos0):
+        m.pos0[i] = int(p)
+    for i, n in enumerate(lens):
+        m.len[i] = int(n)
+    return m
+
+
+def rule_mask(m: MaskGen, B: int, n_q: int, n_kv: int, ne0: int | None = None, device="cuda") -> torch.Tensor:
+    """The f16 mask tensor (B, 1, n_q, ne0) a rule stands for: 0 where key j is
+    visible to query i of batch b, -inf elsewhere (and past n_kv)."""
+    ne0 = ne0 or n_kv
+    j = torch.arange(ne0).view(1, 1, ne0)
+    i = torch.arange(n_q).view(1, n_q, 1)
+    if m.kind == MASK_CAUSAL:
+        vis = j <= torch.tensor([m.pos0[b] for b in range(B)]).view(B, 1, 1) + i
+    elif m.kind == MASK_WINDOW:
+        vis = (i - j).abs() <= m.window
+        vis = vis.expand(B, n_q, ne0)
+    else:
+        vis = (j < torch.tensor([m.len[b] for b in range(B)]).view(B, 1, 1)).expand(B, n_q, ne0)
+    vis = vis & (j < n_kv)
+    out = torch.full((B, 1, n_q, ne0), float("-inf"), dtype=torch.float16)
+    out[:, 0][vis] = 0.0
+    return out.to(device)
 
 
 class AcefaError(RuntimeError):
@@ -110,6 +150,10 @@ def load_library(path: str | None = None):
                                                 ctypes.c_int, T, T, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                 ctypes.c_size_t]
     lib.acefa_flash_attn_ext_append.restype = ctypes.c_int
+    lib.acefa_flash_attn_ext_gen.argtypes = [T, T, T, ctypes.POINTER(MaskGen), T, T, ctypes.c_float,
+                                             ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_size_t]
+    lib.acefa_flash_attn_ext_gen.restype = ctypes.c_int
     lib.acefa_peer_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
     lib.acefa_peer_export.restype = ctypes.c_int
     lib.acefa_peer_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
@@ -180,7 +224,8 @@ class Op:
     """One ggml_flash_attn_ext node's operands, described once, callable many times."""
 
     def __init__(self, q, k, v, mask=None, sinks=None, out=None, kv_type=None, scale=None,
-                 max_bias=0.0, softcap=0.0, prec=PREC_F32, mirrors=(), k_new=None, v_new=None, pos=None):
+                 max_bias=0.0, softcap=0.0, prec=PREC_F32, mirrors=(), k_new=None, v_new=None, pos=None,
+                 mask_gen=None):
         self.lib = load_library()
         self.q, self.k, self.v, self.mask, self.sinks = q, k, v, mask, sinks
         D = q.shape[-1]
@@ -210,11 +255,24 @@ class Op:
                 raise ValueError("append needs k_new, v_new and an int64 device tensor pos")
             self.k_new, self.v_new, self.pos = k_new, v_new, pos
             self.tkn, self.tvn = describe(k_new), describe(v_new)
+        # mask by rule (MaskGen) instead of a mask tensor
+        self.mask_gen = mask_gen
+        if mask_gen is not None and (mask is not None or k_new is not None or mirrors):
+            raise ValueError("mask_gen replaces mask and does not combine with append or mirrors")
         # mirrors: device addresses laid out like `out` (e.g. peer GPUs' buffers)
         self.n_mirrors = len(mirrors)
         self.mirrors = (ctypes.c_void_p * max(1, self.n_mirrors))(*[int(m) for m in mirrors])
 
     def __call__(self, stream=None):
+        if self.mask_gen is not None:
+            st = self.lib.acefa_flash_attn_ext_gen(
+                _ref(self.tq), _ref(self.tk), _ref(self.tv), ctypes.byref(self.mask_gen), _ref(self.ts),
+                _ref(self.td), self.scale, self.max_bias, self.softcap, self.prec,
+                ctypes.c_void_p(_stream_ptr(stream)), ctypes.c_void_p(self.workspace.data_ptr()),
+                ctypes.c_size_t(self.workspace.numel()))
+            if st != OK:
+                raise AcefaError(st, "acefa_flash_attn_ext_gen")
+            return self.out
         if self.append:
             st = self.lib.acefa_flash_attn_ext_append(
                 _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),

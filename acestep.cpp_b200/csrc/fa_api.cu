@@ -291,7 +291,7 @@ DensePlan plan_dense(const OpDesc &o, int sm_count) {
     const int64_t sms   = sm_count > 0 ? sm_count : 1;
     const int64_t tail  = units % sms;
     int64_t       split = 1;
-    if (o.mask == nullptr && units >= sms && tail > 0 && tail <= sms / 2) {
+    if (o.mask == nullptr && o.mg_kind == 0 && units >= sms && tail > 0 && tail <= sms / 2) {
         split = std::min<int64_t>(std::min<int64_t>(sms / tail, kDenseMaxSplit), p.n_kt / 16);
         if (split < 2) {
             split = 1;
@@ -333,6 +333,26 @@ int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D, int box_rows) 
 
 using namespace acefa;
 
+// Copies a mask rule into the operand block.  pos0 and len are clamped into
+// [-(n_q + 1), n_kv]: for keys 0 .. n_kv-1 and queries 0 .. n_q-1 that keeps
+// every visibility decision and bounds the device-side sums.
+static int rc_of_rule(OpDesc &o, const acefa_mask_gen *mg) {
+    const bool per_batch = mg->kind == ACEFA_MASK_CAUSAL || mg->kind == ACEFA_MASK_PADDING;
+    if ((!per_batch && mg->kind != ACEFA_MASK_WINDOW) || (per_batch && o.B > ACEFA_MASK_GEN_MAX_BATCH) ||
+        (mg->kind == ACEFA_MASK_WINDOW && mg->window < 0)) {
+        return ACEFA_ERR_SHAPE;
+    }
+    o.mg_kind   = mg->kind;
+    o.mg_window = mg->window;
+    const int64_t lo = -((int64_t) o.n_q + 1), hi = o.n_kv;
+    for (int b = 0; b < ACEFA_MASK_GEN_MAX_BATCH; ++b) {
+        const bool in = per_batch && b < o.B;
+        o.mg_pos0[b]  = in ? std::min(std::max(mg->pos0[b], lo), hi) : 0;
+        o.mg_len[b]   = in ? std::min(std::max(mg->len[b], lo), hi) : 0;
+    }
+    return ACEFA_OK;
+}
+
 // The operator with optional mirrors (acefa_flash_attn_ext_mirrored) and an
 // optional fused KV-cache append (acefa_flash_attn_ext_append).
 struct AppendArgs {
@@ -344,11 +364,14 @@ struct AppendArgs {
 static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v, const acefa_tensor *mask,
                   const acefa_tensor *sinks, const acefa_tensor *dst, float scale, float max_bias,
                   float logit_softcap, int prec, void *const *mirrors, int n_mirrors, const AppendArgs *app,
-                  void *stream, void *workspace, size_t workspace_bytes) {
+                  const acefa_mask_gen *mg, void *stream, void *workspace, size_t workspace_bytes) {
     (void) prec;  // accumulation is F32 for both GGML_PREC_DEFAULT and GGML_PREC_F32
     Checked c = check_operands(q, k, v, mask, sinks, dst);
     if (c.status != ACEFA_OK) {
         return c.status;
+    }
+    if (mg && (rc_of_rule(c.op, mg) != ACEFA_OK)) {
+        return ACEFA_ERR_SHAPE;
     }
     if (!std::isfinite(scale) || !std::isfinite(max_bias) || !std::isfinite(logit_softcap) || max_bias < 0.0f) {
         return ACEFA_ERR_SHAPE;
@@ -496,7 +519,7 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
                                             const acefa_tensor *dst, float scale, float max_bias,
                                             float logit_softcap, int prec, void *const *mirrors, int n_mirrors,
                                             void *stream, void *workspace, size_t workspace_bytes) {
-    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, mirrors, n_mirrors, nullptr,
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, mirrors, n_mirrors, nullptr, nullptr,
                   stream, workspace, workspace_bytes);
 }
 
@@ -522,8 +545,19 @@ ACEFA_API int acefa_flash_attn_ext_append(const acefa_tensor *q, const acefa_ten
     }
     AppendArgs a{static_cast<const char *>(k_new->data), static_cast<const char *>(v_new->data),
                  (int64_t) k_new->nb[2], (int64_t) k_new->nb[3], (int64_t) v_new->nb[2], (int64_t) v_new->nb[3], pos};
-    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0, &a, stream, workspace,
-                  workspace_bytes);
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0, &a, nullptr, stream,
+                  workspace, workspace_bytes);
+}
+
+ACEFA_API int acefa_flash_attn_ext_gen(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                       const acefa_mask_gen *mask_gen, const acefa_tensor *sinks,
+                                       const acefa_tensor *dst, float scale, float max_bias, float logit_softcap,
+                                       int prec, void *stream, void *workspace, size_t workspace_bytes) {
+    if (!mask_gen) {
+        return ACEFA_ERR_NULL;
+    }
+    return run_op(q, k, v, nullptr, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0, nullptr, mask_gen,
+                  stream, workspace, workspace_bytes);
 }
 
 ACEFA_API int acefa_device_error(void *stream) {

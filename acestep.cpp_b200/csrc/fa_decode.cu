@@ -102,14 +102,21 @@ __device__ __forceinline__ const uint16_t *mask_row(const OpDesc &o, int iq, int
                                               (int64_t) (b % o.m_ne3) * o.m_nb3);
 }
 
-// True if some mask entry of this tile, for some row of the unit, is not -inf.
+// True if some mask entry of this tile, for some row of the unit, is not -inf
+// (under a mask rule: some key of the tile is in some row's visible range).
 __device__ bool tile_live(const DecodeParams &P, const UnitCoord &uc, int tile) {
-    const OpDesc &o = P.op;
+    const OpDesc &o   = P.op;
+    const int     j0  = tile * kDecBN;
+    const int     cnt = min(kDecBN, o.n_kv - j0);
+    if (o.mg_kind) {
+        int lo0, hi0, lo1, hi1;
+        mg_range(o, uc.b, (uc.rb * kDecRows) / o.G, lo0, hi0);
+        mg_range(o, uc.b, (uc.rb * kDecRows + uc.rows - 1) / o.G, lo1, hi1);
+        return max(lo0, j0) < min(hi1, j0 + cnt);
+    }
     if (o.mask == nullptr) {
         return true;
     }
-    const int       j0   = tile * kDecBN;
-    const int       cnt  = min(kDecBN, o.n_kv - j0);
     const uint16_t *prev = nullptr;
     for (int rr = 0; rr < uc.rows; ++rr) {
         int iq, hq;
@@ -545,6 +552,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     // (two MMAs each); the F16 and Q8_0 paths never touch qlo.
     uint32_t  qlo[kBF16 ? KS : 1][4];
     int       mslot[2];  // mask slot (staged row) of fragment rows g and g+8
+    int       vlo[2], vhi[2];  // mask rule: visible keys [vlo, vhi) of rows g and g+8
     float     slope[2];
 
     auto setup_unit = [&](int u) {
@@ -569,6 +577,9 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                                     : nullptr;
             mslot[i] = o.m_ne2 == 1 ? iq - (uc.rb * kDecRows) / o.G : (rr < uc.rows ? rr : 0);
             slope[i] = alibi_slope(o, hq);
+            if (o.mg_kind) {
+                mg_range(o, uc.b, iq, vlo[i], vhi[i]);
+            }
         }
         auto qv = [&](int i, int d) -> float { return qrow[i] ? __ldg(qrow[i] + d) : 0.0f; };
 #pragma unroll
@@ -685,6 +696,9 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                         const float mv = slope[i] * __half2float(__ushort_as_half(
                                                         sM[mslot[i] * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1)]));
                         x              = mv == -INFINITY ? -INFINITY : x + mv;
+                    } else if (o.mg_kind) {
+                        // a visible key adds the rule's 0 like a 0 mask entry
+                        x = pos >= vlo[i] && pos < vhi[i] ? x + 0.0f : -INFINITY;
                     }
                     x *= kLog2e;
                 } else {

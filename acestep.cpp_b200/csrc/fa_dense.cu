@@ -102,13 +102,40 @@ __global__ void __launch_bounds__(256) fa_mask_classify(const __grid_constant__ 
     pdl_launch_dependents();
 }
 
+// Class of (row tile t, key tile kt) under a mask rule: the classes the
+// classify pass gives the equivalent 0 / -inf mask (dead, all visible, or
+// binary), from the rows' visible key ranges alone.
+__device__ __forceinline__ uint8_t rule_class(const OpDesc &o, int b, int t, int kt, int rows_total) {
+    const int gr0 = t * kDenseBM;
+    const int gr1 = min(rows_total, gr0 + kDenseBM) - 1;
+    const int j0 = kt * kDenseBN, j1 = min(o.n_kv, j0 + kDenseBN);
+    int       lo0, hi0, lo1, hi1;
+    mg_range(o, b, gr0 / o.G, lo0, hi0);
+    mg_range(o, b, gr1 / o.G, lo1, hi1);
+    if (max(lo0, j0) >= min(hi1, j1)) {
+        return 0;
+    }
+    return lo1 <= j0 && hi0 >= j1 ? kClsLive : (uint8_t) (kClsLive | kClsMask | kClsBinary);
+}
+
+// Bits [a, b) of a 32-bit word (a, b clipped to 0..32).
+__device__ __forceinline__ uint32_t range_bits(int a, int b) {
+    a = max(a, 0);
+    b = min(b, 32);
+    if (a >= b) {
+        return 0u;
+    }
+    return (b >= 32 ? ~0u : ((1u << b) - 1u)) & ~((1u << a) - 1u);
+}
+
 // ---------------------------------------------------------------------------
 // Softmax helpers of one row (thread) over one 128-key tile held in TMEM.
 
 // Bit k of vis[k/32] = key j0+k visible: inside n_kv and (for binary-mask
-// tiles) a mask entry that is not -inf.
+// tiles) a mask entry that is not -inf, or under a mask rule (rule set) inside
+// the row's visible range [vlo, vhi).
 __device__ __forceinline__ void build_visibility(uint32_t (&vis)[4], uint8_t c, const uint16_t *mrow, int j0,
-                                                 int n_kv, int m_ne0) {
+                                                 int n_kv, int m_ne0, bool rule, int vlo, int vhi) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
         uint32_t bits = ~0u;
@@ -116,7 +143,9 @@ __device__ __forceinline__ void build_visibility(uint32_t (&vis)[4], uint8_t c, 
             const int room = n_kv - (j0 + 32 * w);
             bits           = room >= 32 ? ~0u : (room <= 0 ? 0u : ((1u << room) - 1u));
         }
-        if (c & kClsMask) {
+        if ((c & kClsMask) && rule) {
+            bits &= range_bits(vlo - (j0 + 32 * w), vhi - (j0 + 32 * w));
+        } else if (c & kClsMask) {
             const uint16_t *mp = mrow + j0 + 32 * w;
             uint32_t        mb = 0;
             if ((reinterpret_cast<uintptr_t>(mp) & 15u) == 0 && j0 + 32 * w + 32 <= m_ne0) {
@@ -385,6 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (has_tile[i] && j >= kt_lo && j < kt_hi) {
                 if (P.cls) {
                     c = P.cls[((int64_t) (b % o.m_ne3) * P.n_rt + t0 + i) * P.n_kt + j];
+                } else if (o.mg_kind) {
+                    c = rule_class(o, b, t0 + i, j, P.rows_total);
                 } else {
                     c = kClsLive | (o.mask ? kClsMask : 0);
                 }
@@ -667,6 +698,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                       (int64_t) (hq % o.m_ne2) * o.m_nb2 +
                                                       (int64_t) (b % o.m_ne3) * o.m_nb3);
         }
+        // mask rule: this row's visible keys [vlo, vhi)
+        const bool rule = o.mg_kind != 0;
+        int        vlo = 0, vhi = 0;
+        if (rule) {
+            mg_range(o, b, iq, vlo, vhi);
+        }
         const float slope = alibi_slope(o, hq);
         // softcap or a non-positive scale take the general path on every tile
         const bool  general    = o.softcap != 0.0f || !(o.scale_eff > 0.0f);
@@ -732,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool use_vis = (c & (kClsMask | kClsBounds)) != 0;
                 uint32_t   vis[4]  = {~0u, ~0u, ~0u, ~0u};
                 if (use_vis) {
-                    build_visibility(vis, c, mrow, j0, o.n_kv, o.m_ne0);
+                    build_visibility(vis, c, mrow, j0, o.n_kv, o.m_ne0, rule, vlo, vhi);
                 }
                 float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 if (__any_sync(0xffffffffu, m_run == -INFINITY)) {
@@ -784,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tS + 32 * ch, x);
                     tmem_ld_wait32(x);
                     uint16_t mk[32];
-                    if (c & kClsMask) {
+                    if ((c & kClsMask) && !rule) {
                         const uint16_t *mp = mrow + j0 + 32 * ch;
                         if ((reinterpret_cast<uintptr_t>(mp) & 15u) == 0 && j0 + 32 * ch + 32 <= o.m_ne0) {
 #pragma unroll
@@ -810,7 +847,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (o.softcap != 0.0f) {
                             v = o.softcap * tanhf(v);
                         }
-                        if (c & kClsMask) {
+                        if ((c & kClsMask) && rule) {
+                            // a visible key adds the rule's 0 like a 0 mask entry
+                            const int jj = j0 + 32 * ch + e;
+                            v            = jj >= vlo && jj < vhi ? v + 0.0f : -INFINITY;
+                        } else if (c & kClsMask) {
                             const float mv = slope * __half2float(__ushort_as_half(mk[e]));
                             v              = mv == -INFINITY ? -INFINITY : v + mv;
                         }

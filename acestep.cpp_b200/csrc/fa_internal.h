@@ -25,6 +25,11 @@ struct OpDesc {
     const char *mask;
     int64_t     m_nb1, m_nb2, m_nb3;
     int         m_ne0, m_ne2, m_ne3;
+    // mask given by rule (acefa_flash_attn_ext_gen): mg_kind != 0 replaces
+    // `mask` (which is then null); see acefa_mask_gen
+    int     mg_kind, mg_window;
+    int64_t mg_pos0[ACEFA_MASK_GEN_MAX_BATCH];
+    int64_t mg_len[ACEFA_MASK_GEN_MAX_BATCH];
     // sinks [Hq] f32 (nullptr = none)
     const float *sinks;
     // dst [D, Hq, n_q, B] f32
@@ -44,6 +49,27 @@ struct OpDesc {
     float max_bias, alibi_m0, alibi_m1;
     int   n_head_log2;
 };
+
+// Keys visible to query iq of batch b under the mask rule (mg_kind != 0):
+// [lo, hi), clipped to [0, n_kv].  lo and hi never decrease with iq, so the
+// keys visible to some query of a run iq0..iq1 are [lo(iq0), hi(iq1)) and the
+// keys visible to all of them [lo(iq1), hi(iq0)).  The host clamps pos0 and
+// len into [-(n_q + 1), n_kv], which keeps every sum below in range.
+__host__ __device__ inline void mg_range(const OpDesc &o, int b, int iq, int &lo, int &hi) {
+    int64_t l = 0, h = o.n_kv;
+    if (o.mg_kind == ACEFA_MASK_CAUSAL) {
+        h = o.mg_pos0[b] + iq + 1;
+    } else if (o.mg_kind == ACEFA_MASK_WINDOW) {
+        l = (int64_t) iq - o.mg_window;
+        h = (int64_t) iq + o.mg_window + 1;
+    } else {
+        h = o.mg_len[b];
+    }
+    l  = l < 0 ? 0 : (l > o.n_kv ? o.n_kv : l);
+    h  = h < 0 ? 0 : (h > o.n_kv ? o.n_kv : h);
+    lo = (int) l;
+    hi = (int) h;
+}
 
 __host__ __device__ inline float alibi_slope(const OpDesc &o, int h) {
     if (o.max_bias <= 0.0f) {

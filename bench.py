@@ -395,25 +395,32 @@ def extras(device, stream, args):
         # config 1: one Qwen3-0.6B decode op (8.4 MB), many back-to-back in a graph
         import acefa
 
-        g = torch.Generator(device=device).manual_seed(42 + 1000)
         reps = 64
-        ops = []
-        for _ in range(reps):
-            q = torch.randn(1, 16, 1, D, device=device, generator=g)
-            k = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
-            v = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
-            m = torch.zeros(1, 1, 1, 2048, device=device, dtype=torch.float16)
-            ops.append(acefa.Op(q, k, v, mask=m, scale=D ** -0.5))
-        graph = time_graph(ops, 10, 3, stream)
-        s0.record(stream)
-        for _ in range(10):
-            graph.replay()
-        s1.record(stream)
-        torch.cuda.synchronize()
-        us = s0.elapsed_time(s1) * 1e3 / (10 * reps)
         b1 = 8_409_088
-        res["config1_single_op"] = {"us_per_op": round(us, 2), "gbs": round(b1 / (us / 1e6) / 1e9, 1),
-                                    "note": "64 distinct ops back to back in one CUDA graph (8.4 MB each)"}
+        for key, rule in (("config1_single_op", False), ("config1_single_op_rule", True)):
+            g = torch.Generator(device=device).manual_seed(42 + 1000)
+            ops = []
+            for _ in range(reps):
+                q = torch.randn(1, 16, 1, D, device=device, generator=g)
+                k = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
+                v = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
+                if rule:  # the same visibility (keys 0 .. 2047) by rule: no mask read
+                    ops.append(acefa.Op(q, k, v, mask_gen=acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[2047]),
+                                        scale=D ** -0.5))
+                else:
+                    m = torch.zeros(1, 1, 1, 2048, device=device, dtype=torch.float16)
+                    ops.append(acefa.Op(q, k, v, mask=m, scale=D ** -0.5))
+            graph = time_graph(ops, 10, 3, stream)
+            s0.record(stream)
+            for _ in range(10):
+                graph.replay()
+            s1.record(stream)
+            torch.cuda.synchronize()
+            us = s0.elapsed_time(s1) * 1e3 / (10 * reps)
+            res[key] = {"us_per_op": round(us, 2), "gbs": round(b1 / (us / 1e6) / 1e9, 1),
+                        "note": "64 distinct ops back to back in one CUDA graph (8.4 MB each)" +
+                                ("; mask by rule" if rule else "")}
+            del graph, ops
         res["config1_append"] = append_step(device, stream)
     return res
 
@@ -535,7 +542,8 @@ def dense_pairs(S_q, S_kv, kind, extra):
     raise ValueError(kind)
 
 
-def build_dense(device, name, seed=SEED + 3):
+def build_dense(device, name, seed=SEED + 3, rule=False):
+    """The workload's op; rule=True gives its mask by rule (acefa_flash_attn_ext_gen)."""
     import torch
 
     import acefa
@@ -556,17 +564,23 @@ def build_dense(device, name, seed=SEED + 3):
         else:
             vis = (kj < extra).expand(S_q, S_kv)
         mask = torch.where(vis, 0.0, float("-inf")).half().reshape(1, 1, S_q, S_kv).contiguous()
-    op = acefa.Op(q, k, v, mask=mask, scale=D ** -0.5)
+    if rule and kind is not None:
+        mg = {"causal": lambda: acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[S_kv - S_q] * B),
+              "window": lambda: acefa.mask_gen(acefa.MASK_WINDOW, window=extra),
+              "padding": lambda: acefa.mask_gen(acefa.MASK_PADDING, lens=[extra] * B)}[kind]()
+        op = acefa.Op(q, k, v, mask_gen=mg, scale=D ** -0.5)
+    else:
+        op = acefa.Op(q, k, v, mask=mask, scale=D ** -0.5)
     flops = 4 * D * dense_pairs(S_q, S_kv, kind, extra) * Hq * B
     return op, flops
 
 
-def time_dense(device, stream, name, iters=10, warmup=3):
+def time_dense(device, stream, name, iters=10, warmup=3, rule=False):
     import torch
 
     import acefa
 
-    op, flops = build_dense(device, name)
+    op, flops = build_dense(device, name, rule=rule)
     with torch.cuda.stream(stream):
         op(stream=stream)
         path = acefa.last_path()
@@ -598,6 +612,13 @@ def dense_extras(device, stream):
         r = time_dense(device, stream, name)
         r["frac_of_peak"] = round(r["tflops"] / peak, 4)
         res[name] = r
+    # the masked workloads again with the mask given by rule (no mask tensor,
+    # no classification pass)
+    for name, wl in DENSE_WORKLOADS.items():
+        if wl[5] is not None:
+            r = time_dense(device, stream, name, rule=True)
+            r["frac_of_peak"] = round(r["tflops"] / peak, 4)
+            res[name + "_rule"] = r
     return res
 
 

@@ -172,6 +172,50 @@ ACEFA_API int acefa_flash_attn_ext_append(const acefa_tensor *q, const acefa_ten
                                           const int64_t *pos, void *stream, void *workspace, size_t workspace_bytes);
 
 /*
+ * A mask given by its rule instead of an f16 tensor.  acestep.cpp fills these
+ * masks on the host and the attention node reads them back from HBM: the LM
+ * prefill causal mask (src/qwen3-lm.h:597-609), the batched decode validity
+ * mask (src/qwen3-lm.h:872-881), the DiT sliding window sa_mask_sw and the
+ * cross-attention padding ca_mask (src/dit-sampler.h:262-311).
+ * Key j is visible to query i (0-based within n_q) of batch b when
+ *   ACEFA_MASK_CAUSAL   j <= pos0[b] + i   (LM prefill with the cache holding
+ *                       pos0 earlier tokens; a decode step is i = 0, keys
+ *                       0 .. kv_pos)
+ *   ACEFA_MASK_WINDOW   |i - j| <= window  (DiT self-attention, sliding-window
+ *                       layers; where the reference's window is off -- win <= 0
+ *                       or S <= win -- the node is unmasked: pass no mask)
+ *   ACEFA_MASK_PADDING  j < len[b]         (DiT cross-attention padding)
+ * Visible keys add 0 and hidden keys -inf, exactly as the equivalent f16
+ * mask would; results are bit-identical to acefa_flash_attn_ext with that mask.
+ * pos0 / len are read for b < B (at most ACEFA_MASK_GEN_MAX_BATCH batches).
+ */
+#define ACEFA_MASK_GEN_MAX_BATCH 32
+typedef enum acefa_mask_kind {
+    ACEFA_MASK_CAUSAL  = 1,
+    ACEFA_MASK_WINDOW  = 2,
+    ACEFA_MASK_PADDING = 3,
+} acefa_mask_kind;
+
+typedef struct acefa_mask_gen {
+    int32_t kind;    /* acefa_mask_kind */
+    int32_t window;  /* ACEFA_MASK_WINDOW */
+    int64_t pos0[ACEFA_MASK_GEN_MAX_BATCH];  /* ACEFA_MASK_CAUSAL */
+    int64_t len[ACEFA_MASK_GEN_MAX_BATCH];   /* ACEFA_MASK_PADDING */
+} acefa_mask_gen;
+
+/* acefa_flash_attn_ext() with the mask given by rule (mask_gen, host memory,
+ * read during the call) instead of a tensor: no mask is read on the device and
+ * the dense path needs no mask-classification pass.  The rule is copied into
+ * the launch, so mask_gen may be reused or freed once the call returns.
+ * acefa_workspace_bytes(q, k, v, NULL, dst) is enough workspace.  Returns
+ * ACEFA_ERR_SHAPE for an unknown kind, B > ACEFA_MASK_GEN_MAX_BATCH with a
+ * per-batch kind (CAUSAL, PADDING), or a negative window. */
+ACEFA_API int acefa_flash_attn_ext_gen(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                       const acefa_mask_gen *mask_gen, const acefa_tensor *sinks,
+                                       const acefa_tensor *dst, float scale, float max_bias, float logit_softcap,
+                                       int prec, void *stream, void *workspace, size_t workspace_bytes);
+
+/*
  * CUDA IPC through the ABI, so a host without CUDA bindings can map peer
  * buffers.  acefa_peer_export: an opaque handle (ACEFA_PEER_HANDLE_BYTES bytes)
  * for the allocation holding ptr, plus ptr's byte offset inside it.

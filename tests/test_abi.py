@@ -187,6 +187,27 @@ def test_append_entry_validates_before_launch(lib):
         assert call(kn, vn, 4096) in (-6, -7)         # valid: fails only at the device step
 
 
+def test_mask_rule_entry_validates_before_launch(lib):
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    q, k, v, m, d = _ops(Hq=32, B=4, Bk=4, nkv=700)
+
+    def call(mg):
+        return lib.acefa_flash_attn_ext_gen(r(q), r(k), r(v), r(mg), None, r(d), 0.088, 0.0, 0.0, 10, None, None, 0)
+
+    assert call(None) == -1                                                # no rule
+    assert call(acefa.mask_gen(0)) == -3                                   # unknown kind
+    assert call(acefa.mask_gen(acefa.MASK_WINDOW, window=-1)) == -3        # negative window
+    q40, k40, v40, m40, d40 = _ops(Hq=32, B=40, Bk=40, nkv=700)
+    mg = acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[5] * 32)
+    assert lib.acefa_flash_attn_ext_gen(r(q40), r(k40), r(v40), r(mg), None, r(d40), 0.088, 0.0, 0.0, 10,
+                                        None, None, 0) == -3               # per-batch rule past 32 sets
+    if not torch.cuda.is_available():
+        assert call(mg) in (-6, -7)                                        # valid: fails only at the device step
+        w = acefa.mask_gen(acefa.MASK_WINDOW, window=4)
+        assert lib.acefa_flash_attn_ext_gen(r(q40), r(k40), r(v40), r(w), None, r(d40), 0.088, 0.0, 0.0, 10,
+                                            None, None, 0) in (-6, -7)     # window: any batch count
+
+
 def test_peer_entry_points_reject_null(lib):
     assert lib.acefa_peer_export(None, None, None) == -1
     assert lib.acefa_peer_import(None, 0, None) == -1
