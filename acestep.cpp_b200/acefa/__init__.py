@@ -48,6 +48,8 @@ EXPORTED_SYMBOLS = (
     "acefa_peer_release",
     "acefa_flash_attn_ext_append",
     "acefa_flash_attn_ext_gen",
+    "acefa_flash_attn_ext_fused",
+    "acefa_kv_prologue",
 )
 
 MAX_MIRRORS = 7
@@ -91,6 +93,34 @@ def rule_mask(m: MaskGen, B: int, n_q: int, n_kv: int, ne0: int | None = None, d
     out = torch.full((B, 1, n_q, ne0), float("-inf"), dtype=torch.float16)
     out[:, 0][vis] = 0.0
     return out.to(device)
+
+
+class RopeNormC(ctypes.Structure):
+    """acefa_rope_norm: RMSNorm (times a weight) + RoPE NEOX of rows of D values."""
+    _fields_ = [("norm_weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("theta_base", ctypes.c_float),
+                ("positions", ctypes.c_void_p)]
+
+
+class RopeNorm:
+    """A prologue description that keeps its device tensors alive.
+    weight: (D,) f32 CUDA tensor or None; positions: int32 CUDA tensor or None."""
+
+    def __init__(self, weight=None, eps=1e-6, theta=0.0, positions=None):
+        if positions is not None and (positions.dtype != torch.int32 or not positions.is_cuda):
+            raise ValueError("positions: int32 CUDA tensor (ggml's positions)")
+        if weight is not None and (weight.dtype != torch.float32 or not weight.is_cuda or not weight.is_contiguous()):
+            raise ValueError("weight: contiguous f32 CUDA tensor")
+        self.weight, self.positions = weight, positions
+        self.eps, self.theta = float(eps), float(theta)
+        self.c = RopeNormC(weight.data_ptr() if weight is not None else None, self.eps, self.theta,
+                           positions.data_ptr() if positions is not None else None)
+
+
+class OpExt(ctypes.Structure):
+    """acefa_op_ext."""
+    _fields_ = [("mask_gen", ctypes.c_void_p), ("q_prologue", ctypes.c_void_p), ("k_new", ctypes.c_void_p),
+                ("v_new", ctypes.c_void_p), ("append_pos", ctypes.c_void_p), ("k_prologue", ctypes.c_void_p),
+                ("mirrors", ctypes.c_void_p), ("n_mirrors", ctypes.c_int)]
 
 
 class AcefaError(RuntimeError):
@@ -154,6 +184,12 @@ def load_library(path: str | None = None):
                                              ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_size_t]
     lib.acefa_flash_attn_ext_gen.restype = ctypes.c_int
+    lib.acefa_flash_attn_ext_fused.argtypes = [T, T, T, T, T, T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                               ctypes.c_int, ctypes.POINTER(OpExt), ctypes.c_void_p,
+                                               ctypes.c_void_p, ctypes.c_size_t]
+    lib.acefa_flash_attn_ext_fused.restype = ctypes.c_int
+    lib.acefa_kv_prologue.argtypes = [T, T, T, T, ctypes.POINTER(RopeNormC), ctypes.c_void_p]
+    lib.acefa_kv_prologue.restype = ctypes.c_int
     lib.acefa_peer_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
     lib.acefa_peer_export.restype = ctypes.c_int
     lib.acefa_peer_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
@@ -225,7 +261,7 @@ class Op:
 
     def __init__(self, q, k, v, mask=None, sinks=None, out=None, kv_type=None, scale=None,
                  max_bias=0.0, softcap=0.0, prec=PREC_F32, mirrors=(), k_new=None, v_new=None, pos=None,
-                 mask_gen=None):
+                 mask_gen=None, q_prologue=None, k_prologue=None):
         self.lib = load_library()
         self.q, self.k, self.v, self.mask, self.sinks = q, k, v, mask, sinks
         D = q.shape[-1]
@@ -257,13 +293,40 @@ class Op:
             self.tkn, self.tvn = describe(k_new), describe(v_new)
         # mask by rule (MaskGen) instead of a mask tensor
         self.mask_gen = mask_gen
-        if mask_gen is not None and (mask is not None or k_new is not None or mirrors):
-            raise ValueError("mask_gen replaces mask and does not combine with append or mirrors")
+        if mask_gen is not None and mask is not None:
+            raise ValueError("mask_gen replaces mask")
         # mirrors: device addresses laid out like `out` (e.g. peer GPUs' buffers)
         self.n_mirrors = len(mirrors)
         self.mirrors = (ctypes.c_void_p * max(1, self.n_mirrors))(*[int(m) for m in mirrors])
+        # RMSNorm + RoPE prologues (RopeNorm): Q rows, the appended K row
+        self.q_prologue, self.k_prologue = q_prologue, k_prologue
+        used = [mask_gen is not None, self.append, self.n_mirrors > 0, q_prologue is not None,
+                k_prologue is not None]
+        self.fused = q_prologue is not None or k_prologue is not None or sum(used) > 1
+        if self.fused:
+            self.ext = OpExt()
+            if mask_gen is not None:
+                self.ext.mask_gen = ctypes.addressof(mask_gen)
+            if q_prologue is not None:
+                self.ext.q_prologue = ctypes.addressof(q_prologue.c)
+            if k_prologue is not None:
+                self.ext.k_prologue = ctypes.addressof(k_prologue.c)
+            if self.append:
+                self.ext.k_new, self.ext.v_new = ctypes.addressof(self.tkn), ctypes.addressof(self.tvn)
+                self.ext.append_pos = self.pos.data_ptr()
+            if self.n_mirrors:
+                self.ext.mirrors, self.ext.n_mirrors = ctypes.addressof(self.mirrors), self.n_mirrors
 
     def __call__(self, stream=None):
+        if self.fused:
+            st = self.lib.acefa_flash_attn_ext_fused(
+                _ref(self.tq), _ref(self.tk), _ref(self.tv), _ref(self.tm), _ref(self.ts), _ref(self.td),
+                self.scale, self.max_bias, self.softcap, self.prec, ctypes.byref(self.ext),
+                ctypes.c_void_p(_stream_ptr(stream)), ctypes.c_void_p(self.workspace.data_ptr()),
+                ctypes.c_size_t(self.workspace.numel()))
+            if st != OK:
+                raise AcefaError(st, "acefa_flash_attn_ext_fused")
+            return self.out
         if self.mask_gen is not None:
             st = self.lib.acefa_flash_attn_ext_gen(
                 _ref(self.tq), _ref(self.tk), _ref(self.tv), ctypes.byref(self.mask_gen), _ref(self.ts),
@@ -365,6 +428,18 @@ def last_path() -> int:
 
 
 # --------------------------------------------------------------------------
+def kv_prologue(k_src, k_dst, v_src=None, v_dst=None, prologue: RopeNorm | None = None, stream=None):
+    """acefa_kv_prologue: k_dst = RoPE(RMSNorm(k_src)), v_dst = v_src, converted
+    to k_dst's type (f16 / bf16).  Torch shapes (B, H, rows, D), any strides."""
+    lib = load_library()
+    st = lib.acefa_kv_prologue(_ref(describe(k_src)), _ref(describe(v_src)), _ref(describe(k_dst)),
+                               _ref(describe(v_dst)), ctypes.byref(prologue.c) if prologue is not None else None,
+                               ctypes.c_void_p(_stream_ptr(stream)))
+    if st != OK:
+        raise AcefaError(st, "acefa_kv_prologue")
+    return k_dst, v_dst
+
+
 # input preparation helpers (torch ops; not on the attention path)
 
 def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:

@@ -7,6 +7,7 @@
 // ggml type in the signature.  Status codes replace ggml's GGML_ABORT.
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 
@@ -353,29 +354,95 @@ static int rc_of_rule(OpDesc &o, const acefa_mask_gen *mg) {
     return ACEFA_OK;
 }
 
-// The operator with optional mirrors (acefa_flash_attn_ext_mirrored) and an
-// optional fused KV-cache append (acefa_flash_attn_ext_append).
+// New K/V rows of a fused KV-cache append.
 struct AppendArgs {
     const char    *k_new, *v_new;
     int64_t        kn_nb2, kn_nb3, vn_nb2, vn_nb3;
     const int64_t *pos;
 };
 
+// RMSNorm + RoPE parameters for the kernels.  inv_freq[k] = theta_base^(-2k/D)
+// is computed here, once, with the C library's powf.
+static int fill_rope_norm(RopeNorm &r, const acefa_rope_norm *p, int D) {
+    std::memset(&r, 0, sizeof(r));
+    if (!p) {
+        return ACEFA_OK;
+    }
+    if (!std::isfinite(p->eps) || p->eps < 0.0f || !std::isfinite(p->theta_base) || p->theta_base < 0.0f ||
+        D / 2 > kRopeMaxPairs || D % 64) {
+        return ACEFA_ERR_SHAPE;
+    }
+    if (p->theta_base > 0.0f && !p->positions) {
+        return ACEFA_ERR_NULL;
+    }
+    if (!aligned(p->norm_weight, 4) || !aligned(p->positions, 4)) {
+        return ACEFA_ERR_LAYOUT;
+    }
+    r.on   = 1;
+    r.rope = p->theta_base > 0.0f;
+    r.w    = p->norm_weight;
+    r.pos  = p->positions;
+    r.eps  = p->eps;
+    for (int k = 0; k < D / 2; ++k) {
+        r.inv_freq[k] = r.rope ? std::pow(p->theta_base, -(float) (2 * k) / (float) D) : 0.0f;
+    }
+    return ACEFA_OK;
+}
+
+// The operator with any of the fusions of acefa_op_ext.
 static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v, const acefa_tensor *mask,
                   const acefa_tensor *sinks, const acefa_tensor *dst, float scale, float max_bias,
-                  float logit_softcap, int prec, void *const *mirrors, int n_mirrors, const AppendArgs *app,
-                  const acefa_mask_gen *mg, void *stream, void *workspace, size_t workspace_bytes) {
+                  float logit_softcap, int prec, const acefa_op_ext *ext, void *stream, void *workspace,
+                  size_t workspace_bytes) {
     (void) prec;  // accumulation is F32 for both GGML_PREC_DEFAULT and GGML_PREC_F32
+    static const acefa_op_ext kNone = {};
+    const acefa_op_ext       &x     = ext ? *ext : kNone;
     Checked c = check_operands(q, k, v, mask, sinks, dst);
     if (c.status != ACEFA_OK) {
         return c.status;
     }
-    if (mg && (rc_of_rule(c.op, mg) != ACEFA_OK)) {
+    if (x.mask_gen && (mask || rc_of_rule(c.op, x.mask_gen) != ACEFA_OK)) {
         return ACEFA_ERR_SHAPE;
     }
     if (!std::isfinite(scale) || !std::isfinite(max_bias) || !std::isfinite(logit_softcap) || max_bias < 0.0f) {
         return ACEFA_ERR_SHAPE;
     }
+    int rc = fill_rope_norm(c.op.qp, x.q_prologue, c.op.D);
+    if (rc != ACEFA_OK) {
+        return rc;
+    }
+    // fused KV append: new rows [D, 1, Hkv, Bk] f32, one cache row per set
+    AppendArgs        app_args{};
+    const AppendArgs *app = nullptr;
+    RopeNorm          kp;
+    if (x.k_new || x.v_new || x.append_pos) {
+        const acefa_tensor *kn = x.k_new, *vn = x.v_new;
+        if (!kn || !vn || !x.append_pos || !kn->data || !vn->data) {
+            return ACEFA_ERR_NULL;
+        }
+        if (kn->type != ACEFA_TYPE_F32 || vn->type != ACEFA_TYPE_F32) {
+            return ACEFA_ERR_TYPE;
+        }
+        for (const acefa_tensor *t : {kn, vn}) {
+            if (t->ne[0] != k->ne[0] || t->ne[1] != 1 || t->ne[2] != k->ne[2] || t->ne[3] != k->ne[3]) {
+                return ACEFA_ERR_SHAPE;
+            }
+            if (t->nb[0] != 4 || t->nb[2] % 4 || t->nb[3] % 4 || !aligned(t->data, 4)) {
+                return ACEFA_ERR_LAYOUT;
+            }
+        }
+        app_args = AppendArgs{static_cast<const char *>(kn->data), static_cast<const char *>(vn->data),
+                              (int64_t) kn->nb[2], (int64_t) kn->nb[3], (int64_t) vn->nb[2], (int64_t) vn->nb[3],
+                              x.append_pos};
+        app      = &app_args;
+    } else if (x.k_prologue) {
+        return ACEFA_ERR_SHAPE;  // the K prologue applies to the appended row
+    }
+    if ((rc = fill_rope_norm(kp, x.k_prologue, c.op.D)) != ACEFA_OK) {
+        return rc;
+    }
+    void *const *mirrors   = x.mirrors;
+    const int    n_mirrors = x.n_mirrors;
     if (n_mirrors < 0 || n_mirrors > ACEFA_MAX_MIRRORS || (n_mirrors > 0 && !mirrors)) {
         return n_mirrors > 0 && !mirrors ? ACEFA_ERR_NULL : ACEFA_ERR_SHAPE;
     }
@@ -392,8 +459,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
     }
     c.op.n_mirror = n_mirrors;
     DevInfo *di = nullptr;
-    int      rc = dev_info(&di);
-    if (rc != ACEFA_OK) {
+    if ((rc = dev_info(&di)) != ACEFA_OK) {
         return rc;
     }
     set_scalars(c.op, scale, max_bias, logit_softcap);
@@ -458,6 +524,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         L.p.vn_nb2     = app->vn_nb2;
         L.p.vn_nb3     = app->vn_nb3;
         L.p.append_pos = app->pos;
+        L.p.kp         = kp;
     }
     L.p.partials       = static_cast<float *>(workspace);
     L.p.dev_err        = di->err_ptr;
@@ -510,8 +577,8 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
                                    const acefa_tensor *mask, const acefa_tensor *sinks, const acefa_tensor *dst,
                                    float scale, float max_bias, float logit_softcap, int prec, void *stream,
                                    void *workspace, size_t workspace_bytes) {
-    return acefa_flash_attn_ext_mirrored(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0,
-                                         stream, workspace, workspace_bytes);
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, stream, workspace,
+                  workspace_bytes);
 }
 
 ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
@@ -519,8 +586,11 @@ ACEFA_API int acefa_flash_attn_ext_mirrored(const acefa_tensor *q, const acefa_t
                                             const acefa_tensor *dst, float scale, float max_bias,
                                             float logit_softcap, int prec, void *const *mirrors, int n_mirrors,
                                             void *stream, void *workspace, size_t workspace_bytes) {
-    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, mirrors, n_mirrors, nullptr, nullptr,
-                  stream, workspace, workspace_bytes);
+    acefa_op_ext x = {};
+    x.mirrors      = mirrors;
+    x.n_mirrors    = n_mirrors;
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, &x, stream, workspace,
+                  workspace_bytes);
 }
 
 ACEFA_API int acefa_flash_attn_ext_append(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
@@ -529,24 +599,15 @@ ACEFA_API int acefa_flash_attn_ext_append(const acefa_tensor *q, const acefa_ten
                                           int prec, const acefa_tensor *k_new, const acefa_tensor *v_new,
                                           const int64_t *pos, void *stream, void *workspace,
                                           size_t workspace_bytes) {
-    if (!k_new || !v_new || !pos || !k_new->data || !v_new->data || !k || !v) {
+    if (!k_new || !v_new || !pos) {
         return ACEFA_ERR_NULL;
     }
-    if (k_new->type != ACEFA_TYPE_F32 || v_new->type != ACEFA_TYPE_F32) {
-        return ACEFA_ERR_TYPE;
-    }
-    for (const acefa_tensor *t : {k_new, v_new}) {
-        if (t->ne[0] != k->ne[0] || t->ne[1] != 1 || t->ne[2] != k->ne[2] || t->ne[3] != k->ne[3]) {
-            return ACEFA_ERR_SHAPE;
-        }
-        if (t->nb[0] != 4 || t->nb[2] % 4 || t->nb[3] % 4 || !aligned(t->data, 4)) {
-            return ACEFA_ERR_LAYOUT;
-        }
-    }
-    AppendArgs a{static_cast<const char *>(k_new->data), static_cast<const char *>(v_new->data),
-                 (int64_t) k_new->nb[2], (int64_t) k_new->nb[3], (int64_t) v_new->nb[2], (int64_t) v_new->nb[3], pos};
-    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0, &a, nullptr, stream,
-                  workspace, workspace_bytes);
+    acefa_op_ext x = {};
+    x.k_new        = k_new;
+    x.v_new        = v_new;
+    x.append_pos   = pos;
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, &x, stream, workspace,
+                  workspace_bytes);
 }
 
 ACEFA_API int acefa_flash_attn_ext_gen(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
@@ -556,8 +617,68 @@ ACEFA_API int acefa_flash_attn_ext_gen(const acefa_tensor *q, const acefa_tensor
     if (!mask_gen) {
         return ACEFA_ERR_NULL;
     }
-    return run_op(q, k, v, nullptr, sinks, dst, scale, max_bias, logit_softcap, prec, nullptr, 0, nullptr, mask_gen,
-                  stream, workspace, workspace_bytes);
+    acefa_op_ext x = {};
+    x.mask_gen     = mask_gen;
+    return run_op(q, k, v, nullptr, sinks, dst, scale, max_bias, logit_softcap, prec, &x, stream, workspace,
+                  workspace_bytes);
+}
+
+ACEFA_API int acefa_flash_attn_ext_fused(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                         const acefa_tensor *mask, const acefa_tensor *sinks,
+                                         const acefa_tensor *dst, float scale, float max_bias,
+                                         float logit_softcap, int prec, const acefa_op_ext *ext, void *stream,
+                                         void *workspace, size_t workspace_bytes) {
+    return run_op(q, k, v, mask, sinks, dst, scale, max_bias, logit_softcap, prec, ext, stream, workspace,
+                  workspace_bytes);
+}
+
+ACEFA_API int acefa_kv_prologue(const acefa_tensor *k_src, const acefa_tensor *v_src, const acefa_tensor *k_dst,
+                                const acefa_tensor *v_dst, const acefa_rope_norm *k_prologue, void *stream) {
+    if (!k_src || !k_dst || !k_src->data || !k_dst->data || (!v_src != !v_dst) ||
+        (v_src && (!v_src->data || !v_dst->data))) {
+        return ACEFA_ERR_NULL;
+    }
+    const acefa_tensor *src[2] = {k_src, v_src}, *dstt[2] = {k_dst, v_dst};
+    for (int i = 0; i < 2; ++i) {
+        if (!src[i]) {
+            continue;
+        }
+        if (src[i]->type != ACEFA_TYPE_F32 || dstt[i]->type != k_dst->type ||
+            (k_dst->type != ACEFA_TYPE_F16 && k_dst->type != ACEFA_TYPE_BF16)) {
+            return ACEFA_ERR_TYPE;
+        }
+        for (int d = 0; d < 4; ++d) {
+            if (src[i]->ne[d] <= 0 || src[i]->ne[d] != k_src->ne[d] || dstt[i]->ne[d] != k_src->ne[d]) {
+                return ACEFA_ERR_SHAPE;
+            }
+        }
+        if (src[i]->nb[0] != 4 || dstt[i]->nb[0] != 2 || !aligned(src[i]->data, 4) || !aligned(dstt[i]->data, 2)) {
+            return ACEFA_ERR_LAYOUT;
+        }
+        for (int d = 1; d < 4; ++d) {
+            if (src[i]->nb[d] % 4 || dstt[i]->nb[d] % 2) {
+                return ACEFA_ERR_LAYOUT;
+            }
+        }
+    }
+    const int64_t D = k_src->ne[0];
+    if ((D != 64 && D != 128) || k_src->ne[1] * k_src->ne[2] * k_src->ne[3] > INT32_MAX) {
+        return ACEFA_ERR_SHAPE;  // rows are numbered in 32 bits
+    }
+    RopeNorm kp;
+    int      rc = fill_rope_norm(kp, k_prologue, (int) D);
+    if (rc != ACEFA_OK) {
+        return rc;
+    }
+    DevInfo *di = nullptr;
+    if ((rc = dev_info(&di)) != ACEFA_OK) {
+        return rc;
+    }
+    rc = kv_prologue_launch(k_src, v_src, k_dst, v_dst, kp, di->sm_count, static_cast<cudaStream_t>(stream));
+    if (rc == ACEFA_OK) {
+        t_last_launches = 1;
+    }
+    return rc;
 }
 
 ACEFA_API int acefa_device_error(void *stream) {

@@ -29,6 +29,7 @@
 
 #include "fa_internal.h"
 #include "ptx.cuh"
+#include "rope_norm.cuh"
 
 namespace acefa {
 
@@ -201,7 +202,7 @@ __device__ __forceinline__ int append_index(int lane, int k) {
     return KV_TYPE == ACEFA_TYPE_Q8_0 ? (lane >> 3) * 32 + (lane & 7) * 4 + k : lane + 32 * k;
 }
 
-template <int KV_TYPE, int D>
+template <int KV_TYPE, int D, bool PRO>
 __device__ __forceinline__ void append_load(const DecodeParams &P, int hk, int bk, int lane, float (&xk)[4],
                                             float (&xv)[4]) {
     const float *ks = reinterpret_cast<const float *>(P.k_new + (int64_t) hk * P.kn_nb2 + (int64_t) bk * P.kn_nb3);
@@ -212,6 +213,48 @@ __device__ __forceinline__ void append_load(const DecodeParams &P, int hk, int b
         const bool in = KV_TYPE == ACEFA_TYPE_Q8_0 ? (lane >> 3) < D / 32 : k < D / 32;
         xk[k]         = in ? ks[i] : 0.0f;
         xv[k]         = in ? vs[i] : 0.0f;
+    }
+    const RopeNorm &kp = P.kp;
+    if (PRO && kp.on) {
+        // QK-norm + RoPE of the new K row (values outside the row are 0)
+        if (kp.w) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                ss = fmaf(xk[k], xk[k], ss);
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) {
+                ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            }
+            const float sc = rn_scale(kp, ss, D);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const bool in = KV_TYPE == ACEFA_TYPE_Q8_0 ? (lane >> 3) < D / 32 : k < D / 32;
+                xk[k]         = in ? (xk[k] * sc) * __ldg(kp.w + append_index<KV_TYPE, D>(lane, k)) : 0.0f;
+            }
+        }
+        if (kp.rope) {
+            const int pos = __ldg(kp.pos + bk);
+            if constexpr (KV_TYPE == ACEFA_TYPE_Q8_0) {
+                // dim d + D/2 is D/64 blocks (8 lanes each) further: lane ^ (D/8)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int   d  = append_index<KV_TYPE, D>(lane, k);
+                    const float pt = __shfl_xor_sync(0xffffffffu, xk[k], D / 8);
+                    xk[k] = (lane >> 3) < D / 32 ? rn_rotate(kp, xk[k], pt, d < D / 2, pos, d & (D / 2 - 1)) : 0.0f;
+                }
+            } else {
+                // dim lane + 32k pairs with lane + 32(k + D/64): same lane
+#pragma unroll
+                for (int k = 0; k < D / 64; ++k) {
+                    const float a = xk[k], b = xk[k + D / 64];
+                    const int   d = append_index<KV_TYPE, D>(lane, k);
+                    xk[k]          = rn_rotate(kp, a, b, true, pos, d);
+                    xk[k + D / 64] = rn_rotate(kp, b, a, false, pos, d);
+                }
+            }
+        }
     }
 }
 
@@ -268,7 +311,9 @@ __device__ __forceinline__ void append_store(const DecodeParams &P, int64_t pr, 
     __syncwarp();
 }
 
-template <int KV_TYPE, int D>
+// PRO: the instance that applies the QK-norm + RoPE prologues (Q rows, the
+// appended K row); the others carry none of that code.
+template <int KV_TYPE, int D, bool PRO>
 __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     fa_decode_kernel(const __grid_constant__ DecodeParams P, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
@@ -387,7 +432,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     }
                 } else if (app_row / kDecBN >= tlo && app_row / kDecBN < thi) {
                     app_tile = (int) (app_row / kDecBN);
-                    append_load<KV_TYPE, D>(P, uc.hk, uc.bk, lane, app_k, app_v);
+                    append_load<KV_TYPE, D, PRO>(P, uc.hk, uc.bk, lane, app_k, app_v);
                 }
             }
             // Mask slots: the distinct mask rows this unit reads (one per query
@@ -567,6 +612,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             }
         }
         const float *qrow[2];
+        int          qpos[2] = {0, 0};  // RoPE positions of rows g and g+8 (Q prologue)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             const int rr = g + 8 * i;
@@ -580,24 +626,109 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             if (o.mg_kind) {
                 mg_range(o, uc.b, iq, vlo[i], vhi[i]);
             }
+            if (PRO && o.qp.rope && rr < uc.rows) {
+                qpos[i] = __ldg(o.qp.pos + iq + (int64_t) uc.b * o.n_q);
+            }
         }
-        auto qv = [&](int i, int d) -> float { return qrow[i] ? __ldg(qrow[i] + d) : 0.0f; };
+        if constexpr (!PRO) {
+            auto qv = [&](int i, int d) -> float { return qrow[i] ? __ldg(qrow[i] + d) : 0.0f; };
 #pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            if constexpr (kQ8) {
-                // dims permuted so each thread's K bytes are one contiguous run
-                const int d0 = c * (D / 4) + 4 * ks;
-                qa[ks][0]    = pack2<false>(qv(0, d0), qv(0, d0 + 1));
-                qa[ks][1]    = pack2<false>(qv(1, d0), qv(1, d0 + 1));
-                qa[ks][2]    = pack2<false>(qv(0, d0 + 2), qv(0, d0 + 3));
-                qa[ks][3]    = pack2<false>(qv(1, d0 + 2), qv(1, d0 + 3));
-            } else {
-                const int d0  = 16 * ks + 2 * c;
-                const int ii[4] = {0, 1, 0, 1};
-                const int dd[4] = {d0, d0, d0 + 8, d0 + 8};
+            for (int ks = 0; ks < KS; ++ks) {
+                if constexpr (kQ8) {
+                    // dims permuted so each thread's K bytes are one contiguous run
+                    const int d0 = c * (D / 4) + 4 * ks;
+                    qa[ks][0]    = pack2<false>(qv(0, d0), qv(0, d0 + 1));
+                    qa[ks][1]    = pack2<false>(qv(1, d0), qv(1, d0 + 1));
+                    qa[ks][2]    = pack2<false>(qv(0, d0 + 2), qv(0, d0 + 3));
+                    qa[ks][3]    = pack2<false>(qv(1, d0 + 2), qv(1, d0 + 3));
+                } else {
+                    const int d0    = 16 * ks + 2 * c;
+                    const int ii[4] = {0, 1, 0, 1};
+                    const int dd[4] = {d0, d0, d0 + 8, d0 + 8};
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float x0 = qv(ii[r], dd[r]), x1 = qv(ii[r], dd[r] + 1);
+                        qa[ks][r]      = pack2<kBF16>(x0, x1);
+                        if constexpr (kBF16) {
+                            qlo[ks][r] = split_lo_bf16(x0, x1, qa[ks][r]);
+                        }
+                    }
+                }
+            }
+        } else {
+            // This thread's Q values, x[i][ks][e] of row g + 8i: dims
+            // c*(D/4) + 4ks + e for Q8_0 (each thread's K bytes are one run), else
+            // 16ks + 2c + (e & 1) + 8(e >> 1) (the m16n8k16 A fragment).
+            auto qdim = [&](int ks, int e) -> int {
+                return kQ8 ? c * (D / 4) + 4 * ks + e : 16 * ks + 2 * c + (e & 1) + 8 * (e >> 1);
+            };
+            float x[2][KS][4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        x[i][ks][e] = qrow[i] ? __ldg(qrow[i] + qdim(ks, e)) : 0.0f;
+                    }
+                }
+            }
+            if (o.qp.on) {
+                // QK-norm + RoPE: a row's D values are spread over its quad (c = 0..3)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    if (o.qp.w) {
+                        float ss = 0.0f;
+#pragma unroll
+                        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                ss = fmaf(x[i][ks][e], x[i][ks][e], ss);
+                            }
+                        }
+                        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                        const float sc = rn_scale(o.qp, ss, D);
+#pragma unroll
+                        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                x[i][ks][e] = (x[i][ks][e] * sc) * __ldg(o.qp.w + qdim(ks, e));
+                            }
+                        }
+                    }
+                    if (o.qp.rope) {
+                        if constexpr (kQ8) {
+                            // dim d + D/2 sits on thread c ^ 2 at the same (ks, e)
+#pragma unroll
+                            for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float pt = __shfl_xor_sync(0xffffffffu, x[i][ks][e], 2);
+                                    x[i][ks][e]    = rn_rotate(o.qp, x[i][ks][e], pt, c < 2, qpos[i], qdim(ks, e) & (D / 2 - 1));
+                                }
+                            }
+                        } else {
+                            // dim d + D/2 is this thread's (ks + KS/2, e)
+#pragma unroll
+                            for (int ks = 0; ks < KS / 2; ++ks) {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float a = x[i][ks][e], bb = x[i][ks + KS / 2][e];
+                                    x[i][ks][e]          = rn_rotate(o.qp, a, bb, true, qpos[i], qdim(ks, e));
+                                    x[i][ks + KS / 2][e] = rn_rotate(o.qp, bb, a, false, qpos[i], qdim(ks, e));
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const float x0 = qv(ii[r], dd[r]), x1 = qv(ii[r], dd[r] + 1);
+                    // fragment register r: row r & 1, value pair (r >> 1)
+                    const float x0 = x[r & 1][ks][2 * (r >> 1)], x1 = x[r & 1][ks][2 * (r >> 1) + 1];
                     qa[ks][r]      = pack2<kBF16>(x0, x1);
                     if constexpr (kBF16) {
                         qlo[ks][r] = split_lo_bf16(x0, x1, qa[ks][r]);
@@ -1090,14 +1221,17 @@ namespace {
 template <int KV_TYPE, int D>
 cudaError_t launch_impl(const DecodeLaunch &L, cudaStream_t s, int *launches) {
     using Cfg = DecCfg<KV_TYPE, D>;
-    auto kern = fa_decode_kernel<KV_TYPE, D>;
+    const bool pro  = L.p.op.qp.on || L.p.kp.on;
+    auto       kern = pro ? fa_decode_kernel<KV_TYPE, D, true> : fa_decode_kernel<KV_TYPE, D, false>;
     static thread_local int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-        if (e != cudaSuccess) {
-            return e;
+        for (auto k : {fa_decode_kernel<KV_TYPE, D, false>, fa_decode_kernel<KV_TYPE, D, true>}) {
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+            if (e != cudaSuccess) {
+                return e;
+            }
         }
         configured_dev = dev;
     }

@@ -26,6 +26,7 @@
 // Every wait is bounded (error word + drain on expiry).
 #include "fa_internal.h"
 #include "ptx.cuh"
+#include "rope_norm.cuh"
 
 namespace acefa {
 namespace {
@@ -68,8 +69,28 @@ __device__ __forceinline__ void row_to_query(int gr, int G, int hk, int &iq, int
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Mask classification: one CTA per (key tile, row tile, mask batch).
+// Mask classification: one CTA per (key tile, row tile, mask batch).  The
+// tile's mask rows (at most 128 query rows x 128 keys) are cut into 8-key
+// chunks; each thread takes up to 8 chunks and issues all their 16-B loads
+// before looking at any (the pass is a stream over the mask: it must run at
+// HBM speed, not at load latency).  Chunks that are not 16-B aligned or run
+// past n_kv are read element by element.
+__device__ __forceinline__ void classify_halves(const uint32_t (&w)[4], int kk, int &live, int &nonzero,
+                                                int &nonbinary) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const uint32_t h = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+        if (e < kk) {
+            live |= h != kHalfNegInf;
+            nonzero |= (h & 0x7FFFu) != 0;
+            nonbinary |= (h & 0x7FFFu) != 0 && h != kHalfNegInf;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) fa_mask_classify(const __grid_constant__ DenseParams P) {
+    constexpr int kChunks = kDenseBN / 8;                  // 8-key chunks per row of a tile
+    constexpr int kItems  = kDenseBM * kChunks / 256;      // chunks per thread (rows <= 128)
     const OpDesc &o   = P.op;
     const int     kt  = blockIdx.x;
     const int     t   = blockIdx.y;
@@ -78,18 +99,41 @@ __global__ void __launch_bounds__(256) fa_mask_classify(const __grid_constant__ 
     const int     gr0 = t * kDenseBM;
     const int     gr1 = min(P.rows_total, gr0 + kDenseBM) - 1;
     const int     iq0 = gr0 / G, iq1 = gr1 / G;
+    const int     nrow = iq1 - iq0 + 1;  // <= 128: G = 1 gives 128 rows, G >= 2 at most 65
     const int     j0 = kt * kDenseBN, j1 = min(o.n_kv, j0 + kDenseBN);
     const int     nj = j1 - j0;
     int           live = 0, nonzero = 0, nonbinary = 0;
     pdl_wait_primary();
-    const char *mbase = o.mask + (int64_t) bm * o.m_nb3;
-    for (int idx = threadIdx.x; idx < (iq1 - iq0 + 1) * nj; idx += blockDim.x) {
-        const int       iq = iq0 + idx / nj;
-        const int       j  = j0 + idx % nj;
-        const uint16_t  h  = __ldg(reinterpret_cast<const uint16_t *>(mbase + (int64_t) iq * o.m_nb1) + j);
-        live |= h != kHalfNegInf;
-        nonzero |= (h & 0x7FFFu) != 0;
-        nonbinary |= (h & 0x7FFFu) != 0 && h != kHalfNegInf;
+    const char *mbase = o.mask + (int64_t) bm * o.m_nb3 + (int64_t) iq0 * o.m_nb1 + (int64_t) j0 * 2;
+    const bool  vec   = ((reinterpret_cast<uintptr_t>(mbase) | (uintptr_t) o.m_nb1) & 15u) == 0;
+    uint4       v[kItems];
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        const int idx = (int) threadIdx.x + 256 * it;
+        const int r = idx / kChunks, ch = idx % kChunks;
+        v[it]       = make_uint4(0u, 0u, 0u, 0u);
+        if (vec && r < nrow && nj - 8 * ch >= 8) {
+            v[it] = __ldg(reinterpret_cast<const uint4 *>(mbase + (int64_t) r * o.m_nb1) + ch);
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        const int idx = (int) threadIdx.x + 256 * it;
+        const int r = idx / kChunks, ch = idx % kChunks;
+        const int kk = nj - 8 * ch;  // keys of this chunk inside the tile
+        if (r >= nrow || kk <= 0) {
+            continue;
+        }
+        uint32_t w[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+        if (!vec || kk < 8) {
+            const uint16_t *p = reinterpret_cast<const uint16_t *>(mbase + (int64_t) r * o.m_nb1) + 8 * ch;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t h = e < kk ? __ldg(p + e) : 0u;
+                w[e >> 1]        = (e & 1) ? (w[e >> 1] & 0xFFFFu) | (h << 16) : h;
+            }
+        }
+        classify_halves(w, kk, live, nonzero, nonbinary);
     }
     live      = __syncthreads_or(live);
     nonzero   = __syncthreads_or(nonzero);
@@ -346,6 +390,8 @@ __device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4],
 }
 
 // ---------------------------------------------------------------------------
+// PRO: the instance that applies the QK-norm + RoPE prologue to Q rows.
+template <bool PRO>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap) {
@@ -471,9 +517,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- Q: f32 rows -> f16, 128-B swizzled K-major tiles [2 x 64 dims][128 rows].
     // 16-B chunks, eight loads in flight per thread before any is converted.
+    // A warp's chunks of one load step are one row (lane l: dims 4l..4l+3).
     {
         constexpr int kChunks = 2 * kDenseBM * 32;
         constexpr int kUnroll = 8;
+        auto store_q = [&](int ch, float4 x) {
+            const int      rr = ch >> 5;
+            const int      i  = rr / kDenseBM;
+            const int      r  = rr % kDenseBM;
+            const int      d  = 4 * (ch & 31);
+            const uint32_t lo = pack2<false>(x.x, x.y), hi = pack2<false>(x.z, x.w);
+            uint8_t *dst = smem + kOffQ + i * kQBytes + (d >> 6) * (kDenseBM * 128) + r * 128 +
+                           ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+        };
         for (int base = threadIdx.x; base < kChunks; base += kThreads * kUnroll) {
             float4 v[kUnroll];
 #pragma unroll
@@ -495,19 +552,68 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            if (!PRO || !o.qp.on) {
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    if (base + u * kThreads < kChunks) {
+                        store_q(base + u * kThreads, v[u]);
+                    }
+                }
+                continue;
+            }
+            // QK-norm + RoPE of each row (one row per warp and step), one step
+            // at a time: the loads above are already in flight
+            float4 vl[kUnroll];
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
+                vl[u] = v[u];
+            }
+#pragma unroll 1
+            for (int u = 0; u < kUnroll; ++u) {
                 const int ch = base + u * kThreads;
-                if (ch < kChunks) {
-                    const int      rr = ch >> 5;
-                    const int      i  = rr / kDenseBM;
-                    const int      r  = rr % kDenseBM;
-                    const int      d  = 4 * (ch & 31);
-                    const uint32_t lo = pack2<false>(v[u].x, v[u].y), hi = pack2<false>(v[u].z, v[u].w);
-                    uint8_t *dst = smem + kOffQ + i * kQBytes + (d >> 6) * (kDenseBM * 128) + r * 128 +
-                                   ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
-                    *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+                if (ch >= kChunks) {
+                    break;
                 }
+                const int rr  = ch >> 5;
+                const int i   = rr / kDenseBM;
+                const int gr  = (t0 + i) * kDenseBM + rr % kDenseBM;
+                int       pos = 0;
+                if (o.qp.rope && has_tile[i] && gr < P.rows_total) {
+                    int iq, hq;
+                    row_to_query(gr, o.G, hk, iq, hq);
+                    pos = __ldg(o.qp.pos + iq + (int64_t) b * o.n_q);
+                }
+                float x[4] = {vl[u].x, vl[u].y, vl[u].z, vl[u].w};
+                if (o.qp.w) {
+                    float ss = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        ss = fmaf(x[e], x[e], ss);
+                    }
+#pragma unroll
+                    for (int off = 16; off; off >>= 1) {
+                        ss += __shfl_xor_sync(0xffffffffu, ss, off);
+                    }
+                    const float sc = rn_scale(o.qp, ss, kDenseBM);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        x[e] = (x[e] * sc) * __ldg(o.qp.w + 4 * lane + e);
+                    }
+                }
+                if (o.qp.rope) {
+                    float2 cs[4];
+#pragma unroll 1
+                    for (int e = 0; e < 4; ++e) {  // one inline copy of sincosf
+                        cs[e] = rn_cos_sin_inline((float) pos * o.qp.inv_freq[(4 * lane + e) & 63]);
+                    }
+                    const bool first = lane < 16;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float pt = __shfl_xor_sync(0xffffffffu, x[e], 16);
+                        x[e] = first ? x[e] * cs[e].x - pt * cs[e].y : pt * cs[e].y + x[e] * cs[e].x;
+                    }
+                }
+                store_q(ch, make_float4(x[0], x[1], x[2], x[3]));
             }
         }
     }
@@ -1085,9 +1191,11 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     int                     dev            = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(fa_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        if (e != cudaSuccess) {
-            return e;
+        for (auto k : {fa_dense_kernel<false>, fa_dense_kernel<true>}) {
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            if (e != cudaSuccess) {
+                return e;
+            }
         }
         configured_dev = dev;
     }
@@ -1115,7 +1223,8 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     c.stream             = s;
     c.attrs              = attr;
     c.numAttrs           = 1;
-    cudaError_t e        = cudaLaunchKernelEx(&c, fa_dense_kernel, L.p, L.kmap, L.vmap);
+    cudaError_t e        = cudaLaunchKernelEx(&c, L.p.op.qp.on ? fa_dense_kernel<true> : fa_dense_kernel<false>, L.p,
+                                          L.kmap, L.vmap);
     if (e != cudaSuccess) {
         return e;
     }

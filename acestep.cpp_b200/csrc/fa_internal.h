@@ -11,6 +11,20 @@ namespace acefa {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// RMSNorm + RoPE (NEOX) of rows of D values, device form of acefa_rope_norm.
+// inv_freq[k] = theta_base^(-2k/D) is computed once on the host (powf), so
+// every kernel -- and the CPU oracle -- rotates by the same f32 angles
+// positions[..] * inv_freq[k].
+constexpr int kRopeMaxPairs = 64;  // D <= 128
+struct RopeNorm {
+    int            on;        // apply (a prologue was given)
+    int            rope;      // rotate (theta_base != 0)
+    const float   *w;         // RMSNorm weight [D], or nullptr: no RMSNorm
+    const int32_t *pos;       // positions
+    float          eps;
+    float          inv_freq[kRopeMaxPairs];
+};
+
 // Operands after host-side validation, in ggml terms.  Strides in bytes.
 struct OpDesc {
     // Q [D, n_q, Hq, B] f32
@@ -30,6 +44,10 @@ struct OpDesc {
     int     mg_kind, mg_window;
     int64_t mg_pos0[ACEFA_MASK_GEN_MAX_BATCH];
     int64_t mg_len[ACEFA_MASK_GEN_MAX_BATCH];
+    // Q prologue (acefa_op_ext::q_prologue): Q rows are raw projections,
+    // normalised and rotated as they are loaded; row (iq, b) has position
+    // qp.pos[iq + b * n_q]
+    RopeNorm qp;
     // sinks [Hq] f32 (nullptr = none)
     const float *sinks;
     // dst [D, Hq, n_q, B] f32
@@ -108,6 +126,7 @@ struct DecodeParams {
     const char    *k_new, *v_new;
     int64_t        kn_nb2, kn_nb3, vn_nb2, vn_nb3;
     const int64_t *append_pos;
+    RopeNorm       kp;  // prologue of the new K row (position kp.pos[set])
     int    *dev_err;
     uint64_t wait_limit_ns;
 };
@@ -172,5 +191,9 @@ struct DenseLaunch {
 };
 
 cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches);
+
+// ------------------------------------------------------------------ K/V prologue
+int kv_prologue_launch(const acefa_tensor *k_src, const acefa_tensor *v_src, const acefa_tensor *k_dst,
+                       const acefa_tensor *v_dst, const RopeNorm &kp, int sm_count, cudaStream_t stream);
 
 }  // namespace acefa

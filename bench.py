@@ -422,6 +422,7 @@ def extras(device, stream, args):
                                 ("; mask by rule" if rule else "")}
             del graph, ops
         res["config1_append"] = append_step(device, stream)
+        res["dit6000_prologue"] = dit_prologue(device, stream)
     return res
 
 
@@ -435,7 +436,11 @@ def append_step(device, stream, reps=64, kv_len=2048):
     import acefa
 
     g = torch.Generator(device=device).manual_seed(42 + 1000 + 7)
-    sep, fused = [], []
+    wq = 1.0 + 0.1 * torch.randn(D, device=device, generator=g)
+    wk = 1.0 + 0.1 * torch.randn(D, device=device, generator=g)
+    pos32 = torch.tensor([kv_len - 1], dtype=torch.int32, device=device)
+    cos, sin = rope_table(pos32, device)
+    sep, fused, sep_pro, fused_pro = [], [], [], []
     for _ in range(reps):
         q = torch.randn(1, 16, 1, D, device=device, generator=g)
         k = torch.randn(1, 8, kv_len, D, device=device, generator=g, dtype=torch.float16)
@@ -447,6 +452,12 @@ def append_step(device, stream, reps=64, kv_len=2048):
         op = acefa.Op(q, k, v, mask=m, scale=D ** -0.5)
         sep.append((op, k, v, kn, vn, pos))
         fused.append(acefa.Op(q, k, v, mask=m, scale=D ** -0.5, k_new=kn, v_new=vn, pos=pos))
+        # with the QK-norm + RoPE prologue: torch ops then the operator, or all in one call
+        qr = torch.empty_like(q)
+        sep_pro.append((acefa.Op(qr, k, v, mask=m, scale=D ** -0.5), q, qr, k, v, kn, vn, pos))
+        fused_pro.append(acefa.Op(q, k, v, mask=m, scale=D ** -0.5, k_new=kn, v_new=vn, pos=pos,
+                                  q_prologue=acefa.RopeNorm(wq, 1e-6, 1.0e6, pos32),
+                                  k_prologue=acefa.RopeNorm(wk, 1e-6, 1.0e6, pos32)))
 
     def run_sep():
         for op, k, v, kn, vn, pos in sep:
@@ -458,8 +469,21 @@ def append_step(device, stream, reps=64, kv_len=2048):
         for op in fused:
             op(stream=torch.cuda.current_stream())
 
+    def run_sep_pro():
+        for op, q, qr, k, v, kn, vn, pos in sep_pro:
+            qr.copy_(torch_rope_norm(q, wq, cos, sin))
+            k.index_copy_(2, pos, torch_rope_norm(kn, wk, cos, sin).half())
+            v.index_copy_(2, pos, vn.half())
+            op(stream=torch.cuda.current_stream())
+
+    def run_fused_pro():
+        for op in fused_pro:
+            op(stream=torch.cuda.current_stream())
+
     out = {}
-    for name, fn in (("separate_us_per_step", run_sep), ("fused_us_per_step", run_fused)):
+    for name, fn in (("separate_us_per_step", run_sep), ("fused_us_per_step", run_fused),
+                     ("separate_with_prologue_us_per_step", run_sep_pro),
+                     ("fused_with_prologue_us_per_step", run_fused_pro)):
         with torch.cuda.stream(stream):
             fn()
             torch.cuda.synchronize()
@@ -477,7 +501,106 @@ def append_step(device, stream, reps=64, kv_len=2048):
         out[name] = round(s0.elapsed_time(s1) * 1e3 / (10 * reps), 2)
         del graph
     out["note"] = ("config-1 shape, new row at the last position; separate = two row writes (torch index_copy, "
-                   "standing in for ggml_set_rows) + acefa_flash_attn_ext")
+                   "standing in for ggml_set_rows) + acefa_flash_attn_ext; with_prologue adds QK-norm + RoPE of "
+                   "Q and the new K row (torch ops standing in for ggml's rms_norm / mul / rope nodes, vs fused "
+                   "into the same single launch)")
+    return out
+
+
+def rope_table(pos, device, theta=1.0e6):
+    """cos / sin (rows, D/2) of RoPE NEOX for int positions (torch reference path)."""
+    import torch
+
+    inv = theta ** (-torch.arange(0, D, 2, device=device, dtype=torch.float32) / D)
+    a = pos.float()[:, None] * inv[None, :]
+    return a.cos(), a.sin()
+
+
+def torch_rope_norm(x, w, cos, sin, eps=1e-6):
+    """RMSNorm * w then RoPE NEOX over the last axis, as separate torch kernels
+    (the stand-in for the reference's rms_norm, mul and rope graph nodes).
+    cos / sin broadcast against x's rows (..., rows, D/2)."""
+    import torch
+
+    y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+    y1, y2 = y[..., : D // 2], y[..., D // 2:]
+    return torch.cat([y1 * cos - y2 * sin, y1 * sin + y2 * cos], dim=-1)
+
+
+def dit_prologue(device, stream, N=2, H=16, S=6000, iters=10):
+    """A DiT self-attention layer's prologue + attention (config-4 shape):
+    separate = torch rms_norm / mul / rope / cast / permute kernels (standing in
+    for the reference's graph nodes) then acefa_flash_attn_ext, against
+    acefa_kv_prologue + the operator with the Q prologue fused."""
+    import torch
+
+    import acefa
+
+    g = torch.Generator(device=device).manual_seed(42 + 2000)
+    # projections as the DiT graph leaves them: [D, H, S, N] f32 = torch (N, S, H, D)
+    q_raw = torch.randn(N, S, H, D, device=device, generator=g)
+    k_raw = torch.randn(N, S, H, D, device=device, generator=g)
+    v_raw = torch.randn(N, S, H, D, device=device, generator=g)
+    wq = 1.0 + 0.1 * torch.randn(D, device=device, generator=g)
+    wk = 1.0 + 0.1 * torch.randn(D, device=device, generator=g)
+    pos = torch.arange(S, device=device, dtype=torch.int32).repeat(N)
+    cos, sin = rope_table(torch.arange(S, device=device, dtype=torch.int32), device)
+    cos, sin = cos[None, :, None, :], sin[None, :, None, :]  # against (N, S, H, D/2)
+    qs = torch.empty(N, H, S, D, device=device)
+    k16 = torch.empty(N, H, S, D, device=device, dtype=torch.float16)
+    v16 = torch.empty_like(k16)
+    op_sep = acefa.Op(qs, k16, v16, scale=D ** -0.5)
+    op_fused = acefa.Op(q_raw.permute(0, 2, 1, 3), k16, v16, scale=D ** -0.5,
+                        q_prologue=acefa.RopeNorm(wq, 1e-6, 1.0e6, pos))
+    k_pro = acefa.RopeNorm(wk, 1e-6, 1.0e6, pos)
+
+    def run_sep():
+        qs.copy_(torch_rope_norm(q_raw, wq, cos, sin).permute(0, 2, 1, 3))
+        k16.copy_(torch_rope_norm(k_raw, wk, cos, sin).permute(0, 2, 1, 3))
+        v16.copy_(v_raw.permute(0, 2, 1, 3))
+        op_sep(stream=torch.cuda.current_stream())
+
+    def run_fused():
+        st = torch.cuda.current_stream()
+        acefa.kv_prologue(k_raw.permute(0, 2, 1, 3), k16, v_raw.permute(0, 2, 1, 3), v16, k_pro, stream=st)
+        op_fused(stream=st)
+
+    out = {}
+    for name, fn in (("separate_ms", run_sep), ("fused_ms", run_fused)):
+        with torch.cuda.stream(stream):
+            fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                fn()
+            for _ in range(3):
+                graph.replay()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(iters):
+                graph.replay()
+            s1.record(stream)
+            torch.cuda.synchronize()
+        out[name] = round(s0.elapsed_time(s1) / iters, 4)
+        del graph
+    # the prologue pass alone: K and V read as f32, written as f16
+    with torch.cuda.stream(stream):
+        st = stream
+        for _ in range(3):
+            acefa.kv_prologue(k_raw.permute(0, 2, 1, 3), k16, v_raw.permute(0, 2, 1, 3), v16, k_pro, stream=st)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(iters):
+            acefa.kv_prologue(k_raw.permute(0, 2, 1, 3), k16, v_raw.permute(0, 2, 1, 3), v16, k_pro, stream=st)
+        s1.record(stream)
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / iters
+    nbytes = 2 * N * S * H * D * (4 + 2)
+    peak, _ = read_peaks()
+    out["kv_prologue_ms"] = round(ms, 4)
+    out["kv_prologue_gbs"] = round(nbytes / (ms / 1e3) / 1e9, 1)
+    out["kv_prologue_frac_of_hbm_peak"] = round(nbytes / (ms / 1e3) / 1e9 / peak, 4)
+    out["note"] = "N=2 x H=16 x S=6000, D=128; separate = torch kernels standing in for the reference's graph nodes"
     return out
 
 
@@ -678,8 +801,8 @@ def run_dense_workload(args):
     torch.cuda.set_device(0)
     device = torch.device("cuda", 0)
     stream = torch.cuda.Stream(device=device)
-    r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup)
-    emit({"workload": args.workload, **r})
+    r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup, rule=args.mask_rule)
+    emit({"workload": args.workload, "mask_rule": bool(args.mask_rule), **r})
     return 0
 
 
@@ -718,6 +841,8 @@ def main():
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
     ap.add_argument("--workload", default="decode4b",
                     help="decode4b (headline) or one dense op: " + ", ".join(DENSE_WORKLOADS))
+    ap.add_argument("--mask-rule", action="store_true",
+                    help="dense workload: give the mask by rule (acefa_flash_attn_ext_gen) instead of a tensor")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

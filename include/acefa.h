@@ -216,6 +216,62 @@ ACEFA_API int acefa_flash_attn_ext_gen(const acefa_tensor *q, const acefa_tensor
                                        int prec, void *stream, void *workspace, size_t workspace_bytes);
 
 /*
+ * The attention prologue acestep.cpp runs as separate graph nodes before the
+ * attention node (src/qwen3-lm.h:423-431, src/dit-graph.h:181-197):
+ *   y = ggml_rms_norm(x, eps) * norm_weight        (per row of D values)
+ *   y = ggml_rope_ext(y, positions, mode 2 = NEOX, n_dims = D, freq_base =
+ *       theta_base, freq_scale 1, no YaRN)
+ * i.e. pair k < D/2 rotates (y[k], y[k + D/2]) by positions[..] *
+ * theta_base^(-2k/D).  Row i of batch b has position positions[i + b * n],
+ * n being the rows per batch of the tensor it applies to (n_q for Q; for a
+ * decode step's new K row, n = 1: positions[set]).
+ */
+typedef struct acefa_rope_norm {
+    const float   *norm_weight;  /* [D] f32, device; NULL = no RMSNorm */
+    float          eps;          /* rms_norm_eps */
+    float          theta_base;   /* rope_theta; 0 = no RoPE */
+    const int32_t *positions;    /* int32, device (ggml's positions tensor); unused without RoPE */
+} acefa_rope_norm;
+
+/*
+ * Options of acefa_flash_attn_ext_fused().  Zero-initialise and set what is
+ * used; every member may be NULL / 0.
+ */
+typedef struct acefa_op_ext {
+    const acefa_mask_gen  *mask_gen;    /* mask by rule; `mask` must then be NULL */
+    const acefa_rope_norm *q_prologue;  /* applied to each Q row as the kernels load it */
+    /* Fused KV-cache append (decode path), as acefa_flash_attn_ext_append: */
+    const acefa_tensor    *k_new, *v_new;
+    const int64_t         *append_pos;
+    const acefa_rope_norm *k_prologue;  /* applied to k_new before it is converted and stored */
+    /* Mirrors, as acefa_flash_attn_ext_mirrored: */
+    void *const           *mirrors;
+    int                    n_mirrors;
+} acefa_op_ext;
+
+/* The operator with any combination of the fusions above (NULL ext = plain
+ * acefa_flash_attn_ext).  Q given with a q_prologue is the raw projection
+ * output (before RMSNorm and RoPE), in the same [D, n_q, Hq, B] view. */
+ACEFA_API int acefa_flash_attn_ext_fused(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                         const acefa_tensor *mask, const acefa_tensor *sinks,
+                                         const acefa_tensor *dst, float scale, float max_bias,
+                                         float logit_softcap, int prec, const acefa_op_ext *ext, void *stream,
+                                         void *workspace, size_t workspace_bytes);
+
+/*
+ * K / V preparation for the dense path in one pass: k_dst = RoPE(RMSNorm(k_src))
+ * and v_dst = v_src, converted to the destination type (F16 or BF16), at any
+ * strides on either side (so the permute of the reference's graph and a
+ * write into a KV-cache window are both just destination views).  Replaces
+ * the rms_norm, mul, rope, cont and cast / set_rows nodes of
+ * src/dit-graph.h:181-213 and src/qwen3-lm.h:423-449.  k_src / v_src: F32
+ * [D, rows, H, B] with rows * H * B < 2^31; k_dst / v_dst: the same ne.
+ * v_src / v_dst may be NULL.  Positions index as positions[row + b * rows].
+ */
+ACEFA_API int acefa_kv_prologue(const acefa_tensor *k_src, const acefa_tensor *v_src, const acefa_tensor *k_dst,
+                                const acefa_tensor *v_dst, const acefa_rope_norm *k_prologue, void *stream);
+
+/*
  * CUDA IPC through the ABI, so a host without CUDA bindings can map peer
  * buffers.  acefa_peer_export: an opaque handle (ACEFA_PEER_HANDLE_BYTES bytes)
  * for the allocation holding ptr, plus ptr's byte offset inside it.

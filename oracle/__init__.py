@@ -7,7 +7,9 @@ links or calls it; it is the checker, never the thing measured or shipped.
 Parity status: the attention arithmetic is *parity unpinned* -- the reference
 kernel lives in the absent ggml submodule (acestep.cpp ``.gitmodules:1-3``) and
 the reference ships no op-level golden vectors.  The Q8_0 block format is pinned
-bit-exactly against gguf 0.19.0 (``tests/golden/q8_0_*.npy``).
+bit-exactly against gguf 0.19.0 (``tests/golden/q8_0_*.npy``).  The
+RMSNorm + RoPE prologue (``rope_norm``) is pinned against the Qwen3 model
+definition in HF transformers (``tests/golden/rope_norm_*.npz``).
 """
 from .oracle import (  # noqa: F401
     GGML_F16,
@@ -21,4 +23,5 @@ from .oracle import (  # noqa: F401
     quantize_q8_0,
     dequantize_q8_0,
     lib_path,
+    rope_norm,
 )

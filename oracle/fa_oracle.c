@@ -593,3 +593,36 @@ int ora_flash_attn_ext(const ora_tensor *q, const ora_tensor *k, const ora_tenso
     }
     return 0;
 }
+
+/* RMSNorm + RoPE NEOX of contiguous rows (see fa_oracle.h).  The frequency of
+ * pair k is powf(theta_base, -2k/D) in f32, the same table the library
+ * computes on the host, so both rotate by identical f32 angles. */
+void ora_rope_norm(float *x, int64_t rows, int D, const float *weight, float eps, float theta_base,
+                   const int32_t *pos) {
+    float inv_freq[256];
+    for (int k = 0; k < D / 2 && k < 256; ++k) {
+        inv_freq[k] = powf(theta_base, -(float) (2 * k) / (float) D);
+    }
+    for (int64_t r = 0; r < rows; ++r) {
+        float *y = x + r * D;
+        if (weight) {
+            double ss = 0.0;
+            for (int d = 0; d < D; ++d) {
+                ss += (double) y[d] * y[d];
+            }
+            const float sc = 1.0f / sqrtf((float) (ss / D) + eps);
+            for (int d = 0; d < D; ++d) {
+                y[d] = (y[d] * sc) * weight[d];
+            }
+        }
+        if (theta_base > 0.0f) {
+            for (int k = 0; k < D / 2; ++k) {
+                const float a  = (float) pos[r] * inv_freq[k];
+                const float c  = cosf(a), s = sinf(a);
+                const float x0 = y[k], x1 = y[k + D / 2];
+                y[k]           = x0 * c - x1 * s;
+                y[k + D / 2]   = x0 * s + x1 * c;
+            }
+        }
+    }
+}

@@ -61,6 +61,9 @@ def _load():
         lib.ora_flash_attn_ext.restype = ctypes.c_int
         lib.ora_quantize_q8_0.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
         lib.ora_dequantize_q8_0.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
+        lib.ora_rope_norm.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+                                      ctypes.c_float, ctypes.c_float, ctypes.c_void_p]
+        lib.ora_rope_norm.restype = None
         _lib = lib
     return _lib
 
@@ -123,6 +126,22 @@ def flash_attn_ext(q, k, v, mask=None, sinks=None, scale=1.0, max_bias=0.0, soft
     if rc != 0:
         raise ValueError(f"oracle rejected the operands (status {rc})")
     return out
+
+
+def rope_norm(x: np.ndarray, weight=None, eps=1e-6, theta=0.0, positions=None) -> np.ndarray:
+    """RMSNorm (times weight) + RoPE NEOX over the last axis (D).  positions
+    holds one int per row of x.reshape(-1, D).  Returns a new f32 array."""
+    lib = _load()
+    y = np.array(x, dtype=np.float32, order="C", copy=True)
+    D = y.shape[-1]
+    rows = y.size // D
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    p = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32).reshape(-1)
+    if theta > 0.0:
+        assert p is not None and p.size == rows
+    lib.ora_rope_norm(y.ctypes.data, rows, D, None if w is None else w.ctypes.data, eps, theta,
+                      None if p is None else p.ctypes.data)
+    return y
 
 
 def quantize_q8_0(x: np.ndarray) -> np.ndarray:

@@ -1,6 +1,7 @@
 """CPU tests of the oracle: Q8_0 pinned against gguf, attention cross-checked
-against independent float64 fixtures, and the ggml-cpu (F16 accumulation)
-mode's known drift."""
+against independent float64 fixtures, the ggml-cpu (F16 accumulation)
+mode's known drift, and the QK-norm + RoPE prologue pinned against the Qwen3
+model definition."""
 import glob
 import os
 
@@ -86,3 +87,22 @@ def test_contract_violations_rejected(oracle_mod):
     k = np.zeros((1, 2, 8, 64), np.float16)  # Hkv = 2 does not divide 3
     with pytest.raises(ValueError):
         oracle_mod.flash_attn_ext(q, k, k, scale=1.0)
+
+
+@pytest.mark.parametrize("name", ["d128", "d64"])
+def test_rope_norm_matches_qwen3_definition(oracle_mod, name):
+    """QK-norm + RoPE NEOX against HF transformers' Qwen3 modules
+    (tests/golden/make_rope_golden.py).  RMSNorm agrees to f32 rounding; the
+    rotation to f32 rounding of the angle pos * inv_freq (the two sides compute
+    inv_freq by different f32 expressions, so the angle may differ by ~pos * 1e-7
+    rad): the bound per row is 2e-6 + 1.2e-7 * pos * max|x|."""
+    z = np.load(os.path.join(GOLDEN, f"rope_norm_{name}.npz"))
+    normed = oracle_mod.rope_norm(z["x"], z["weight"], float(z["eps"]), 0.0, None)
+    np.testing.assert_allclose(normed, z["normed"], rtol=2e-6, atol=2e-6)
+    out = oracle_mod.rope_norm(z["x"], z["weight"], float(z["eps"]), float(z["theta"]), z["positions"])
+    err = np.abs(out - z["out"]).max(axis=1)
+    bound = 2e-6 + 1.2e-7 * z["positions"].astype(np.float64) * np.abs(z["normed"]).max(axis=1)
+    assert (err <= bound).all(), (err, bound)
+    # without a weight nothing is normalised; without theta nothing rotates
+    x = z["x"][:2]
+    assert np.array_equal(oracle_mod.rope_norm(x, None, 1e-6, 0.0, None), x)
