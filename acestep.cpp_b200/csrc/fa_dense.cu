@@ -602,9 +602,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (o.qp.rope) {
                     float2 cs[4];
-#pragma unroll 1
-                    for (int e = 0; e < 4; ++e) {  // one inline copy of sincosf
-                        cs[e] = rn_cos_sin_inline((float) pos * o.qp.inv_freq[(4 * lane + e) & 63]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        cs[e] = rn_cos_sin((float) pos * o.qp.inv_freq[(4 * lane + e) & 63]);
                     }
                     const bool first = lane < 16;
 #pragma unroll

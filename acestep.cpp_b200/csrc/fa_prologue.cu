@@ -95,36 +95,85 @@ __device__ __forceinline__ void store_row(const KvSide &s, const RowCoord &rc, i
 }
 
 template <int DPL>
-__global__ void __launch_bounds__(kProWarps * 32) fa_kv_prologue(const __grid_constant__ KvProParams P) {
-    const int lane   = threadIdx.x & 31;
-    const int warp0  = (int) blockIdx.x * kProWarps + (int) (threadIdx.x >> 5);
-    const int stride = (int) gridDim.x * kProWarps;
-    const int n      = (int) P.n_rows;
+__global__ void __launch_bounds__(kProWarps * 32, 3) fa_kv_prologue(const __grid_constant__ KvProParams P) {
+    constexpr int D = 32 * DPL, H = DPL / 2;
+    const int     lane   = threadIdx.x & 31;
+    const int     warp0  = (int) blockIdx.x * kProWarps + (int) (threadIdx.x >> 5);
+    const int     stride = (int) gridDim.x * kProWarps;
+    const int     n      = (int) P.n_rows;
+    const RopeNorm &kp   = P.kp;
+    // Per-lane constants: this lane's norm weights and the frequencies of the
+    // half of its angles it computes (lane ^ 16 computes the other half).
+    const bool first = lane < 16;
+    float      wreg[DPL], freq[H];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+        wreg[e] = kp.w ? __ldg(kp.w + DPL * lane + e) : 1.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+        freq[j] = kp.inv_freq[(DPL * lane + (first ? 0 : H) + j) & (D / 2 - 1)];
+    }
     for (int r0 = warp0; r0 < n; r0 += stride * kProUnroll) {
         float    k[kProUnroll][DPL], v[kProUnroll][DPL];
         RowCoord rc[kProUnroll];
+        int      pos[kProUnroll];
 #pragma unroll
         for (int u = 0; u < kProUnroll; ++u) {
             const int r = r0 + u * stride;
             rc[u]       = row_coord(P, r < n ? r : 0);
+            pos[u]      = 0;
             if (r < n) {
                 load_row<DPL>(P.side[0], rc[u], lane, k[u]);
                 if (P.side[1].src) {
                     load_row<DPL>(P.side[1], rc[u], lane, v[u]);
                 }
+                if (kp.rope) {
+                    pos[u] = __ldg(kp.pos + rc[u].i + (int64_t) rc[u].b * P.rows);
+                }
             }
         }
 #pragma unroll
         for (int u = 0; u < kProUnroll; ++u) {
-            if (r0 + u * stride < n) {  // warp-uniform
-                if (P.kp.on) {
-                    const int pos = P.kp.rope ? __ldg(P.kp.pos + rc[u].i + (int64_t) rc[u].b * P.rows) : 0;
-                    rn_warp_row<DPL>(P.kp, k[u], lane, pos);
+            if (r0 + u * stride >= n) {  // warp-uniform
+                break;
+            }
+            float(&x)[DPL] = k[u];
+            if (kp.w) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) {
+                    ss = fmaf(x[e], x[e], ss);
                 }
-                store_row<DPL>(P.side[0], rc[u], lane, P.dst_bf16, k[u]);
-                if (P.side[1].src) {
-                    store_row<DPL>(P.side[1], rc[u], lane, P.dst_bf16, v[u]);
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    ss += __shfl_xor_sync(0xffffffffu, ss, off);
                 }
+                const float sc = rn_scale(kp, ss, D);
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) {
+                    x[e] = (x[e] * sc) * wreg[e];
+                }
+            }
+            if (kp.rope) {
+                float2 cs[DPL];
+#pragma unroll
+                for (int j = 0; j < H; ++j) {
+                    const float2 mine  = rn_cos_sin((float) pos[u] * freq[j]);
+                    const float2 other = make_float2(__shfl_xor_sync(0xffffffffu, mine.x, 16),
+                                                     __shfl_xor_sync(0xffffffffu, mine.y, 16));
+                    cs[j]     = first ? mine : other;
+                    cs[j + H] = first ? other : mine;
+                }
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) {
+                    const float pt = __shfl_xor_sync(0xffffffffu, x[e], 16);
+                    x[e]           = first ? x[e] * cs[e].x - pt * cs[e].y : pt * cs[e].y + x[e] * cs[e].x;
+                }
+            }
+            store_row<DPL>(P.side[0], rc[u], lane, P.dst_bf16, x);
+            if (P.side[1].src) {
+                store_row<DPL>(P.side[1], rc[u], lane, P.dst_bf16, v[u]);
             }
         }
     }
