@@ -55,11 +55,6 @@ static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= 384 * 168, "register sp
 
 constexpr uint16_t kHalfNegInf = 0xFC00u;
 
-// Share of softmax exponentials computed by poly_exp2 on the FMA pipe instead of
-// ex2 on the MUFU unit: 0 = none, 1 = one in four, 2 = one in two.
-#ifndef ACEFA_POLY_EXP
-#define ACEFA_POLY_EXP 0
-#endif
 
 __device__ __forceinline__ void row_to_query(int gr, int G, int hk, int &iq, int &hq) {
     iq = gr / G;
@@ -364,16 +359,8 @@ __device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4],
         for (int e = 0; e < 16; ++e) {
             float p0 = fast_exp2(fmaf(__uint_as_float(x[2 * e]), mul, -m_use));
             float p1 = fast_exp2(fmaf(__uint_as_float(x[2 * e + 1]), mul, -m_use));
-#if ACEFA_POLY_EXP >= 2
-            float q0 = poly_exp2(fmaf(__uint_as_float(y[2 * e]), mul, -m_use));
-#else
             float q0 = fast_exp2(fmaf(__uint_as_float(y[2 * e]), mul, -m_use));
-#endif
-#if ACEFA_POLY_EXP >= 1
-            float q1 = poly_exp2(fmaf(__uint_as_float(y[2 * e + 1]), mul, -m_use));
-#else
             float q1 = fast_exp2(fmaf(__uint_as_float(y[2 * e + 1]), mul, -m_use));
-#endif
             if constexpr (VIS) {
                 p0 = (va >> (2 * e)) & 1u ? p0 : 0.0f;
                 p1 = (va >> (2 * e + 1)) & 1u ? p1 : 0.0f;

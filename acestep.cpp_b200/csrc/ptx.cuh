@@ -159,21 +159,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-// 2^x on the FMA/ALU pipes, for x in [-126, 126]: x = j + f with j = round(x)
-// taken from the low mantissa bits of x + 1.5*2^23 and f in [-0.5, 0.5]; 2^f by a
-// degree-3 polynomial whose coefficients are a relative-error minimax (Remez
-// exchange) fit on [-0.5, 0.5] (max relative error 7.5e-5, 13.7 bits); j is
-// added to the exponent field.  Used for part of the softmax exponentials so
-// that the MUFU unit (16 results per clock per SM) is not the bottleneck.
-__device__ __forceinline__ float poly_exp2(float x) {
-    x             = fmaxf(x, -126.0f);
-    const float t = x + 12582912.0f;
-    const float j = t - 12582912.0f;
-    const float f = x - j;
-    const float p = fmaf(fmaf(fmaf(0.05517167f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 // Packed Blackwell arithmetic: two f32 lanes per 64-bit register pair.
 __device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
     uint64_t r;

@@ -208,6 +208,66 @@ def test_mask_rule_entry_validates_before_launch(lib):
                                             None, None, 0) in (-6, -7)     # window: any batch count
 
 
+def test_fused_entry_validates_before_launch(lib):
+    """acefa_flash_attn_ext_fused: every fusion's operands are checked before
+    any device work (fake device pointers; nothing may be dereferenced)."""
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    q, k, v, m, d = _ops(Hq=32, B=4, Bk=4, nkv=700)
+
+    def call(ext, mask=m):
+        return lib.acefa_flash_attn_ext_fused(r(q), r(k), r(v), r(mask), None, r(d), 0.088, 0.0, 0.0, 10,
+                                              r(ext), None, None, 0)
+
+    ext = acefa.OpExt()
+    pro = acefa.RopeNormC(4096, 1e-6, 1.0e6, None)
+    ext.q_prologue = ctypes.addressof(pro)
+    assert call(ext) == -1                                   # RoPE without positions
+    bad = acefa.RopeNormC(4096, -1.0, 1.0e6, 8192)
+    ext.q_prologue = ctypes.addressof(bad)
+    assert call(ext) == -3                                   # negative eps
+    odd = acefa.RopeNormC(4098, 1e-6, 0.0, None)
+    ext.q_prologue = ctypes.addressof(odd)
+    assert call(ext) == -4                                   # misaligned weight
+    ext = acefa.OpExt()
+    ok = acefa.RopeNormC(4096, 1e-6, 1.0e6, 8192)
+    ext.k_prologue = ctypes.addressof(ok)
+    assert call(ext) == -3                                   # K prologue without an append
+    ext = acefa.OpExt()
+    mg = acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[1, 2, 3, 4])
+    ext.mask_gen = ctypes.addressof(mg)
+    assert call(ext) == -3                                   # rule and mask tensor together
+    if not torch.cuda.is_available():
+        assert call(ext, mask=None) in (-6, -7)             # valid: fails only at the device step
+        ext = acefa.OpExt()
+        ext.q_prologue = ctypes.addressof(ok)
+        assert call(ext) in (-6, -7)
+        assert call(None) in (-6, -7)                        # no options = the plain operator
+
+
+def test_kv_prologue_validates_before_launch(lib):
+    r = lambda x: ctypes.byref(x) if x is not None else None  # noqa: E731
+    ne = [128, 300, 8, 2]
+    src = _td(ne, _contig(ne, 4), acefa.GGML_F32, ptr=1 << 20)
+    dst = _td(ne, _contig(ne, 2), acefa.GGML_F16, ptr=1 << 22)
+    pro = acefa.RopeNormC(4096, 1e-6, 1.0e6, 8192)
+    assert lib.acefa_kv_prologue(None, None, r(dst), None, r(pro), None) == -1
+    assert lib.acefa_kv_prologue(r(src), r(src), r(dst), None, r(pro), None) == -1   # V without a destination
+    q8 = _td(ne, _contig(ne, 2), acefa.GGML_Q8_0, ptr=1 << 22)
+    assert lib.acefa_kv_prologue(r(src), None, r(q8), None, r(pro), None) == -2     # F16 / BF16 only
+    ne2 = [128, 301, 8, 2]
+    dst2 = _td(ne2, _contig(ne2, 2), acefa.GGML_F16, ptr=1 << 22)
+    assert lib.acefa_kv_prologue(r(src), None, r(dst2), None, r(pro), None) == -3    # shapes differ
+    ne96 = [96, 300, 8, 2]
+    s96 = _td(ne96, _contig(ne96, 4), acefa.GGML_F32, ptr=1 << 20)
+    d96 = _td(ne96, _contig(ne96, 2), acefa.GGML_F16, ptr=1 << 22)
+    assert lib.acefa_kv_prologue(r(s96), None, r(d96), None, r(pro), None) == -3     # D 64 or 128
+    strided = _td(ne, [8] + _contig(ne, 4)[1:], acefa.GGML_F32, ptr=1 << 20)
+    assert lib.acefa_kv_prologue(r(strided), None, r(dst), None, r(pro), None) == -4  # rows contiguous
+    if not torch.cuda.is_available():
+        assert lib.acefa_kv_prologue(r(src), r(src), r(dst), r(dst), r(pro), None) in (-6, -7)
+        assert lib.acefa_kv_prologue(r(src), None, r(dst), None, None, None) in (-6, -7)  # plain conversion
+
+
 def test_peer_entry_points_reject_null(lib):
     assert lib.acefa_peer_export(None, None, None) == -1
     assert lib.acefa_peer_import(None, 0, None) == -1
