@@ -795,12 +795,16 @@ def sharded_dit(device, stream, world, rank, iters=10, warmup=3):
 
 
 def run_dense_workload(args):
-    """--workload <dense name>: time one dense op (also the ncu profiling case)."""
+    """--workload <dense name>: time one dense op (also the ncu profiling case);
+    --workload dit6000_prologue: the DiT layer with its QK-norm + RoPE prologue."""
     import torch
 
     torch.cuda.set_device(0)
     device = torch.device("cuda", 0)
     stream = torch.cuda.Stream(device=device)
+    if args.workload == "dit6000_prologue":
+        emit({"workload": args.workload, **dit_prologue(device, stream, iters=args.steps)})
+        return 0
     r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup, rule=args.mask_rule)
     emit({"workload": args.workload, "mask_rule": bool(args.mask_rule), **r})
     return 0
@@ -840,7 +844,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (36 = the headline stack)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
     ap.add_argument("--workload", default="decode4b",
-                    help="decode4b (headline) or one dense op: " + ", ".join(DENSE_WORKLOADS))
+                    help="decode4b (headline), dit6000_prologue, or one dense op: " + ", ".join(DENSE_WORKLOADS))
     ap.add_argument("--mask-rule", action="store_true",
                     help="dense workload: give the mask by rule (acefa_flash_attn_ext_gen) instead of a tensor")
     args = ap.parse_args()

@@ -198,3 +198,34 @@ def test_full_size_prefill_config3_sampled_rows():
     c.k_cache_cpu = (kf / kf.pow(2).mean(-1, keepdim=True).sqrt()).half()
     c.to("cuda")
     run_case(c, rows=rows)
+
+
+def test_binary_mask_rows_with_holes():
+    """0 / -inf masks whose rows are single runs take arithmetic visibility
+    (the classify pass records each row's run); rows with holes, or with a
+    finite non-zero entry, keep reading the mask.  Mixed in one mask, over
+    several key chunks (n_kv 2300 = 18 key tiles, chunks of 8), both kinds
+    must meet the tolerance, and a row that is one run in every chunk but
+    broken across chunks must not pass as a run."""
+    n_q, n_kv = 256, 2300
+
+    def mk(m):
+        g = torch.Generator().manual_seed(4900)
+        m[:] = float("-inf")
+        for i in range(n_q):
+            a = int(torch.randint(0, n_kv - 64, (1,), generator=g))
+            b = int(torch.randint(a + 1, n_kv + 1, (1,), generator=g))
+            m[:, :, i, a:b] = 0.0
+            if i % 3 == 1 and b - a > 4:  # a hole: not a run any more
+                h = int(torch.randint(a + 1, b - 1, (1,), generator=g))
+                m[:, :, i, h] = float("-inf")
+            if i % 7 == 2:  # one run per chunk, two runs in the row
+                m[:, :, i, :] = float("-inf")
+                m[:, :, i, 100:900] = 0.0
+                m[:, :, i, 1500:2000] = 0.0
+            if i % 11 == 5:  # a finite non-zero entry: not binary
+                m[:, :, i, min(b, n_kv - 1)] = -2.5
+        return m
+
+    c = Case(4901, B=2, Hq=8, Hkv=4, n_q=n_q, n_kv=n_kv, mask=mk, m_batch=1)
+    assert_close(c.gpu(), c.oracle(), what="binary mask rows with holes")
