@@ -273,14 +273,20 @@ struct DensePlan {
     size_t ws_bytes;
 };
 
-// One CTA per SM at a time.  If the units do not fill the last wave, the
-// leftover units are cut into key ranges so that the last wave keeps nearly
-// every SM busy: only for unmasked nodes (every unit the same work; with a
-// causal mask the heavy-first order already packs the last wave) and only
-// when each range keeps at least 16 key tiles, so that a range outweighs its
-// fixed cost (Q conversion, partial write, merge).  At most 8 ranges.  A
-// function of shapes and the SM count only.
-DensePlan plan_dense(const OpDesc &o, int sm_count) {
+// One CTA per SM at a time.  The units that do not fill a whole last wave
+// ("tail") may be cut into key ranges run by separate CTAs and merged by
+// fa_dense_combine, so that the last wave ends sooner.  The split is chosen by
+// the estimated duration of that wave, in key-tile steps of one CTA: a CTA's
+// fixed cost (launch, Q conversion, output stores) measured ~5.6 steps and the
+// merge ~1.3 (per-CTA %globaltimer stamps on B200).  Only for unmasked nodes
+// (every unit the same work; a causal mask's heavy-first order already packs
+// the last wave), at most 8 ranges of at least 8 key tiles (shorter ranges
+// measured slower than no split: DiT S = 1500, 3 ranges of 4 tiles, -7 %),
+// the ranges of the tail within one wave, and the partial results within the
+// caller's workspace.  A function of shapes, the SM count and the workspace
+// size.
+DensePlan plan_dense(const OpDesc &o, int sm_count, size_t ws_limit) {
+    constexpr double kFixedSteps = 5.6, kMergeSteps = 1.3;
     DensePlan p;
     p.rows_total = o.G * o.n_q;
     p.n_rt       = (p.rows_total + kDenseBM - 1) / kDenseBM;
@@ -288,23 +294,32 @@ DensePlan plan_dense(const OpDesc &o, int sm_count) {
     p.n_kt       = (o.n_kv + kDenseBN - 1) / kDenseBN;
     // per-tile classes need one mask row per query: a mask shared by all heads
     p.classify          = o.mask != nullptr && o.m_ne2 == 1;
+    size_t b            = p.classify ? (size_t) o.m_ne3 * p.n_rt * p.n_kt : 0;
+    p.cls_bytes         = (b + 255) / 256 * 256;
     const int64_t units = (int64_t) p.n_pairs * o.B * o.Hkv;
     const int64_t sms   = sm_count > 0 ? sm_count : 1;
     const int64_t tail  = units % sms;
-    int64_t       split = 1;
-    if (o.mask == nullptr && o.mg_kind == 0 && units >= sms && tail > 0 && tail <= sms / 2) {
-        split = std::min<int64_t>(std::min<int64_t>(sms / tail, kDenseMaxSplit), p.n_kt / 16);
-        if (split < 2) {
-            split = 1;
+    auto part_bytes     = [&](int64_t split) {
+        return (size_t) tail * (size_t) split * 2 * dense_part_floats() * sizeof(float);
+    };
+    int64_t split = 1;
+    if (o.mask == nullptr && o.mg_kind == 0 && tail > 0) {
+        double best = kFixedSteps + (double) p.n_kt;
+        for (int64_t sp = 2; sp <= kDenseMaxSplit && tail * sp <= sms && p.n_kt / sp >= 8; ++sp) {
+            if (p.cls_bytes + part_bytes(sp) > ws_limit) {
+                break;
+            }
+            const double t = kMergeSteps + kFixedSteps + (double) ((p.n_kt + sp - 1) / sp);
+            if (t < best) {
+                best  = t;
+                split = sp;
+            }
         }
     }
-    p.n_split     = (int) split;
-    p.n_tail      = split > 1 ? (int) tail : 0;
-    p.n_full      = (int) (units - p.n_tail);
-    size_t b      = p.classify ? (size_t) o.m_ne3 * p.n_rt * p.n_kt : 0;
-    p.cls_bytes   = (b + 255) / 256 * 256;
-    size_t part   = (size_t) p.n_tail * p.n_split * 2 * dense_part_floats() * sizeof(float);
-    p.ws_bytes    = p.cls_bytes + part;
+    p.n_split  = (int) split;
+    p.n_tail   = split > 1 ? (int) tail : 0;
+    p.n_full   = (int) (units - p.n_tail);
+    p.ws_bytes = p.cls_bytes + (split > 1 ? part_bytes(split) : 0);
     if (p.ws_bytes == 0) {
         p.ws_bytes = 256;
     }
@@ -469,7 +484,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         if (app) {
             return ACEFA_ERR_SHAPE;  // the fused append serves the decode path (one new row per set)
         }
-        const DensePlan dp = plan_dense(c.op, di->sm_count);
+        const DensePlan dp = plan_dense(c.op, di->sm_count, workspace_bytes);
         if (workspace_bytes < dp.ws_bytes || !workspace || !aligned(workspace, 256)) {
             return ACEFA_ERR_WORKSPACE;
         }
@@ -568,7 +583,7 @@ ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor
         return 0;
     }
     if (use_dense(c.op)) {
-        return plan_dense(c.op, di->sm_count).ws_bytes;
+        return plan_dense(c.op, di->sm_count, SIZE_MAX).ws_bytes;
     }
     return plan_decode(c.op, di->sm_count).ws_bytes;
 }
