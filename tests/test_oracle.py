@@ -106,3 +106,45 @@ def test_rope_norm_matches_qwen3_definition(oracle_mod, name):
     # without a weight nothing is normalised; without theta nothing rotates
     x = z["x"][:2]
     assert np.array_equal(oracle_mod.rope_norm(x, None, 1e-6, 0.0, None), x)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,nq,nkv,kind", [(2, 8, 2, 1, 300, "valid"), (1, 8, 4, 40, 70, "causal"),
+                                                  (2, 4, 4, 33, 33, "window"), (1, 6, 2, 17, 45, "holes")])
+def test_oracle_matches_torch_sdpa(oracle_mod, B, Hq, Hkv, nq, nkv, kind):
+    """The oracle's F32 mode against an implementation it shares no code with:
+    PyTorch's scaled_dot_product_attention in float64 on the CPU (GQA by head
+    repetition), for the parts of the contract SDPA expresses -- scale, GQA,
+    additive 0 / -inf masks in the shapes acestep.cpp builds.  Rows with no
+    visible key are left out (SDPA returns NaN there, ggml 0)."""
+    import torch
+
+    rng = np.random.default_rng(77 + nq)
+    D = 64
+    q = rng.standard_normal((B, Hq, nq, D)).astype(np.float32)
+    k = rng.standard_normal((B, Hkv, nkv, D)).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, nkv, D)).astype(np.float16)
+    i = np.arange(nq)[:, None]
+    j = np.arange(nkv)[None, :]
+    if kind == "valid":
+        vis = np.stack([j < 150, j < 300])[:, None].repeat(nq, axis=1)[:, :, 0][:, None]
+        vis = np.broadcast_to(vis, (B, 1, nq, nkv))
+    elif kind == "causal":
+        vis = np.broadcast_to(j <= i + (nkv - nq), (B, 1, nq, nkv))
+    elif kind == "window":
+        vis = np.broadcast_to(np.abs(i - j) <= 5, (B, 1, nq, nkv))
+    else:
+        vis = np.broadcast_to(rng.random((1, 1, nq, nkv)) < 0.6, (B, 1, nq, nkv))
+    mask = np.where(vis, 0.0, -np.inf).astype(np.float16)
+    scale = D ** -0.5
+    got = oracle_mod.flash_attn_ext(q, k, v, mask, None, scale=scale)  # (B, nq, Hq, D)
+    rep = Hq // Hkv
+    tq = torch.from_numpy(q).double()
+    tk = torch.from_numpy(k.astype(np.float32)).double().repeat_interleave(rep, dim=1)
+    tv = torch.from_numpy(v.astype(np.float32)).double().repeat_interleave(rep, dim=1)
+    tm = torch.from_numpy(mask.astype(np.float32)).double()
+    want = torch.nn.functional.scaled_dot_product_attention(tq, tk, tv, attn_mask=tm, scale=scale)
+    want = want.permute(0, 2, 1, 3).numpy()  # (B, nq, Hq, D)
+    rows = vis[:, 0].any(axis=-1)  # (B, nq)
+    sel = np.broadcast_to(rows[:, :, None, None], want.shape)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got[sel], want[sel], rtol=0, atol=2e-5)
