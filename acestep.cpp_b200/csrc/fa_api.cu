@@ -6,10 +6,12 @@
 // dst->src[0..4] and dst->op_params {scale, max_bias, logit_softcap}) without any
 // ggml type in the signature.  Status codes replace ggml's GGML_ABORT.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "fa_internal.h"
 #include "ptx.cuh"
@@ -26,12 +28,13 @@ thread_local int t_last_path     = 0;
 constexpr int kMaxDevices = 64;
 
 struct DevInfo {
-    int  sm_count = 0;
-    int  cc_major = 0, cc_minor = 0;
-    int *err_ptr  = nullptr;
-    bool ready    = false;
+    int               sm_count = 0;
+    int               cc_major = 0, cc_minor = 0;
+    int              *err_ptr  = nullptr;
+    std::atomic<bool> ready{false};  // set once the fields above are filled
 };
-DevInfo g_dev[kMaxDevices];  // immutable once ready (per-device properties cache)
+DevInfo    g_dev[kMaxDevices];  // per-device properties, immutable once ready
+std::mutex g_dev_mutex;         // serialises the one-time fill
 
 int dev_info(DevInfo **out) {
     int dev = 0;
@@ -39,18 +42,23 @@ int dev_info(DevInfo **out) {
         return ACEFA_ERR_CUDA;
     }
     DevInfo &d = g_dev[dev];
-    if (!d.ready) {
-        if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
-            return ACEFA_ERR_CUDA;
+    if (!d.ready.load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lock(g_dev_mutex);
+        if (!d.ready.load(std::memory_order_relaxed)) {  // retried on a later call if it fails
+            int   sm = 0, major = 0, minor = 0;
+            void *p  = nullptr;
+            if (cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+                cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) {
+                return ACEFA_ERR_CUDA;
+            }
+            d.sm_count = sm;
+            d.cc_major = major;
+            d.cc_minor = minor;
+            d.err_ptr  = static_cast<int *>(p);
+            d.ready.store(true, std::memory_order_release);
         }
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) {
-            return ACEFA_ERR_CUDA;
-        }
-        d.err_ptr = static_cast<int *>(p);
-        d.ready   = true;
     }
     if (d.cc_major != 10 || d.cc_minor != 0) {
         return ACEFA_ERR_DEVICE;
@@ -65,25 +73,24 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (fn == nullptr) {
-        void                            *p = nullptr;
-        cudaDriverEntryPointQueryResult  q;
+    static const EncodeTiledFn fn = [] {  // thread-safe one-time lookup
+        void                           *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess) {
-            fn = reinterpret_cast<EncodeTiledFn>(p);
+            return reinterpret_cast<EncodeTiledFn>(p);
         }
-    }
+        return static_cast<EncodeTiledFn>(nullptr);
+    }();
     return fn;
 }
 
 uint64_t wait_limit_ns() {
-    static uint64_t lim = 0;
-    if (lim == 0) {
+    static const uint64_t lim = [] {
         const char *e  = std::getenv("ACEFA_WAIT_LIMIT_MS");
         long        ms = e ? std::atol(e) : 0;
-        lim            = (ms > 0 ? (uint64_t) ms : 1000ull) * 1000000ull;
-    }
+        return (ms > 0 ? (uint64_t) ms : 1000ull) * 1000000ull;
+    }();
     return lim;
 }
 
