@@ -4,7 +4,6 @@ src/qwen3-lm.h:776-777).  The fused call must leave exactly the cache a
 separate append would (F16 / BF16 rounding, Q8_0 blocks bit-exact with ggml's
 quantiser) and produce exactly the output of acefa_flash_attn_ext on that
 cache: both kernels are deterministic, so the comparison is bit for bit."""
-import numpy as np
 import pytest
 import torch
 

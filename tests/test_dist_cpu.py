@@ -12,7 +12,6 @@ import datetime
 import os
 import socket
 
-import numpy as np
 import pytest
 import torch
 import torch.distributed as dist

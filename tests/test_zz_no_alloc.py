@@ -9,7 +9,6 @@ collected last so that a stopping run has already exercised everything else.
 """
 import ctypes
 
-import numpy as np
 import pytest
 import torch
 
