@@ -399,9 +399,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const OpDesc &o    = P.op;
     const int     warp = threadIdx.x >> 5;
     const int     lane = threadIdx.x & 31;
-    // 1-D grid of work units, pair index slowest and descending: every (batch,
-    // head) unit's late (for causal masks, heaviest) row tiles are scheduled
-    // first.  CTAs past n_full each take one key range of a split unit.
+    // 1-D grid of work units.  Masked nodes: pair index slowest and descending,
+    // so every (batch, head)'s late (for causal masks, heaviest) row tiles are
+    // scheduled first.  Unmasked nodes (every unit the same work): (batch, kv
+    // head) slowest, so the CTAs in flight share few heads' K/V and re-read them
+    // from L2.  CTAs past n_full each take one key range of a split unit.
     const int     units   = o.B * o.Hkv;
     const bool    is_part = (int) blockIdx.x >= P.n_full;
     const int     xs      = (int) blockIdx.x - P.n_full;
@@ -409,9 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int     sp      = is_part ? xs % P.n_split : 0;
     const int     kt_lo   = is_part ? (int) ((int64_t) P.n_kt * sp / P.n_split) : 0;
     const int     kt_hi   = is_part ? (int) ((int64_t) P.n_kt * (sp + 1) / P.n_split) : P.n_kt;
-    const int     pair    = P.n_pairs - 1 - unit_id / units;
-    const int     hk      = (unit_id % units) % o.Hkv;
-    const int     b       = (unit_id % units) / o.Hkv;
+    const int     pair    = P.head_major ? unit_id % P.n_pairs : P.n_pairs - 1 - unit_id / units;
+    const int     bh      = P.head_major ? unit_id / P.n_pairs : unit_id % units;
+    const int     hk      = bh % o.Hkv;
+    const int     b       = bh / o.Hkv;
     const int     bk   = b / o.rk3;
     const int     t0   = 2 * pair;
     const bool    has_tile[2] = {t0 < P.n_rt, t0 + 1 < P.n_rt};
@@ -1107,9 +1110,10 @@ __global__ void __launch_bounds__(kDenseBM) fa_dense_combine(const __grid_consta
     const int     r     = threadIdx.x;
     const int     units = o.B * o.Hkv;
     const int     unit  = P.n_full + t;
-    const int     pair  = P.n_pairs - 1 - unit / units;
-    const int     hk    = (unit % units) % o.Hkv;
-    const int     b     = (unit % units) / o.Hkv;
+    const int     pair  = P.head_major ? unit % P.n_pairs : P.n_pairs - 1 - unit / units;
+    const int     bh    = P.head_major ? unit / P.n_pairs : unit % units;
+    const int     hk    = bh % o.Hkv;
+    const int     b     = bh / o.Hkv;
     const int     gr    = (2 * pair + i) * kDenseBM + r;
     pdl_wait_primary();
     if (2 * pair + i >= P.n_rt || gr >= P.rows_total) {

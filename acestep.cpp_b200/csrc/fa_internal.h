@@ -159,10 +159,11 @@ constexpr uint8_t kClsBounds = 4;  // tile runs past n_kv
 constexpr uint8_t kClsBinary = 8;  // every mask entry of the tile is 0 or -inf
 
 // Work units are (row-tile pair, batch, kv head), numbered pair-major from
-// the heaviest pair.  The first n_full units run whole, one CTA each; when the
-// last wave would leave most SMs idle, each of the n_tail remaining units is
-// cut into n_split key ranges run by separate CTAs, which write unnormalised
-// partial results (O, running max, row sum) that fa_dense_combine merges.
+// the heaviest pair (head-major for unmasked nodes).  The first n_full units
+// run whole, one CTA each; when the last wave would leave most SMs idle, each
+// of the n_tail remaining units is cut into n_split key ranges run by
+// separate CTAs, which write unnormalised partial results (O, running max,
+// row sum) that fa_dense_combine merges.
 struct DenseParams {
     OpDesc         op;
     int            rows_total;  // G * n_q rows per (b, hk) unit
@@ -172,6 +173,7 @@ struct DenseParams {
     int            n_full;      // units run whole
     int            n_tail;      // units split over key ranges
     int            n_split;     // key ranges per split unit (1 = none)
+    int            head_major;  // units numbered (batch, kv head) slowest: a head's pairs run together
     const uint8_t *cls;         // [m_ne3][n_rt][n_kt] classes, or nullptr (no per-tile info)
     uint8_t       *cls_out;     // same buffer, written by the classify pre-pass
     float         *part;        // [n_tail][n_split][2 tiles] partial slots (dense_part_floats each)
