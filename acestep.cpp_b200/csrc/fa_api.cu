@@ -568,6 +568,25 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
     return ACEFA_OK;
 }
 
+// Workspace the operator needs when the caller offers at most `limit` bytes:
+// the dense plan shrinks its last-wave split to fit (down to no split), so a
+// smaller offer can need less.  0 = unsupported operands or no device.
+size_t acefa::workspace_bytes_within(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                                     const acefa_tensor *mask, const acefa_tensor *dst, size_t limit) {
+    Checked c = check_operands(q, k, v, mask, nullptr, dst);
+    if (c.status != ACEFA_OK) {
+        return 0;
+    }
+    DevInfo *di = nullptr;
+    if (dev_info(&di) != ACEFA_OK) {
+        return 0;
+    }
+    if (use_dense(c.op)) {
+        return plan_dense(c.op, di->sm_count, limit).ws_bytes;
+    }
+    return plan_decode(c.op, di->sm_count).ws_bytes;
+}
+
 extern "C" {
 
 ACEFA_API int acefa_check(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
@@ -582,18 +601,7 @@ ACEFA_API int acefa_supports(const acefa_tensor *q, const acefa_tensor *k, const
 
 ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
                                        const acefa_tensor *mask, const acefa_tensor *dst) {
-    Checked c = check_operands(q, k, v, mask, nullptr, dst);
-    if (c.status != ACEFA_OK) {
-        return 0;
-    }
-    DevInfo *di = nullptr;
-    if (dev_info(&di) != ACEFA_OK) {
-        return 0;
-    }
-    if (use_dense(c.op)) {
-        return plan_dense(c.op, di->sm_count, SIZE_MAX).ws_bytes;
-    }
-    return plan_decode(c.op, di->sm_count).ws_bytes;
+    return acefa::workspace_bytes_within(q, k, v, mask, dst, SIZE_MAX);
 }
 
 ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,

@@ -194,6 +194,12 @@ struct DenseLaunch {
 
 cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches);
 
+// ------------------------------------------------------------------ workspace
+// Bytes of workspace the operator needs when it is offered at most `limit`
+// (acefa_workspace_bytes is limit = SIZE_MAX); 0 for unsupported operands.
+size_t workspace_bytes_within(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
+                              const acefa_tensor *mask, const acefa_tensor *dst, size_t limit);
+
 // ------------------------------------------------------------------ K/V prologue
 int kv_prologue_launch(const acefa_tensor *k_src, const acefa_tensor *v_src, const acefa_tensor *k_dst,
                        const acefa_tensor *v_dst, const RopeNorm &kp, int sm_count, cudaStream_t stream);

@@ -69,7 +69,10 @@ extern "C" ACEFA_API int acefa_flash_attn_ext_noalloc(const acefa_tensor *q, con
     if (st != ACEFA_OK) {
         return st;
     }
-    const size_t need = acefa_workspace_bytes(q, k, v, mask, dst);
+    // Sized with the same limit the call below passes: the dense plan then
+    // cuts its last-wave split (or drops it) to fit the fixed array, so only
+    // operands whose smallest plan exceeds it are refused.
+    const size_t need = acefa::workspace_bytes_within(q, k, v, mask, dst, acefa::kNoAllocScratchBytes);
     if (need == 0) {
         return ACEFA_ERR_DEVICE;  // operands are valid, so the device query failed
     }

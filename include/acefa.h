@@ -106,11 +106,16 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
  *
  * Arguments and results are those of acefa_flash_attn_ext() without the
  * workspace pair.  The split-KV scratch is a fixed 8 MiB array inside the
- * library, one per GPU, held from library load until process exit; operands
- * whose acefa_workspace_bytes() exceeds 8 MiB are refused with
+ * library, one per GPU, held from library load until process exit.  The call
+ * plans its work for that 8 MiB (the dense path shrinks or drops its last-wave
+ * key-range split to fit, exactly as acefa_flash_attn_ext would with an 8 MiB
+ * workspace); operands that need more even then -- a decode node with very many
+ * split-KV partials, a mask class table over 8 MiB -- are refused with
  * ACEFA_ERR_NOALLOC_LIMIT and nothing is launched.  The first call on each
  * device looks up that array's device address (with the device current), so
- * make that first call before any stream capture.  Every call on a device
+ * make that first call before any stream capture.  The address is kept for the
+ * life of the process: after cudaDeviceReset() on a device this entry (like the
+ * engine's device error word) must not be used on it again.  Every call on a device
  * shares the array: calls whose kernels may overlap on the GPU (other streams or
  * other threads without ordering) race and must be serialised by the caller.
  * Nothing is allocated, freed or zeroed by the call.
@@ -306,7 +311,12 @@ ACEFA_API int acefa_check(const acefa_tensor *q, const acefa_tensor *k, const ac
 
 /* Reads and clears the device-side error word set by bounded waits inside the
  * kernels (0 = none).  Synchronises `stream`; for diagnostics, not hot paths.
- * Returns a negative acefa_status if the read itself fails. */
+ * There is ONE word per device, shared by every stream and thread using the
+ * engine on it: the first code recorded since the last read is kept, whichever
+ * call's kernel recorded it, and a read from one stream also clears what a
+ * kernel on another stream recorded.  Callers that run the engine on several
+ * streams of one device and need to know which call failed read it with those
+ * streams idle.  Returns a negative acefa_status if the read itself fails. */
 ACEFA_API int acefa_device_error(void *stream);
 
 /* Human-readable name of an acefa_status. */

@@ -9,11 +9,15 @@ collected last so that a stopping run has already exercised everything else.
 """
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
 import acefa
+import oracle
 from fa_cases import Case, assert_close
+
+NOALLOC_BYTES = 8 << 20  # the fixed array's size, as include/acefa.h states it
 
 pytestmark = pytest.mark.gpu
 
@@ -46,6 +50,53 @@ def test_noalloc_matches_allocating_entry_twice(kv):
         torch.cuda.synchronize()
         assert_close(op.out.cpu().numpy(), want.cpu().numpy(), what=f"noalloc {kv}")
         assert acefa.device_error() == 0
+
+
+def _oracle_rows(c, rows):
+    q = np.ascontiguousarray(c.q_cpu.numpy()[:, :, rows])
+    kc = c.k_cache_cpu.numpy()[:, :, :c.n_kv]
+    vc = c.v_cache_cpu.numpy()[:, :, :c.n_kv]
+    m = None if c.mask_cpu is None else np.ascontiguousarray(c.mask_cpu.numpy()[:, :, rows])
+    return oracle.flash_attn_ext(q, kc, vc, m, scale=c.D ** -0.5, k_type=oracle.GGML_F16, v_type=oracle.GGML_F16,
+                                 d=c.D, dv=c.D)
+
+
+def test_noalloc_dense_runs_within_the_fixed_array():
+    """Dense (tcgen05) operands whose preferred last-wave split would need more
+    scratch than the fixed array holds: 512 work units on 148 SMs leave 68 in
+    the last wave, and splitting them would take ~18 MB of partials.  Given
+    8 MiB, the plan drops the split instead of refusing the call.  The result
+    must equal, bit for bit, the allocating entry given an 8 MiB workspace
+    (the same plan), and meet the oracle on sampled rows -- on a second call
+    too, after a decode call and a masked dense call have left their own data
+    in the shared array."""
+    rows = [0, 1, 127, 128, 2047, 4095]
+    big = Case(4244, B=1, Hq=32, Hkv=8, n_q=4096, n_kv=4096, mask=None)
+    # a decode call and a masked dense call (class table in the array) between the two dense runs
+    dec = Case(4245, B=8, Hq=32, Hkv=8, n_q=1, n_kv=1536, mask="valid", valid=[1536 - 100 * i for i in range(8)])
+    msk = Case(4246, B=2, Hq=16, Hkv=8, n_q=700, n_kv=900, mask="random", m_batch=1)
+    ref_big = big.op()
+    ref_big.workspace = torch.empty(NOALLOC_BYTES, dtype=torch.uint8, device="cuda")
+    want_big = ref_big().clone()
+    assert acefa.last_path() == 2
+    want_msk = msk.op()().clone()
+    want_dec = dec.op()().clone()
+    torch.cuda.synchronize()
+    for rep in range(2):
+        for c, want in ((big, want_big), (dec, want_dec), (msk, want_msk)):
+            op = c.op()
+            op.out.fill_(float("nan"))
+            st = _noalloc(op)
+            assert st == 0, acefa.STATUS_NAMES.get(st, st)
+            torch.cuda.synchronize()
+            got = op.out.cpu().numpy()
+            if c is big:
+                assert np.array_equal(got, want.cpu().numpy()), f"dense no-alloc call {rep} differs"
+                assert_close(got[:, rows], _oracle_rows(c, rows), what=f"dense noalloc rows, call {rep}")
+            else:
+                assert_close(got, want.cpu().numpy(), what=f"noalloc call {rep}")
+    assert_close(want_msk.cpu().numpy(), msk.oracle(), what="masked dense vs oracle")
+    assert acefa.device_error() == 0
 
 
 def test_noalloc_refuses_oversized_operands():
