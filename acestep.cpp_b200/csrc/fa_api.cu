@@ -236,27 +236,22 @@ void set_scalars(OpDesc &o, float scale, float max_bias, float softcap) {
 }
 
 // ------------------------------------------------------------------ decode plan
+// A unit (batch, kv head, 16-row block) runs on a cluster of C CTAs that split
+// its keys and merge through distributed shared memory.  C is the largest
+// power of two (<= the unit's key tiles) for which the device keeps every
+// unit's cluster resident at once, so the op runs in one wave; units beyond
+// that run one CTA each.  A function of shapes and the device only.
 struct DecodePlan {
-    int     n_rb, units, tpu, n_ctas;
-    int64_t total_tiles;
-    size_t  ws_bytes;
+    int n_rb, units, tpu, cluster;
 };
 
-DecodePlan plan_decode(const OpDesc &o, int sm_count) {
+DecodePlan plan_decode(const OpDesc &o, bool prologue) {
     DecodePlan p;
-    const int rows   = o.G * o.n_q;
-    p.n_rb           = (rows + kDecRows - 1) / kDecRows;
-    p.units          = o.B * o.Hkv * p.n_rb;
-    p.tpu            = (o.n_kv + kDecBN - 1) / kDecBN;
-    p.total_tiles    = (int64_t) p.units * p.tpu;
-    // persistent CTAs fill the SMs, but no unit is cut into more than
-    // ~kDecMaxParts pieces (small ops would otherwise pay for a wide combine)
-    int64_t cap = (int64_t) sm_count * decode_ctas_per_sm(o.kv_type, o.D);
-    const int64_t part_cap = (int64_t) p.units * kDecMaxParts;
-    cap = cap < part_cap ? cap : part_cap;
-    p.n_ctas         = (int) (p.total_tiles < cap ? p.total_tiles : cap);
-    p.ws_bytes       = (size_t) (p.n_ctas + p.units) * (size_t) dec_slot_floats(o.D) * sizeof(float);
-    p.ws_bytes       = (p.ws_bytes + 255) / 256 * 256;
+    const int rows = o.G * o.n_q;
+    p.n_rb         = (rows + kDecRows - 1) / kDecRows;
+    p.units        = o.B * o.Hkv * p.n_rb;
+    p.tpu          = (o.n_kv + kDecBN - 1) / kDecBN;
+    p.cluster      = decode_cluster(o.kv_type, o.D, prologue, p.units, p.tpu);
     return p;
 }
 
@@ -526,9 +521,11 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         return ACEFA_OK;
     }
 
-    DecodePlan plan = plan_decode(c.op, di->sm_count);
-    if (workspace_bytes < plan.ws_bytes || (plan.ws_bytes && (!workspace || !aligned(workspace, 256)))) {
-        return ACEFA_ERR_WORKSPACE;
+    // the decode path needs no workspace: split keys merge inside the cluster
+    const bool pro  = c.op.qp.on || kp.on;
+    DecodePlan plan = plan_decode(c.op, pro);
+    if ((int64_t) plan.units * plan.cluster >= (1ll << 31)) {
+        return ACEFA_ERR_SHAPE;
     }
     DecodeLaunch L;
     std::memset(&L, 0, sizeof(L));
@@ -536,9 +533,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
     L.p.n_rb           = plan.n_rb;
     L.p.units          = plan.units;
     L.p.tiles_per_unit = plan.tpu;
-    L.p.total_tiles    = plan.total_tiles;
-    L.p.n_ctas         = plan.n_ctas;
-    L.p.div32          = (uint64_t) plan.total_tiles * (uint64_t) (plan.n_ctas + 1) < (1ull << 32) ? 1 : 0;
+    L.p.cluster        = plan.cluster;
     if (app) {
         L.p.k_new      = app->k_new;
         L.p.v_new      = app->v_new;
@@ -549,7 +544,6 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         L.p.append_pos = app->pos;
         L.p.kp         = kp;
     }
-    L.p.partials       = static_cast<float *>(workspace);
     L.p.dev_err        = di->err_ptr;
     L.p.wait_limit_ns  = wait_limit_ns();
     if (c.op.kv_type != ACEFA_TYPE_Q8_0) {
@@ -584,7 +578,7 @@ size_t acefa::workspace_bytes_within(const acefa_tensor *q, const acefa_tensor *
     if (use_dense(c.op)) {
         return plan_dense(c.op, di->sm_count, limit).ws_bytes;
     }
-    return plan_decode(c.op, di->sm_count).ws_bytes;
+    return 256;  // the decode path uses none; a nonzero size marks the operands supported
 }
 
 extern "C" {

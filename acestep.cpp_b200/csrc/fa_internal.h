@@ -103,23 +103,22 @@ __host__ __device__ inline float alibi_slope(const OpDesc &o, int h) {
 // ------------------------------------------------------------------ decode
 // The split-KV decode kernel works on "units" (batch b, kv head hk, row block
 // rb); a unit's rows are the G*n_q (query, head) pairs that share one K/V head,
-// 16 at a time.  Its keys are cut into tiles of kDecBN positions and the
-// flattened (unit, tile) list is split evenly over the persistent CTAs.
-constexpr int kDecBN      = 64;  // keys per pipeline stage
-constexpr int kDecWarps   = 4;   // consumer warps (16 keys each per stage)
-constexpr int kDecStages  = 3;   // pipeline depth
-constexpr int kDecRows    = 16;  // rows per unit (one m16 MMA tile)
-constexpr int kDecMaxParts = 15; // cap on CTAs sharing one unit (bounds the combine)
+// 16 at a time.  Its keys are cut into tiles of kDecBN positions.  A unit runs
+// on one thread-block cluster of `cluster` CTAs, each streaming a contiguous
+// range of the unit's tiles; the CTAs merge their partial results through
+// distributed shared memory, so the op is one launch and needs no workspace.
+constexpr int kDecBN         = 64;  // keys per pipeline stage
+constexpr int kDecWarps      = 4;   // consumer warps (16 keys each per stage)
+constexpr int kDecStages     = 3;   // pipeline depth
+constexpr int kDecRows       = 16;  // rows per unit (one m16 MMA tile)
+constexpr int kDecMaxCluster = 16;  // CTAs per unit (16 needs the non-portable cluster size)
 
 struct DecodeParams {
     OpDesc  op;
     int     n_rb;            // row blocks per (b, hk)
     int     units;           // B * Hkv * n_rb
     int     tiles_per_unit;  // ceil(n_kv / kDecBN)
-    int64_t total_tiles;     // units * tiles_per_unit
-    int     n_ctas;          // persistent CTAs
-    int     div32;           // total_tiles * (n_ctas + 1) < 2^32: tile/CTA arithmetic fits 32-bit division
-    float  *partials;        // workspace: (n_ctas + units) slots
+    int     cluster;         // CTAs per unit (grid = units * cluster)
     // Fused KV-cache append (acefa_flash_attn_ext_append), or all null: the
     // new K/V row of (kv head h, set s) is f32 at k_new + h*kn_nb2 + s*kn_nb3
     // and goes into cache row append_pos[s] before that row is read.
@@ -131,18 +130,16 @@ struct DecodeParams {
     uint64_t wait_limit_ns;
 };
 
-// Slot layout: m[kDecRows], l[kDecRows], O[kDecRows][D] (f32).
-__host__ __device__ inline int64_t dec_slot_floats(int D) { return (int64_t) kDecRows * (D + 2); }
-
 struct DecodeLaunch {
     DecodeParams p;
     CUtensorMap  kmap, vmap;  // F16/BF16 tiles via TMA (unused for Q8_0)
 };
 
 cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches);
-bool        decode_needs_combine(const DecodeParams &p);
-int         decode_ctas_per_sm(int kv_type, int D);
-size_t      decode_smem_bytes(int kv_type, int D);
+// CTAs per unit for the decode kernel of these operands on the current
+// device: the largest power of two (<= kDecMaxCluster, <= the unit's key
+// tiles) whose clusters for all `units` are resident at once; 1 otherwise.
+int         decode_cluster(int kv_type, int D, bool prologue, int units, int tiles_per_unit);
 
 // ------------------------------------------------------------------ dense
 // tcgen05 kernel for query-heavy nodes (LM prefill, DiT self/cross, encoders):

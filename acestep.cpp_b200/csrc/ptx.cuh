@@ -20,6 +20,7 @@ enum : int {
     DEVERR_TIMEOUT_MMA   = 3,  // tensor-core completion never signalled
     DEVERR_TIMEOUT_DRAIN = 4,  // in-flight copies did not land while aborting
     DEVERR_APPEND_POS    = 5,  // an append position outside [0, n_kv): row not written
+    DEVERR_TIMEOUT_PEER  = 6,  // a CTA of the cluster never published its partial result
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -199,6 +200,55 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // Named barrier over a subset of warps (id 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- clusters
+// Shared memory of the other CTAs of this thread-block cluster (distributed
+// shared memory).  Only plain loads and mbarrier arrivals cross CTAs here; no
+// bulk or tensor copy in this file reads another CTA's or another GPU's memory.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every non-exited thread of the cluster arrives, then waits for the others.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Address in CTA `rank`'s shared memory of the variable this CTA has at `addr`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// Arrive on an mbarrier of any CTA of the cluster, releasing this thread's
+// prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t cluster_addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
 }
 
 // Programmatic dependent launch controls (no-ops without the launch attribute).

@@ -165,9 +165,28 @@ def test_distance_to_ggml_cpu_arithmetic():
     assert cosine(got, g16) > 0.999
 
 
-def test_workspace_too_small_is_rejected():
-    c = Case(1200, B=1, Hq=16, Hkv=8, n_q=1, n_kv=2048)
+def test_decode_needs_no_workspace():
+    """Split keys merge inside the thread-block cluster: the decode path runs
+    with no workspace at all (NULL, 0 bytes) and gives the same result."""
+    c = Case(1200, B=16, Hq=32, Hkv=8, n_q=1, n_kv=2048, mask="valid", valid=[2048 - 61 * i for i in range(16)])
     op = c.op()
+    want = op().clone()
+    assert acefa.last_launch_count() == 1 and acefa.last_path() == 1
+    op.out.fill_(float("nan"))
+    st = op.lib.acefa_flash_attn_ext(
+        acefa._ref(op.tq), acefa._ref(op.tk), acefa._ref(op.tv), acefa._ref(op.tm), None, acefa._ref(op.td),
+        op.scale, 0.0, 0.0, op.prec, None, None, 0)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(op.out, want)
+    assert_close(want.cpu().numpy(), c.oracle())
+
+
+def test_workspace_too_small_is_rejected():
+    """The dense path's mask class table lives in the workspace."""
+    c = Case(1201, B=1, Hq=16, Hkv=8, n_q=600, n_kv=700, mask="random")
+    op = c.op()
+    assert op.ws_bytes >= 256
     op.workspace = op.workspace[: max(op.ws_bytes // 2, 1)]
     with pytest.raises(acefa.AcefaError) as e:
         op()

@@ -100,10 +100,11 @@ def test_noalloc_dense_runs_within_the_fixed_array():
 
 
 def test_noalloc_refuses_oversized_operands():
-    # 256 KV sets x 8 heads need far more than the fixed 8 MiB of split-KV
-    # partials; descriptors only (nothing is launched, so no memory behind them)
+    # A masked dense node whose mask-class table alone (one byte per mask batch
+    # x 128-row tile x 128-key tile: 160 x 128 x 512 = 10 MiB) exceeds the fixed
+    # 8 MiB; descriptors only (nothing is launched, so no memory behind them)
     lib = acefa.load_library()
-    D, Hq, Hkv, B, nkv = 128, 32, 8, 256, 8192
+    D, Hq, Hkv, B, nkv, nq = 128, 8, 8, 160, 65536, 16384
 
     def td(ne, es, gtype):
         t = acefa.Tensor()
@@ -116,11 +117,11 @@ def test_noalloc_refuses_oversized_operands():
         t.data = 1 << 20
         return t
 
-    q = td([D, 1, Hq, B], 4, acefa.GGML_F32)
+    q = td([D, nq, Hq, B], 4, acefa.GGML_F32)
     k = td([D, nkv, Hkv, B], 2, acefa.GGML_F16)
     v = td([D, nkv, Hkv, B], 2, acefa.GGML_F16)
-    m = td([nkv, 1, 1, B], 2, acefa.GGML_F16)
-    d = td([D, Hq, 1, B], 4, acefa.GGML_F32)
+    m = td([nkv, nq, 1, B], 2, acefa.GGML_F16)
+    d = td([D, Hq, nq, B], 4, acefa.GGML_F32)
     r = ctypes.byref
     assert lib.acefa_workspace_bytes(r(q), r(k), r(v), r(m), r(d)) > (8 << 20)
     st = lib.acefa_flash_attn_ext_noalloc(r(q), r(k), r(v), r(m), None, r(d), 0.088, 0.0, 0.0, 10, None)
