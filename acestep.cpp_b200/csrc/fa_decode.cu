@@ -42,6 +42,18 @@
 #ifndef ACEFA_DEC_MAX_CLUSTER
 #define ACEFA_DEC_MAX_CLUSTER 16
 #endif
+// Q8_0 pipeline shape (tuning macros): raw stages in flight, and converted-K
+// slots (2 lets K of the next tile be converted while the current one is
+// scored; 1 leaves the shared memory to a fourth raw stage).
+#ifndef ACEFA_Q8_STAGES
+#define ACEFA_Q8_STAGES 4
+#endif
+#ifndef ACEFA_Q8_KSLOTS
+#define ACEFA_Q8_KSLOTS 1
+#endif
+#ifndef ACEFA_Q8_CONV_UNROLL
+#define ACEFA_Q8_CONV_UNROLL 1
+#endif
 
 namespace acefa {
 
@@ -59,30 +71,39 @@ struct DecCfg {
     static constexpr int  kRowBytes   = kQ8 ? D / 32 * 34 : D * 2;  // one cache row
     // a 64-key tile of 16-bit values: D/64 swizzled boxes of 64 keys x 128 B
     static constexpr int  kF16Tile    = kDecBN * D * 2;
-    // staged raw tile: F16/BF16 = the TMA boxes; Q8_0 = whole block rows plus
-    // up to 15 lead bytes, rounded to keep stages 1 KB aligned
-    static constexpr int  kRawTile    = kQ8 ? ((kDecBN * kRowBytes + 16) + 1023) / 1024 * 1024 : kF16Tile;
+    // staged raw tile: F16/BF16 = the TMA boxes (1 KB aligned for the 128-B
+    // swizzle); Q8_0 = whole block rows plus up to 15 lead bytes (bulk copies
+    // only need 16-B alignment)
+    static constexpr int  kRawTile    = kQ8 ? (kDecBN * kRowBytes + 16 + 15) / 16 * 16 : kF16Tile;
     static constexpr int  kMaskBytes  = kDecRows * kDecBN * 2;  // up to 16 mask rows x 64 keys (f16)
     static constexpr int  kStageBytes = 2 * kRawTile + kMaskBytes;
-    static_assert(kStageBytes % 1024 == 0, "stages must stay 1 KB aligned");
+    static constexpr int  kStages     = kQ8 ? ACEFA_Q8_STAGES : kDecStages;
+    static constexpr int  kKSlots     = kQ8 ? ACEFA_Q8_KSLOTS : 1;  // converted K tiles (with their masks)
+    static_assert(kQ8 || kStageBytes % 1024 == 0, "TMA stages must stay 1 KB aligned");
     // warps 0-3 consume, warp 4 produces, warps 5-7 convert (Q8_0 only)
     static constexpr int  kConvWarps   = kQ8 ? 3 : 0;
     static constexpr int  kProdWarp    = kDecWarps;
     static constexpr int  kThreads     = (kDecWarps + 1 + kConvWarps) * 32;
     static constexpr int  kMergeStride = D + 8;  // floats per merge row (bank spread)
-    // shared memory carve-up (offsets from the 1024-B aligned base)
+    static constexpr int  kMergeBytes  = kDecRows * kMergeStride * 4;
+    // shared memory carve-up (offsets from the 1024-B aligned base).  Q8_0
+    // adds two converted K tiles (each with its tile's mask segments) and one
+    // converted V tile, and keeps the end-of-op merge rows in the raw stages,
+    // which are idle by then.
     static constexpr int kOffStages  = 0;
-    static constexpr int kOffCvtK    = kOffStages + kDecStages * kStageBytes;  // Q8_0: converted K tile
-    static constexpr int kOffCvtV    = kOffCvtK + (kQ8 ? kF16Tile : 0);        // Q8_0: converted V tile
-    static constexpr int kOffCvtM    = kOffCvtV + (kQ8 ? kF16Tile : 0);        // Q8_0: 2 mask segments
-    static constexpr int kOffMerge   = kOffCvtM + (kQ8 ? 2 * kMaskBytes : 0);
-    static constexpr int kOffStats   = kOffMerge + kDecRows * kMergeStride * 4;  // m,l per warp per row
+    static constexpr int kOffCvtK    = kQ8 ? (kStages * kStageBytes + 1023) / 1024 * 1024 : 0;  // [kKSlots]
+    static constexpr int kOffCvtV    = kOffCvtK + kKSlots * kF16Tile;
+    static constexpr int kOffCvtM    = kOffCvtV + kF16Tile;  // [kKSlots] mask segments
+    static constexpr int kOffMerge   = kQ8 ? 0 : kStages * kStageBytes;
+    static_assert(!kQ8 || kMergeBytes <= kStages * kStageBytes, "merge rows must fit the idle stages");
+    static constexpr int kOffStats   = kQ8 ? kOffCvtM + kKSlots * kMaskBytes : kOffMerge + kMergeBytes;
     static constexpr int kOffFin     = kOffStats + 2 * kDecWarps * kDecRows * 4;  // merged m,l per row
     static constexpr int kOffBars    = kOffFin + 2 * kDecRows * 4;
-    // full/empty per stage; K/V slot full/empty (Q8_0); cluster ready / done
-    static constexpr int kNumBars    = 2 * kDecStages + 4 + 2;
+    // full/empty per stage; converted K slots full/empty [2]; V slot
+    // full/empty; cluster ready / done
+    static constexpr int kNumBars    = 2 * kStages + 4 + 2 + 2;
     static constexpr int kOffMeta    = kOffBars + kNumBars * 8;
-    static constexpr int kOffCvtMeta = kOffMeta + kDecStages * 16;
+    static constexpr int kOffCvtMeta = kOffMeta + kStages * 16;
     static constexpr int kOffFlags   = kOffCvtMeta + 2 * 16;
     static constexpr int kSmemBytes  = kOffFlags + 16 + 1024;  // + alignment slack
     // Q8_0 register split (setmaxnreg): the consumer warpgroup grows, the
@@ -93,6 +114,7 @@ struct DecCfg {
     static constexpr uint32_t kRegsConvert  = 88;
     static_assert(!kQ8 || 128 * kRegsConsumer + 128 * kRegsConvert <= kThreads * kRegsLaunch,
                   "register split exceeds the launch pool");
+    static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
 };
 
 struct UnitCoord {
@@ -200,9 +222,10 @@ __device__ __forceinline__ void q8_tile_to_f16(uint32_t src, uint32_t dst, int n
     constexpr int RB    = D / 32 * 34;
     constexpr int RPI   = 32 / NB;    // rows per warp iteration
     constexpr int ITERS = kDecBN / RPI;
+    constexpr int kUnroll = ACEFA_Q8_CONV_UNROLL;
     const int     blk   = lane % NB;
     const int     rr    = lane / NB;
-#pragma unroll 1
+#pragma unroll kUnroll
     for (int it = cw; it < ITERS; it += NW) {
         const int      j   = it * RPI + rr;
         const uint32_t a0  = src + (uint32_t) (j * RB + 34 * blk);  // block start: scale, then 32 quants
@@ -374,13 +397,13 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     uint64_t     *full_bar  = reinterpret_cast<uint64_t *>(smem + Cfg::kOffBars);
-    uint64_t     *empty_bar = full_bar + kDecStages;
-    uint64_t     *kfull     = empty_bar + kDecStages;  // converted K tile ready (Q8_0)
-    uint64_t     *kempty    = kfull + 1;               // converted K tile consumed
-    uint64_t     *vfull     = kfull + 2;
-    uint64_t     *vempty    = kfull + 3;
-    uint64_t     *peer_rdy  = kfull + 4;  // every CTA of the cluster published its partial
-    uint64_t     *peer_done = kfull + 5;  // every CTA of the cluster finished reading this one's
+    uint64_t     *empty_bar = full_bar + Cfg::kStages;
+    uint64_t     *kfull     = empty_bar + Cfg::kStages;  // [2] converted K tile + mask ready (Q8_0)
+    uint64_t     *kempty    = kfull + 2;               // [2] converted K tile + mask consumed
+    uint64_t     *vfull     = kfull + 4;               // converted V tile ready
+    uint64_t     *vempty    = kfull + 5;               // converted V tile consumed
+    uint64_t     *peer_rdy  = kfull + 6;  // every CTA of the cluster published its partial
+    uint64_t     *peer_done = kfull + 7;  // every CTA of the cluster finished reading this one's
     int4         *meta      = reinterpret_cast<int4 *>(smem + Cfg::kOffMeta);
     int4         *cvt_meta  = reinterpret_cast<int4 *>(smem + Cfg::kOffCvtMeta);
     volatile int *abort_f   = reinterpret_cast<volatile int *>(smem + Cfg::kOffFlags);
@@ -394,12 +417,14 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     const int C    = P.cluster;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kDecStages; ++i) {
+        for (int i = 0; i < Cfg::kStages; ++i) {
             mbar_init(&full_bar[i], 1);
             mbar_init(&empty_bar[i], kQ8 ? Cfg::kConvWarps : kDecWarps);
         }
-        mbar_init(kfull, Cfg::kConvWarps > 0 ? Cfg::kConvWarps : 1);
-        mbar_init(kempty, kDecWarps);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&kfull[i], Cfg::kConvWarps > 0 ? Cfg::kConvWarps : 1);
+            mbar_init(&kempty[i], kDecWarps);
+        }
         mbar_init(vfull, Cfg::kConvWarps > 0 ? Cfg::kConvWarps : 1);
         mbar_init(vempty, kDecWarps);
         mbar_init(peer_rdy, C);
@@ -447,12 +472,12 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         int      stage = 0;
         uint32_t phase = 0;
         bool     ok    = true;
-        int      pend[kDecStages];  // parity of the last phase armed on each full barrier
-        for (int i = 0; i < kDecStages; ++i) {
+        int      pend[Cfg::kStages];  // parity of the last phase armed on each full barrier
+        for (int i = 0; i < Cfg::kStages; ++i) {
             pend[i] = -1;
         }
         auto advance = [&]() {
-            if (++stage == kDecStages) {
+            if (++stage == Cfg::kStages) {
                 stage = 0;
                 phase ^= 1u;
             }
@@ -612,7 +637,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         if (!ok) {
             // Aborting: let the last copy armed on each stage land before the CTA
             // exits (a phase can never run more than one ahead of its last arm).
-            for (int i = 0; i < kDecStages; ++i) {
+            for (int i = 0; i < Cfg::kStages; ++i) {
                 if (pend[i] < 0) {
                     continue;
                 }
@@ -631,16 +656,21 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     if constexpr (kQ8) {
         if (warp >= kDecWarps) {
             // ============================ converters ==========================
+            // Tile i: K (and the tile's mask segments) into K slot i % 2 once
+            // the consumers are done with tile i - 2 there, then V into the V
+            // slot once they are done with tile i - 1's V.
             const int cw    = warp - kDecWarps - 1;
             const int ct    = cw * 32 + lane;
             int       stage = 0;
             uint32_t  phase = 0;
             for (int it = 0;; ++it) {
+                const int      ks  = Cfg::kKSlots == 2 ? (it & 1) : 0;
+                const uint32_t kph = (uint32_t) (Cfg::kKSlots == 2 ? (it >> 1) & 1 : it & 1);
                 bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err,
                                                                     DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
                 if (ok) {
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(kempty, (uint32_t) (it & 1) ^ 1u, abort_f,
-                                                                   P.dev_err, DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&kempty[ks], kph ^ 1u, abort_f, P.dev_err,
+                                                                   DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
                 }
                 if (!ok) {
                     break;
@@ -649,19 +679,19 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                 const uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
                 if (md.z == kMetaData) {
                     q8_tile_to_f16<D, Cfg::kConvWarps>(smem_u32(sK) + (uint32_t) (md.w & 0xff),
-                                                        smem_u32(smem + Cfg::kOffCvtK), md.x, cw, lane);
-                    // the tile's mask segments travel with K (read before PV)
+                                                        smem_u32(smem + Cfg::kOffCvtK + ks * Cfg::kF16Tile), md.x, cw,
+                                                        lane);
                     for (int x = ct; x < n_ms * (kDecBN * 2 / 16); x += 32 * Cfg::kConvWarps) {
                         const uint4 v = *reinterpret_cast<const uint4 *>(sK + 2 * Cfg::kRawTile + 16 * x);
-                        *reinterpret_cast<uint4 *>(smem + Cfg::kOffCvtM + (it & 1) * Cfg::kMaskBytes + 16 * x) = v;
+                        *reinterpret_cast<uint4 *>(smem + Cfg::kOffCvtM + ks * Cfg::kMaskBytes + 16 * x) = v;
                     }
                 }
                 if (ct == 0) {
-                    cvt_meta[it & 1] = md;
+                    cvt_meta[ks] = md;
                 }
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(kfull);
+                    mbar_arrive(&kfull[ks]);
                 }
                 if (md.z != kMetaData) {
                     break;
@@ -678,7 +708,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     mbar_arrive(vfull);
                     mbar_arrive(&empty_bar[stage]);
                 }
-                if (++stage == kDecStages) {
+                if (++stage == Cfg::kStages) {
                     stage = 0;
                     phase ^= 1u;
                 }
@@ -930,24 +960,27 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
 
     if constexpr (kQ8) {
         for (int it = 0;; ++it) {
-            bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(kfull, (uint32_t) (it & 1), abort_f, P.dev_err,
+            const int      ks  = Cfg::kKSlots == 2 ? (it & 1) : 0;
+            const uint32_t kph = (uint32_t) (Cfg::kKSlots == 2 ? (it >> 1) & 1 : it & 1);
+            bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&kfull[ks], kph, abort_f, P.dev_err,
                                                                 DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
             if (!ok) {
                 break;
             }
-            const int4 md = cvt_meta[it & 1];
+            const int4 md = cvt_meta[ks];
             if (md.z != kMetaData) {
                 break;
             }
             float s[2][4];
-            tile_scores(smem + Cfg::kOffCvtK, s);
+            tile_scores(smem + Cfg::kOffCvtK + ks * Cfg::kF16Tile, s);
+            uint32_t pa[4], palo[4];
+            tile_softmax(s, reinterpret_cast<const uint16_t *>(smem + Cfg::kOffCvtM + ks * Cfg::kMaskBytes), md.y, pa,
+                         palo);
+            // the K slot and its mask segments are free once the softmax has read them
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(kempty);
+                mbar_arrive(&kempty[ks]);
             }
-            uint32_t pa[4], palo[4];
-            tile_softmax(s, reinterpret_cast<const uint16_t *>(smem + Cfg::kOffCvtM + (it & 1) * Cfg::kMaskBytes),
-                         md.y, pa, palo);
             ok = __all_sync(0xffffffffu, mbar_wait_bounded(vfull, (uint32_t) (it & 1), abort_f, P.dev_err,
                                                            DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
             if (!ok) {
@@ -983,7 +1016,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             if (lane == 0) {
                 mbar_arrive(&empty_bar[stage]);
             }
-            if (++stage == kDecStages) {
+            if (++stage == Cfg::kStages) {
                 stage = 0;
                 phase ^= 1u;
             }

@@ -393,12 +393,18 @@ def run_ours(args):
         sharded = sharded_dit(device, stream, world, rank)  # collective: every rank
         if rank == 0:
             out["extras"]["dit6000_heads_sharded"] = sharded
+    if not args.no_extras and not args.no_config5:
+        c5 = config5(device, stream, world, rank, gen=args.c5_gen)  # collective at N > 1: every rank
+        if rank == 0:
+            out["extras"]["config5"] = c5
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+            if "config5" in out.get("extras", {}):
+                out["extras"]["config5"]["cpu_baseline"] = config5_cpu_baseline()
         emit(out)
     return 0
 
@@ -826,6 +832,243 @@ def sharded_dit(device, stream, world, rank, iters=10, warmup=3):
                     "rank's buffer over NVLink (one-element all-reduce as completion barrier)"}
 
 
+# -------------------------------------------------------------------------
+# the end-to-end attention workload of one generation --
+# a random-init Qwen3-4B Q8_0 LM (36 layers, Hq 32 / Hkv 8, 8 requests x CFG =
+# 16 KV sets) with a 512-token prompt prefilled per set (qw3lm_forward,
+# src/qwen3-lm.h:480-621) and 2000 batched decode steps (qw3lm_forward_batch,
+# :629-894) whose window n_kv_pad = PAD(kv_len, 256) grows 768 -> 2560 with the
+# graph rebuilt at each new window (:496-500, src/pipeline-lm.cpp:427-527);
+# then 8 DiT steps x 24 layers of S = 6000 self-attention (128-key sliding
+# window on even layers, src/dit.h:400) and cross-attention to 512 text tokens
+# (461 valid), B = 2 (CFG), 16 x 128 heads (src/dit-sampler.h:415).  Masks are
+# f16 tensors filled the way the reference fills them.  At N GPUs the 16 KV
+# sets split N ways (no collective) and the DiT heads split N ways with one
+# NCCL all-gather per node (strong scaling: the total work is fixed).
+C5_LAYERS, C5_SETS, C5_PROMPT, C5_GEN, C5_MAXSEQ = 36, 16, 512, 2000, 2560
+C5_DIT_STEPS, C5_DIT_LAYERS, C5_DIT_S, C5_DIT_ENC, C5_DIT_VALID, C5_DIT_WIN = 8, 24, 6000, 512, 461, 128
+Q8_ROW = D // 32 * 34
+
+
+def pad256(n):
+    return (n + 255) // 256 * 256
+
+
+def c5_decode_bytes(sets, kv_len, n_kv_pad):
+    """Algorithmic HBM bytes of one batched decode op: the valid K/V rows of
+    every (set, kv head) once, Q and O (f32), the mask rows."""
+    return sets * HKV * kv_len * Q8_ROW * 2 + sets * HQ * D * 4 * 2 + sets * n_kv_pad * 2
+
+
+def c5_prefill_flops(S=C5_PROMPT):
+    return 4 * D * HQ * S * (S + 1) // 2  # one set, one layer, unmasked (q, k) pairs
+
+
+def c5_dit_flops(heads=16, B=2):
+    full = 4 * D * heads * B * C5_DIT_S * C5_DIT_S
+    win = 4 * D * heads * B * dense_pairs(C5_DIT_S, C5_DIT_S, "window", C5_DIT_WIN)
+    cross = 4 * D * heads * B * C5_DIT_S * C5_DIT_VALID
+    return full, win, cross
+
+
+def config5(device, stream, world=1, rank=0, gen=C5_GEN):
+    """Runs the whole config-5 workload once untimed (warm-up, graph capture)
+    and once timed; device time per part, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import acefa
+    from acefa.dist import ShardedOp, head_shard
+
+    sets = C5_SETS // world
+    g = torch.Generator(device=device).manual_seed(SEED + 5000 + 7919 * rank)
+    # ---- LM: one Q8_0 KV cache per layer, (sets, Hkv, max_seq, 136 B rows)
+    caches = []
+    for _ in range(C5_LAYERS):
+        kf = torch.randn(sets, HKV, C5_MAXSEQ, D, device=device, generator=g, dtype=torch.float16)
+        vf = torch.randn(sets, HKV, C5_MAXSEQ, D, device=device, generator=g, dtype=torch.float16)
+        caches.append((acefa.quantize_q8_0(kf), acefa.quantize_q8_0(vf)))
+        del kf, vf
+    # prompt prefill: one op per (layer, set), Q [128, 512, 32] f32, causal mask
+    qp = torch.randn(1, HQ, C5_PROMPT, D, device=device, generator=g)
+    mp = torch.where(torch.arange(C5_PROMPT, device=device)[None, :] <= torch.arange(C5_PROMPT, device=device)[:, None],
+                     0.0, float("-inf")).half().reshape(1, 1, C5_PROMPT, C5_PROMPT).contiguous()
+    outp = torch.empty(1, C5_PROMPT, HQ, D, device=device)
+    pre_ops = [acefa.Op(qp, k[s:s + 1, :, :C5_PROMPT], v[s:s + 1, :, :C5_PROMPT], mask=mp, out=outp,
+                        kv_type=acefa.GGML_Q8_0, scale=D ** -0.5)
+               for (k, v) in caches for s in range(sets)]
+    pre_path = None
+    # decode: per window, one CUDA graph of all its steps (36 ops each); step
+    # i's ops read mask slice i of the window's table (0 up to kv_len, -inf after)
+    qd = [torch.randn(sets, HQ, 1, D, device=device, generator=g) for _ in range(C5_LAYERS)]
+    outd = [torch.empty(sets, 1, HQ, D, device=device) for _ in range(C5_LAYERS)]
+    windows = {}
+    for t in range(gen):
+        kv_len = C5_PROMPT + t + 1
+        windows.setdefault(min(pad256(kv_len), C5_MAXSEQ), []).append(kv_len)
+    dec_bytes = sum(c5_decode_bytes(sets, kl, w) for w, kls in windows.items() for kl in kls) * C5_LAYERS
+    graphs, keep = [], []
+    with torch.cuda.stream(stream):
+        for w, kls in sorted(windows.items()):
+            lens = torch.tensor(kls, device=device)
+            tab = torch.where(torch.arange(w, device=device)[None, :] < lens[:, None], 0.0, float("-inf")).half()
+            tab = tab[:, None, None, None, :].expand(len(kls), sets, 1, 1, w).contiguous()
+            ops = [acefa.Op(qd[l], caches[l][0][:, :, :w], caches[l][1][:, :, :w], mask=tab[0], out=outd[l],
+                            kv_type=acefa.GGML_Q8_0, scale=D ** -0.5) for l in range(C5_LAYERS)]
+            for op in ops:  # warm-up outside capture (first-call set-up per kernel instance)
+                op(stream=stream)
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for i in range(len(kls)):
+                    ptr = tab[i].data_ptr()
+                    for op in ops:
+                        op.tm.data = ptr
+                        op(stream=stream)
+            graphs.append(gr)
+            keep.append((tab, ops))
+        for op in pre_ops[:2]:
+            op(stream=stream)
+        pre_path = acefa.last_path()
+        pre_graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(pre_graph, stream=stream):
+            for op in pre_ops:
+                op(stream=stream)
+    # ---- DiT: 24 layers of self (window on even layers) + cross attention
+    sh = head_shard(16, 16, world, rank)
+    hs = sh.hq1 - sh.hq0
+    B, S = 2, C5_DIT_S
+    qx = torch.randn(B, hs, S, D, device=device, generator=g)
+    qi = torch.arange(S, device=device)
+    mwin = torch.where((qi[:, None] - qi[None, :]).abs() <= C5_DIT_WIN, 0.0, float("-inf")).half()
+    mwin = mwin.reshape(1, 1, S, S).contiguous()
+    mpad = torch.where(torch.arange(C5_DIT_ENC, device=device) < C5_DIT_VALID, 0.0, float("-inf")).half()
+    mpad = mpad.reshape(1, 1, 1, C5_DIT_ENC).expand(B, 1, S, C5_DIT_ENC).contiguous()
+    dit_ops = []
+    out1 = torch.empty(B, S, hs, D, device=device) if world == 1 else None
+    for l in range(C5_DIT_LAYERS):
+        ks = torch.randn(B, hs, S, D, device=device, generator=g, dtype=torch.float16)
+        vs = torch.randn(B, hs, S, D, device=device, generator=g, dtype=torch.float16)
+        kc = torch.randn(B, hs, C5_DIT_ENC, D, device=device, generator=g, dtype=torch.float16)
+        vc = torch.randn(B, hs, C5_DIT_ENC, D, device=device, generator=g, dtype=torch.float16)
+        for kk, vv, mm in ((ks, vs, mwin if l % 2 == 0 else None), (kc, vc, mpad)):
+            if world == 1:  # the full output directly, no gather
+                dit_ops.append(acefa.Op(qx, kk, vv, mask=mm, out=out1, scale=D ** -0.5))
+            else:
+                dit_ops.append(ShardedOp(qx, kk, vv, mm, world, scale=D ** -0.5))
+
+    def run_dit(steps):
+        for _ in range(steps):
+            for op in dit_ops:
+                op(stream)
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    with torch.cuda.stream(stream):
+        pre_graph.replay()
+        for gr in graphs:
+            gr.replay()
+        run_dit(1)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev[0].record(stream)
+        pre_graph.replay()
+        ev[1].record(stream)
+        for gr in graphs:
+            gr.replay()
+        ev[2].record(stream)
+        run_dit(C5_DIT_STEPS)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])],
+                     device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    assert acefa.device_error(stream) == 0
+    ms_pre, ms_dec, ms_dit = (float(x) for x in t)
+    hbm, _ = read_peaks()
+    tf_peak = read_tflops_peak()
+    pre_fl = c5_prefill_flops() * C5_LAYERS * C5_SETS
+    full, win, cross = c5_dit_flops()
+    dit_fl = C5_DIT_STEPS * (C5_DIT_LAYERS // 2) * (full + win) + C5_DIT_STEPS * C5_DIT_LAYERS * cross
+    dec_total = dec_bytes * world
+    del graphs, pre_graph, keep, pre_ops, dit_ops, caches
+    torch.cuda.empty_cache()
+    return {
+        "gpus": world, "wall_ms": round(ms_pre + ms_dec + ms_dit, 2),
+        "prefill": {"ms": round(ms_pre, 3), "ops": C5_LAYERS * C5_SETS, "gflop": round(pre_fl / 1e9, 1),
+                    "tflops": round(pre_fl / (ms_pre / 1e3) / 1e12, 1),
+                    "frac_of_bf16_peak": round(pre_fl / (ms_pre / 1e3) / 1e12 / tf_peak, 4),
+                    "path": "dense tcgen05" if pre_path == 2 else "split-KV decode kernel"},
+        "decode": {"ms": round(ms_dec, 2), "steps": gen, "ops": gen * C5_LAYERS,
+                   "windows": sorted(windows), "gb": round(dec_total / 1e9, 2),
+                   "gbs": round(dec_total / (ms_dec / 1e3) / 1e9, 1),
+                   "frac_of_hbm_peak": round(dec_total / (ms_dec / 1e3) / 1e9 / hbm, 4),
+                   "us_per_op": round(ms_dec * 1e3 / (gen * C5_LAYERS), 2)},
+        "dit": {"ms": round(ms_dit, 2), "steps": C5_DIT_STEPS, "layers": C5_DIT_LAYERS,
+                "tflop": round(dit_fl / 1e12, 2), "tflops": round(dit_fl / (ms_dit / 1e3) / 1e12, 1),
+                "frac_of_bf16_peak": round(dit_fl / (ms_dit / 1e3) / 1e12 / tf_peak, 4),
+                "assembly": "NCCL all_gather_into_tensor + permute" if world > 1 else "single GPU"},
+        "note": "device time per part (CUDA events, max over ranks); decode bytes count valid K/V rows; "
+                "f16 masks filled like the reference's; LM KV sets and DiT heads split over the GPUs",
+    }
+
+
+def read_tflops_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"])
+    return 1590.0
+
+
+def config5_cpu_baseline(budget_s=6.0, threads=None):
+    """The reference operator's CPU arithmetic (oracle, ggml-cpu mode) on bounded
+    samples of config 5: one batched Q8_0 decode op at a mid window and a slice of
+    DiT query rows; the whole workload's CPU time is estimated from their rates."""
+    import numpy as np
+
+    import oracle
+
+    threads = threads or os.cpu_count()
+    rng = np.random.default_rng(SEED + 5)
+    kv_len, w = 1536, 1536
+    q = rng.standard_normal((C5_SETS, HQ, 1, D), dtype=np.float32)
+    kq = oracle.quantize_q8_0(rng.standard_normal((C5_SETS, HKV, w, D), dtype=np.float32))
+    vq = oracle.quantize_q8_0(rng.standard_normal((C5_SETS, HKV, w, D), dtype=np.float32))
+    m = np.zeros((C5_SETS, 1, 1, w), np.float16)
+    args = dict(scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, k_type=oracle.GGML_Q8_0, v_type=oracle.GGML_Q8_0,
+                d=D, dv=D, nthreads=threads)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s / 2 or n == 0:
+        oracle.flash_attn_ext(q, kq, vq, m, **args)
+        n += 1
+    dec_gbs = n * c5_decode_bytes(C5_SETS, kv_len, w) / (time.perf_counter() - t0) / 1e9
+    rows = 64
+    qd = rng.standard_normal((2, 16, rows, D), dtype=np.float32)
+    kd = rng.standard_normal((2, 16, C5_DIT_S, D), dtype=np.float32).astype(np.float16)
+    vd = rng.standard_normal((2, 16, C5_DIT_S, D), dtype=np.float32).astype(np.float16)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s / 2 or n == 0:
+        oracle.flash_attn_ext(qd, kd, vd, None, scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=threads)
+        n += 1
+    dit_tflops = n * 4 * D * 16 * 2 * rows * C5_DIT_S / (time.perf_counter() - t0) / 1e12
+    windows = {}
+    for t in range(C5_GEN):
+        kl = C5_PROMPT + t + 1
+        windows.setdefault(pad256(kl), []).append(kl)
+    dec_bytes = sum(c5_decode_bytes(C5_SETS, kl, w) for w, kls in windows.items() for kl in kls) * C5_LAYERS
+    full, win, cross = c5_dit_flops()
+    dit_fl = C5_DIT_STEPS * (C5_DIT_LAYERS // 2) * (full + win) + C5_DIT_STEPS * C5_DIT_LAYERS * cross
+    pre_fl = c5_prefill_flops() * C5_LAYERS * C5_SETS
+    est_s = dec_bytes / (dec_gbs * 1e9) + (dit_fl + pre_fl) / (dit_tflops * 1e12)
+    return {"decode_gbs": round(dec_gbs, 2), "dense_tflops": round(dit_tflops, 4), "cores": threads,
+            "kind": "port", "estimated_wall_s": round(est_s, 1),
+            "sample": f"one 16-set Q8_0 decode op at window {w} and {rows} query rows x 16 heads x B=2 of "
+                      f"DiT self-attention over {C5_DIT_S} keys, oracle/fa_oracle.c ggml-cpu arithmetic, "
+                      f"OpenMP; the workload's CPU time is estimated from these two rates"}
+
+
 def run_dense_workload(args):
     """--workload <dense name>: time one dense op (also the ncu profiling case);
     --workload dit6000_prologue: the DiT layer with its QK-norm + RoPE prologue."""
@@ -836,6 +1079,9 @@ def run_dense_workload(args):
     stream = torch.cuda.Stream(device=device)
     if args.workload == "dit6000_prologue":
         emit({"workload": args.workload, **dit_prologue(device, stream, iters=args.steps)})
+        return 0
+    if args.workload == "config5":
+        emit({"workload": args.workload, **config5(device, stream, gen=args.c5_gen)})
         return 0
     r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup, rule=args.mask_rule)
     emit({"workload": args.workload, "mask_rule": bool(args.mask_rule), **r})
@@ -876,7 +1122,9 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (36 = the headline stack)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
     ap.add_argument("--workload", default="decode4b",
-                    help="decode4b (headline), dit6000_prologue, or one dense op: " + ", ".join(DENSE_WORKLOADS))
+                    help="decode4b (headline), config5, dit6000_prologue, or one dense op: " + ", ".join(DENSE_WORKLOADS))
+    ap.add_argument("--no-config5", action="store_true", help="skip the config-5 end-to-end workload extra")
+    ap.add_argument("--c5-gen", type=int, default=C5_GEN, help="config-5 decode steps (2000 = the BASELINE workload)")
     ap.add_argument("--mask-rule", action="store_true",
                     help="dense workload: give the mask by rule (acefa_flash_attn_ext_gen) instead of a tensor")
     args = ap.parse_args()
