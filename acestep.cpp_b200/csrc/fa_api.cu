@@ -238,7 +238,7 @@ void set_scalars(OpDesc &o, float scale, float max_bias, float softcap) {
 // ------------------------------------------------------------------ decode plan
 // A unit (batch, kv head, 16-row block) runs on a cluster of C CTAs that split
 // its keys and merge through distributed shared memory.  C is the largest
-// power of two (<= the unit's key tiles) for which the device keeps every
+// size (<= 16, <= the unit's key tiles) for which the device keeps every
 // unit's cluster resident at once, so the op runs in one wave; units beyond
 // that run one CTA each.  A function of shapes and the device only.
 struct DecodePlan {
@@ -248,7 +248,8 @@ struct DecodePlan {
 DecodePlan plan_decode(const OpDesc &o, bool prologue) {
     DecodePlan p;
     const int rows = o.G * o.n_q;
-    p.n_rb         = (rows + kDecRows - 1) / kDecRows;
+    const int R    = decode_unit_rows(o.kv_type);
+    p.n_rb         = (rows + R - 1) / R;
     p.units        = o.B * o.Hkv * p.n_rb;
     p.tpu          = (o.n_kv + kDecBN - 1) / kDecBN;
     p.cluster      = decode_cluster(o.kv_type, o.D, prologue, p.units, p.tpu);

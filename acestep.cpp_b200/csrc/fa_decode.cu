@@ -22,12 +22,15 @@
 //     TMA tensor tiles with 128-B swizzle for F16/BF16, 1-D bulk copies of
 //     whole 34-B-block rows for Q8_0 -- and skips tiles whose mask is entirely
 //     -inf (the padded decode window tail).
-//   * Q8_0: three converter warps dequantise each staged tile once, K and V
-//     separately, into F16 tiles with the same swizzled layout TMA writes
-//     (value = f16(d * q), one rounding), so the consumers run the F16 code.
-//   * Four consumer warps each take 16 keys of every tile: S = Q K^T and
-//     O += P V on mma.sync m16n8k16 with F32 accumulation, online softmax in
-//     the log2 domain with quad shuffles.
+//   * Four consumer warps each take 16 keys of every tile, on mma.sync
+//     m16n8k16 with F32 accumulation and an online softmax in the log2 domain.
+//     F16/BF16: S = Q K^T and O += P V over 16-row units, K and V by ldmatrix
+//     from the swizzled tiles.  Q8_0: transposed, S^T = K Q^T and
+//     O^T += V^T P^T over 8-row units (the keys fill the MMA's M dimension, so
+//     a 4-head GQA group wastes half an n8 tile instead of three quarters of an
+//     m16 tile); head dims are assigned so that each thread's K and V bytes
+//     are contiguous runs of Q8_0 blocks, dequantised once in registers as
+//     f16(d * q).
 //   * Every wait is bounded; on expiry the CTA records an error word, drains
 //     its in-flight copies (bounded) and exits.
 #include <cfloat>
@@ -40,19 +43,14 @@
 // Largest cluster the host plan may pick (a tuning macro; the device may
 // allow less).
 #ifndef ACEFA_DEC_MAX_CLUSTER
-#define ACEFA_DEC_MAX_CLUSTER 16
+#define ACEFA_DEC_MAX_CLUSTER 8
 #endif
-// Q8_0 pipeline shape (tuning macros): raw stages in flight, and converted-K
-// slots (2 lets K of the next tile be converted while the current one is
-// scored; 1 leaves the shared memory to a fourth raw stage).
+// Q8_0 stages in flight and CTAs per SM (tuning macros).
 #ifndef ACEFA_Q8_STAGES
 #define ACEFA_Q8_STAGES 4
 #endif
-#ifndef ACEFA_Q8_KSLOTS
-#define ACEFA_Q8_KSLOTS 1
-#endif
-#ifndef ACEFA_Q8_CONV_UNROLL
-#define ACEFA_Q8_CONV_UNROLL 1
+#ifndef ACEFA_Q8_CTAS
+#define ACEFA_Q8_CTAS 2
 #endif
 
 namespace acefa {
@@ -63,64 +61,45 @@ constexpr int kMetaData = 1;
 constexpr int kMetaTerm = 3;
 
 constexpr uint16_t kHalfNegInf = 0xFC00u;
+constexpr float    kQ8RescaleLog2 = 8.0f;  // Q8_0 consumer: rescale when the max grows by > 2^8
 
 template <int KV_TYPE, int D>
 struct DecCfg {
     static constexpr bool kQ8         = KV_TYPE == ACEFA_TYPE_Q8_0;
     static constexpr bool kBF16       = KV_TYPE == ACEFA_TYPE_BF16;
     static constexpr int  kRowBytes   = kQ8 ? D / 32 * 34 : D * 2;  // one cache row
-    // a 64-key tile of 16-bit values: D/64 swizzled boxes of 64 keys x 128 B
-    static constexpr int  kF16Tile    = kDecBN * D * 2;
-    // staged raw tile: F16/BF16 = the TMA boxes (1 KB aligned for the 128-B
-    // swizzle); Q8_0 = whole block rows plus up to 15 lead bytes (bulk copies
-    // only need 16-B alignment)
-    static constexpr int  kRawTile    = kQ8 ? (kDecBN * kRowBytes + 16 + 15) / 16 * 16 : kF16Tile;
+    // rows per unit: the m16 tile of the F16/BF16 consumer, the n8 tile of the
+    // transposed Q8_0 consumer
+    static constexpr int  kRows       = decode_unit_rows(KV_TYPE);
+    // staged tile: F16/BF16 = the TMA boxes (D/64 swizzled boxes of 64 keys x
+    // 128 B, 1 KB aligned); Q8_0 = whole block rows plus up to 15 lead bytes
+    // (bulk copies only need 16-B alignment)
+    static constexpr int  kTile       = kQ8 ? (kDecBN * kRowBytes + 16 + 15) / 16 * 16 : kDecBN * D * 2;
     static constexpr int  kMaskBytes  = kDecRows * kDecBN * 2;  // up to 16 mask rows x 64 keys (f16)
-    static constexpr int  kStageBytes = 2 * kRawTile + kMaskBytes;
+    static constexpr int  kStageBytes = 2 * kTile + kMaskBytes;
     static constexpr int  kStages     = kQ8 ? ACEFA_Q8_STAGES : kDecStages;
-    static constexpr int  kKSlots     = kQ8 ? ACEFA_Q8_KSLOTS : 1;  // converted K tiles (with their masks)
     static_assert(kQ8 || kStageBytes % 1024 == 0, "TMA stages must stay 1 KB aligned");
-    // warps 0-3 consume, warp 4 produces, warps 5-7 convert (Q8_0 only)
-    static constexpr int  kConvWarps   = kQ8 ? 3 : 0;
-    static constexpr int  kProdWarp    = kDecWarps;
-    static constexpr int  kThreads     = (kDecWarps + 1 + kConvWarps) * 32;
-    static constexpr int  kMergeStride = D + 8;  // floats per merge row (bank spread)
-    static constexpr int  kMergeBytes  = kDecRows * kMergeStride * 4;
-    // shared memory carve-up (offsets from the 1024-B aligned base).  Q8_0
-    // adds two converted K tiles (each with its tile's mask segments) and one
-    // converted V tile, and keeps the end-of-op merge rows in the raw stages,
-    // which are idle by then.
-    static constexpr int kOffStages  = 0;
-    static constexpr int kOffCvtK    = kQ8 ? (kStages * kStageBytes + 1023) / 1024 * 1024 : 0;  // [kKSlots]
-    static constexpr int kOffCvtV    = kOffCvtK + kKSlots * kF16Tile;
-    static constexpr int kOffCvtM    = kOffCvtV + kF16Tile;  // [kKSlots] mask segments
-    static constexpr int kOffMerge   = kQ8 ? 0 : kStages * kStageBytes;
-    static_assert(!kQ8 || kMergeBytes <= kStages * kStageBytes, "merge rows must fit the idle stages");
-    static constexpr int kOffStats   = kQ8 ? kOffCvtM + kKSlots * kMaskBytes : kOffMerge + kMergeBytes;
-    static constexpr int kOffFin     = kOffStats + 2 * kDecWarps * kDecRows * 4;  // merged m,l per row
-    static constexpr int kOffBars    = kOffFin + 2 * kDecRows * 4;
-    // full/empty per stage; converted K slots full/empty [2]; V slot
-    // full/empty; cluster ready / done
-    static constexpr int kNumBars    = 2 * kStages + 4 + 2 + 2;
-    static constexpr int kOffMeta    = kOffBars + kNumBars * 8;
-    static constexpr int kOffCvtMeta = kOffMeta + kStages * 16;
-    static constexpr int kOffFlags   = kOffCvtMeta + 2 * 16;
-    static constexpr int kSmemBytes  = kOffFlags + 16 + 1024;  // + alignment slack
-    // Q8_0 register split (setmaxnreg): the consumer warpgroup grows, the
-    // producer + converter warpgroup shrinks.  Launched as 256 threads x 128
-    // registers (2 CTAs per SM); the split must stay within that pool.
-    static constexpr uint32_t kRegsLaunch   = 128;
-    static constexpr uint32_t kRegsConsumer = 168;
-    static constexpr uint32_t kRegsConvert  = 88;
-    static_assert(!kQ8 || 128 * kRegsConsumer + 128 * kRegsConvert <= kThreads * kRegsLaunch,
-                  "register split exceeds the launch pool");
-    static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
+    static constexpr int  kThreads     = (kDecWarps + 1) * 32;  // 4 consumer warps + the producer
+    static constexpr int  kMergeStride = D + 8;                   // floats per merge row (bank spread)
+    // shared memory carve-up (offsets from the 1024-B aligned base)
+    static constexpr int kOffStages = 0;
+    static constexpr int kOffMerge  = kStages * kStageBytes;
+    static constexpr int kOffStats  = kOffMerge + kDecRows * kMergeStride * 4;  // m,l per warp per row
+    static constexpr int kOffFin    = kOffStats + 2 * kDecWarps * kDecRows * 4;  // merged m,l per row
+    static constexpr int kOffBars   = kOffFin + 2 * kDecRows * 4;
+    static constexpr int kNumBars   = 2 * kStages + 2;  // full/empty per stage; cluster ready / done
+    static constexpr int kOffMeta   = kOffBars + kNumBars * 8;
+    static constexpr int kOffFlags  = kOffMeta + kStages * 16;
+    static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
+    static constexpr int kCtasPerSm = kQ8 ? ACEFA_Q8_CTAS : 2;
+    static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024, "CTAs per SM exceed shared memory");
 };
 
 struct UnitCoord {
     int b, hk, rb, bk, rows;
 };
 
+template <int R>
 __device__ __forceinline__ UnitCoord unit_coord(const DecodeParams &P, int u) {
     UnitCoord c;
     c.rb            = u % P.n_rb;
@@ -128,13 +107,14 @@ __device__ __forceinline__ UnitCoord unit_coord(const DecodeParams &P, int u) {
     c.b             = u / (P.n_rb * P.op.Hkv);
     c.bk            = c.b / P.op.rk3;
     const int total = P.op.G * P.op.n_q;
-    c.rows          = min(kDecRows, total - c.rb * kDecRows);
+    c.rows          = min(R, total - c.rb * R);
     return c;
 }
 
 // Row rr of unit -> (query index iq, q head hq).
+template <int R>
 __device__ __forceinline__ void row_coord(const DecodeParams &P, const UnitCoord &uc, int rr, int &iq, int &hq) {
-    const int gr = uc.rb * kDecRows + rr;
+    const int gr = uc.rb * R + rr;
     iq           = gr / P.op.G;
     hq           = uc.hk * P.op.G + gr % P.op.G;
 }
@@ -146,14 +126,15 @@ __device__ __forceinline__ const uint16_t *mask_row(const OpDesc &o, int iq, int
 
 // True if some mask entry of this tile, for some row of the unit, is not -inf
 // (under a mask rule: some key of the tile is in some row's visible range).
+template <int R>
 __device__ bool tile_live(const DecodeParams &P, const UnitCoord &uc, int tile) {
     const OpDesc &o   = P.op;
     const int     j0  = tile * kDecBN;
     const int     cnt = min(kDecBN, o.n_kv - j0);
     if (o.mg_kind) {
         int lo0, hi0, lo1, hi1;
-        mg_range(o, uc.b, (uc.rb * kDecRows) / o.G, lo0, hi0);
-        mg_range(o, uc.b, (uc.rb * kDecRows + uc.rows - 1) / o.G, lo1, hi1);
+        mg_range(o, uc.b, (uc.rb * R) / o.G, lo0, hi0);
+        mg_range(o, uc.b, (uc.rb * R + uc.rows - 1) / o.G, lo1, hi1);
         return max(lo0, j0) < min(hi1, j0 + cnt);
     }
     if (o.mask == nullptr) {
@@ -162,7 +143,7 @@ __device__ bool tile_live(const DecodeParams &P, const UnitCoord &uc, int tile) 
     const uint16_t *prev = nullptr;
     for (int rr = 0; rr < uc.rows; ++rr) {
         int iq, hq;
-        row_coord(P, uc, rr, iq, hq);
+        row_coord<R>(P, uc, rr, iq, hq);
         const uint16_t *m = mask_row(o, iq, hq, uc.b);
         if (m == prev) {
             continue;
@@ -197,63 +178,42 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
     asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
     return v;
 }
-
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+__device__ __forceinline__ uint16_t lds16(uint32_t addr) {
+    uint16_t v;
+    asm volatile("ld.shared.b16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
 }
 
-// Two int8 values, biased to unsigned (b ^ 0x80) and placed in the low bytes
-// of an f16 pair with exponent 0x64, are the f16 values 1152 + b: subtracting
-// 1152 recovers b exactly; the multiply by the block scale rounds once.
+// NW words of int8 quants of one Q8_0 block starting `sub` bytes into its 32
+// values (blk = the block's shared address: f16 scale, then the quants; any
+// 2-B alignment), each byte biased to unsigned (b ^ 0x80).  Returns the scale.
+template <int NW>
+__device__ __forceinline__ uint16_t q8_load_run(uint32_t blk, int sub, uint32_t (&q)[NW]) {
+    const uint32_t a  = blk + 2u + (uint32_t) sub;
+    const uint32_t aw = a & ~3u;
+    const uint32_t sh = (a & 3u) * 8u;  // 0 or 16
+    uint32_t       w[NW + 1];
+#pragma unroll
+    for (int k = 0; k <= NW; ++k) {
+        w[k] = lds32(aw + 4u * k);
+    }
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        q[k] = __funnelshift_r(w[k], w[k + 1], sh) ^ 0x80808080u;
+    }
+    return lds16(blk);
+}
+
+// Two biased int8 values placed in the low bytes of an f16 pair with exponent
+// 0x64 are the f16 values 1152 + b: subtracting 1152 recovers b exactly, and
+// the multiply by the block scale rounds once (f16(d * q), as ggml's
+// dequantisation to F16).  sel picks the two bytes (0x4140: bytes 0,1;
+// 0x4342: bytes 2,3).
 __device__ __forceinline__ uint32_t i8x2_scaled(uint32_t biased_word, uint32_t sel, __half2 d2) {
     const uint32_t t = __byte_perm(biased_word, 0x64646464u, sel);
     const __half2  v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&t), __half2half2(__ushort_as_half(0x6480u))),
                                d2);
     return *reinterpret_cast<const uint32_t *>(&v);
-}
-
-// Q8_0 tile -> F16 tile.  The staged rows (kRowBytes each, any 2-B alignment)
-// become the 128-B swizzled layout a TMA box {64 dims, 64 keys} writes.  A
-// warp iteration converts 32/NB rows: lane = (row, 32-value block).  Rows at
-// or past `nvalid` (a ragged last tile) become zeros.
-template <int D, int NW>
-__device__ __forceinline__ void q8_tile_to_f16(uint32_t src, uint32_t dst, int nvalid, int cw, int lane) {
-    constexpr int NB    = D / 32;     // blocks per row
-    constexpr int RB    = D / 32 * 34;
-    constexpr int RPI   = 32 / NB;    // rows per warp iteration
-    constexpr int ITERS = kDecBN / RPI;
-    constexpr int kUnroll = ACEFA_Q8_CONV_UNROLL;
-    const int     blk   = lane % NB;
-    const int     rr    = lane / NB;
-#pragma unroll kUnroll
-    for (int it = cw; it < ITERS; it += NW) {
-        const int      j   = it * RPI + rr;
-        const uint32_t a0  = src + (uint32_t) (j * RB + 34 * blk);  // block start: scale, then 32 quants
-        const uint32_t aw  = a0 & ~3u;
-        const uint32_t sh  = (a0 & 3u) * 8u;  // 0 or 16
-        uint32_t       w[9];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) {
-            w[k] = lds32(aw + 4 * k);
-        }
-        const unsigned short dbits = (unsigned short) ((w[0] >> sh) & 0xFFFFu);
-        const __half2        d2    = __half2half2(j < nvalid ? __ushort_as_half(dbits) : __ushort_as_half(0));
-        uint32_t             o[16];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            // quant word k: bytes 2 + 4k .. 5 + 4k of the block
-            const uint32_t q = __funnelshift_rc(w[k], w[k + 1], 16u + sh) ^ 0x80808080u;
-            o[2 * k]         = i8x2_scaled(q, 0x4140u, d2);
-            o[2 * k + 1]     = i8x2_scaled(q, 0x4342u, d2);
-        }
-        // dims 32*blk .. +31 = 16-B chunks cc = 4*blk .. 4*blk + 3
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            const int      cc   = 4 * blk + m;
-            const uint32_t addr = dst + (uint32_t) ((cc >> 3) * (kDecBN * 128) + j * 128 + (((cc & 7) ^ (j & 7)) << 4));
-            sts128(addr, o[4 * m], o[4 * m + 1], o[4 * m + 2], o[4 * m + 3]);
-        }
-    }
 }
 
 }  // namespace
@@ -384,28 +344,24 @@ __device__ __forceinline__ void append_store(const DecodeParams &P, int64_t pr, 
 // PRO: the instance that applies the QK-norm + RoPE prologues (Q rows, the
 // appended K row); the others carry none of that code.
 template <int KV_TYPE, int D, bool PRO>
-__global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
+__global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, D>::kCtasPerSm)
     fa_decode_kernel(const __grid_constant__ DecodeParams P, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
     using Cfg            = DecCfg<KV_TYPE, D>;
     constexpr bool kQ8   = Cfg::kQ8;
-    constexpr bool kBF16 = Cfg::kBF16;  // operand type of the MMAs (Q8_0 tiles become F16)
+    constexpr bool kBF16 = Cfg::kBF16;
     constexpr int  KS    = D / 16;      // k-steps over the head dim
     constexpr int  NT    = D / 8;       // n8 tiles over the head dim
+    constexpr int  R     = Cfg::kRows;  // rows per unit
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     uint64_t     *full_bar  = reinterpret_cast<uint64_t *>(smem + Cfg::kOffBars);
     uint64_t     *empty_bar = full_bar + Cfg::kStages;
-    uint64_t     *kfull     = empty_bar + Cfg::kStages;  // [2] converted K tile + mask ready (Q8_0)
-    uint64_t     *kempty    = kfull + 2;               // [2] converted K tile + mask consumed
-    uint64_t     *vfull     = kfull + 4;               // converted V tile ready
-    uint64_t     *vempty    = kfull + 5;               // converted V tile consumed
-    uint64_t     *peer_rdy  = kfull + 6;  // every CTA of the cluster published its partial
-    uint64_t     *peer_done = kfull + 7;  // every CTA of the cluster finished reading this one's
+    uint64_t     *peer_rdy  = empty_bar + Cfg::kStages;  // every CTA of the cluster published its partial
+    uint64_t     *peer_done = peer_rdy + 1;              // every CTA of the cluster finished reading this one's
     int4         *meta      = reinterpret_cast<int4 *>(smem + Cfg::kOffMeta);
-    int4         *cvt_meta  = reinterpret_cast<int4 *>(smem + Cfg::kOffCvtMeta);
     volatile int *abort_f   = reinterpret_cast<volatile int *>(smem + Cfg::kOffFlags);
     float        *merge     = reinterpret_cast<float *>(smem + Cfg::kOffMerge);
     float        *s_m       = reinterpret_cast<float *>(smem + Cfg::kOffStats);
@@ -419,14 +375,8 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     if (threadIdx.x == 0) {
         for (int i = 0; i < Cfg::kStages; ++i) {
             mbar_init(&full_bar[i], 1);
-            mbar_init(&empty_bar[i], kQ8 ? Cfg::kConvWarps : kDecWarps);
+            mbar_init(&empty_bar[i], kDecWarps);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&kfull[i], Cfg::kConvWarps > 0 ? Cfg::kConvWarps : 1);
-            mbar_init(&kempty[i], kDecWarps);
-        }
-        mbar_init(vfull, Cfg::kConvWarps > 0 ? Cfg::kConvWarps : 1);
-        mbar_init(vempty, kDecWarps);
         mbar_init(peer_rdy, C);
         mbar_init(peer_done, C);
         *abort_f = 0;
@@ -448,22 +398,16 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     const int       tpu = P.tiles_per_unit;
     const int       tlo = (int) ((int64_t) tpu * r / C);
     const int       thi = (int) ((int64_t) tpu * (r + 1) / C);
-    const UnitCoord uc  = unit_coord(P, u);
+    const UnitCoord uc  = unit_coord<R>(P, u);
 
     // Mask slots: the distinct mask rows this unit reads (one per query index
     // when the mask is shared by all heads).
     int n_ms = 0;
     if (o.mask) {
-        n_ms = o.m_ne2 == 1 ? (uc.rb * kDecRows + uc.rows - 1) / o.G - (uc.rb * kDecRows) / o.G + 1 : uc.rows;
+        n_ms = o.m_ne2 == 1 ? (uc.rb * R + uc.rows - 1) / o.G - (uc.rb * R) / o.G + 1 : uc.rows;
     }
 
-    // Role dispatch.  Each role's code is entered only through its own
-    // register-budget change (no path joins after them), so the compiler
-    // budgets the consumer code with the consumer's registers.
-    if (warp >= kDecWarps && kQ8) {
-        setmaxnreg_dec<Cfg::kRegsConvert>();
-    }
-    if (warp == Cfg::kProdWarp) {
+    if (warp == kDecWarps) {
         // ============================ producer ============================
         if (!kQ8 && lane == 0) {
             prefetch_tensormap(&kmap);
@@ -492,10 +436,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         const uint16_t *my_mr = nullptr;
         if (o.mask && lane < n_ms) {
             if (o.m_ne2 == 1) {
-                my_mr = mask_row(o, (uc.rb * kDecRows) / o.G + lane, 0, uc.b);
+                my_mr = mask_row(o, (uc.rb * R) / o.G + lane, 0, uc.b);
             } else {
                 int iq, hq;
-                row_coord(P, uc, lane, iq, hq);
+                row_coord<R>(P, uc, lane, iq, hq);
                 my_mr = mask_row(o, iq, hq, uc.b);
             }
         }
@@ -548,7 +492,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         }
         for (int tb = tlo; tb < thi && ok; tb += 32) {
             const int  tile = tb + lane;
-            const bool live = tile < thi && tile_live(P, uc, tile);
+            const bool live = tile < thi && tile_live<R>(P, uc, tile);
             uint32_t   bits = __ballot_sync(0xffffffffu, live);
             while (bits && ok) {
                 const int i = __ffs(bits) - 1;
@@ -563,8 +507,8 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     break;
                 }
                 uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
-                uint8_t *sV = sK + Cfg::kRawTile;
-                uint8_t *sM = sK + 2 * Cfg::kRawTile;
+                uint8_t *sV = sK + Cfg::kTile;
+                uint8_t *sM = sK + 2 * Cfg::kTile;
                 if constexpr (kQ8) {
                     // Rows are contiguous 34-B blocks; a tile starts at any even
                     // address.  Copy from the 16-B boundary below it (inside the
@@ -605,7 +549,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                     const uint32_t mbytes = stage_mask(ti, sM);
                     if (lane == 0) {
                         meta[stage] = make_int4(0, ti, kMetaData, 0);
-                        mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) (2 * Cfg::kRawTile) + mbytes);
+                        mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) (2 * Cfg::kTile) + mbytes);
 #pragma unroll
                         for (int h = 0; h < D / 64; ++h) {
                             tma_load_4d(sK + h * kDecBN * 128, &kmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
@@ -654,237 +598,160 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
     }
 
     if constexpr (kQ8) {
-        if (warp >= kDecWarps) {
-            // ============================ converters ==========================
-            // Tile i: K (and the tile's mask segments) into K slot i % 2 once
-            // the consumers are done with tile i - 2 there, then V into the V
-            // slot once they are done with tile i - 1's V.
-            const int cw    = warp - kDecWarps - 1;
-            const int ct    = cw * 32 + lane;
-            int       stage = 0;
-            uint32_t  phase = 0;
-            for (int it = 0;; ++it) {
-                const int      ks  = Cfg::kKSlots == 2 ? (it & 1) : 0;
-                const uint32_t kph = (uint32_t) (Cfg::kKSlots == 2 ? (it >> 1) & 1 : it & 1);
-                bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err,
-                                                                    DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
-                if (ok) {
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&kempty[ks], kph ^ 1u, abort_f, P.dev_err,
-                                                                   DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
-                }
-                if (!ok) {
-                    break;
-                }
-                const int4     md = meta[stage];
-                const uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
-                if (md.z == kMetaData) {
-                    q8_tile_to_f16<D, Cfg::kConvWarps>(smem_u32(sK) + (uint32_t) (md.w & 0xff),
-                                                        smem_u32(smem + Cfg::kOffCvtK + ks * Cfg::kF16Tile), md.x, cw,
-                                                        lane);
-                    for (int x = ct; x < n_ms * (kDecBN * 2 / 16); x += 32 * Cfg::kConvWarps) {
-                        const uint4 v = *reinterpret_cast<const uint4 *>(sK + 2 * Cfg::kRawTile + 16 * x);
-                        *reinterpret_cast<uint4 *>(smem + Cfg::kOffCvtM + ks * Cfg::kMaskBytes + 16 * x) = v;
-                    }
-                }
-                if (ct == 0) {
-                    cvt_meta[ks] = md;
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&kfull[ks]);
-                }
-                if (md.z != kMetaData) {
-                    break;
-                }
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(vempty, (uint32_t) (it & 1) ^ 1u, abort_f, P.dev_err,
-                                                               DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
-                if (!ok) {
-                    break;
-                }
-                q8_tile_to_f16<D, Cfg::kConvWarps>(smem_u32(sK + Cfg::kRawTile) + (uint32_t) ((md.w >> 8) & 0xff),
-                                                    smem_u32(smem + Cfg::kOffCvtV), md.x, cw, lane);
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(vfull);
-                    mbar_arrive(&empty_bar[stage]);
-                }
-                if (++stage == Cfg::kStages) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            }
-            return;
-        }
-    }
-
-    // ============================== consumers ==============================
-    if constexpr (kQ8) {
-        setmaxnreg_inc<Cfg::kRegsConsumer>();
-    }
-    const int g = lane >> 2;  // fragment row group
-    const int c = lane & 3;   // fragment column pair
-
-    float    m_run[2], l_run[2];
-    float    oacc[NT][4];
-    uint32_t qa[KS][4];
-    // BF16 operands keep ~16 mantissa bits of Q and P by a hi + lo split
-    // (two MMAs each); the F16 and Q8_0 paths never touch qlo.
-    uint32_t qlo[kBF16 ? KS : 1][4];
-    int      mslot[2];        // mask slot (staged row) of fragment rows g and g+8
-    int      vlo[2], vhi[2];  // mask rule: visible keys [vlo, vhi) of rows g and g+8
-    float    slope[2];
-
-    // ---- Q fragments of rows g and g+8 (QK-norm + RoPE applied in the PRO instance)
-    {
-        m_run[0] = m_run[1] = -INFINITY;
-        l_run[0] = l_run[1] = 0.0f;
+        // ======================= consumers, Q8_0 (transposed) ========================
+        // S^T = K Q^T and O^T += V^T P^T on mma.sync m16n8k16: the warp's 16 keys
+        // of a tile are the M dimension, the unit's 8 rows the N dimension.
+        // Head dims are assigned so that every K or V byte a thread needs is one
+        // contiguous run of a Q8_0 block: for S, thread (g, c) holds K dims
+        // [c*D/4, (c+1)*D/4) of keys g and g+8 (k-step ks: dims c*D/4 + 4ks +
+        // {0,1} and {2,3}, the same for Q^T); for PV it holds dims
+        // [g*D/8, (g+1)*D/8) of keys 2c, 2c+1, 2c+8, 2c+9 (m-tile mt: dims
+        // g*D/8 + mt and g*D/8 + D/16 + mt).  Every K and V value is
+        // dequantised once, in registers, as f16(d * q).
+        constexpr int KSQ = D / 16;  // k-steps of S^T = quant words of K per key and thread
+        constexpr int MT  = D / 16;  // m-tiles of O^T
+        constexpr int VW  = D / 32;  // quant words of V per key and thread (D/8 bytes)
+        constexpr int RB  = Cfg::kRowBytes;
+        const int     g   = lane >> 2;
+        const int     c   = lane & 3;
+        float         m_run[2] = {-INFINITY, -INFINITY};  // rows 2c, 2c+1 (log2 units)
+        float         l_run[2] = {0.0f, 0.0f};             // this thread's keys only until the flush
+        float         oacc[MT][4];
+        uint32_t      qb[KSQ][2];  // Q^T fragments of row g
+        int           mslot[2], vlo[2] = {0, 0}, vhi[2] = {0, 0};
+        float         slope[2];
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
+        for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                oacc[j][e] = 0.0f;
+                oacc[mt][e] = 0.0f;
             }
         }
-        const float *qrow[2];
-        int          qpos[2] = {0, 0};  // RoPE positions of rows g and g+8 (Q prologue)
+        {
+            int iq, hq;
+            row_coord<R>(P, uc, g < uc.rows ? g : 0, iq, hq);
+            const float *qrow = g < uc.rows ? reinterpret_cast<const float *>(o.q + (int64_t) iq * o.q_nb1 +
+                                                                              (int64_t) hq * o.q_nb2 +
+                                                                              (int64_t) uc.b * o.q_nb3)
+                                            : nullptr;
+            const int d0 = c * (D / 4);
+            float     x[KSQ][4];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int rr = g + 8 * i;
-            int       iq, hq;
-            row_coord(P, uc, rr < uc.rows ? rr : 0, iq, hq);
-            qrow[i]  = rr < uc.rows ? reinterpret_cast<const float *>(o.q + (int64_t) iq * o.q_nb1 +
-                                                                     (int64_t) hq * o.q_nb2 + (int64_t) uc.b * o.q_nb3)
-                                    : nullptr;
-            mslot[i] = o.m_ne2 == 1 ? iq - (uc.rb * kDecRows) / o.G : (rr < uc.rows ? rr : 0);
-            slope[i] = alibi_slope(o, hq);
-            if (o.mg_kind) {
-                mg_range(o, uc.b, iq, vlo[i], vhi[i]);
-            }
-            if (PRO && o.qp.rope && rr < uc.rows) {
-                qpos[i] = __ldg(o.qp.pos + iq + (int64_t) uc.b * o.n_q);
-            }
-        }
-        // This thread's Q values, x[i][ks][e] of row g + 8i: dims
-        // 16ks + 2c + (e & 1) + 8(e >> 1) (the m16n8k16 A fragment).
-        auto qdim = [&](int ks, int e) -> int { return 16 * ks + 2 * c + (e & 1) + 8 * (e >> 1); };
-        float x[2][KS][4];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
+            for (int ks = 0; ks < KSQ; ++ks) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    x[i][ks][e] = qrow[i] ? __ldg(qrow[i] + qdim(ks, e)) : 0.0f;
+                    x[ks][e] = qrow ? __ldg(qrow + d0 + 4 * ks + e) : 0.0f;
                 }
             }
-        }
-        if (PRO && o.qp.on) {
-            // QK-norm + RoPE: a row's D values are spread over its quad (c = 0..3)
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
+            if (PRO && o.qp.on) {
+                // QK-norm + RoPE: row g's D values are spread over its quad (c = 0..3)
                 if (o.qp.w) {
                     float ss = 0.0f;
 #pragma unroll
-                    for (int ks = 0; ks < KS; ++ks) {
+                    for (int ks = 0; ks < KSQ; ++ks) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            ss = fmaf(x[i][ks][e], x[i][ks][e], ss);
+                            ss = fmaf(x[ks][e], x[ks][e], ss);
                         }
                     }
                     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
                     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
                     const float sc = rn_scale(o.qp, ss, D);
 #pragma unroll
-                    for (int ks = 0; ks < KS; ++ks) {
+                    for (int ks = 0; ks < KSQ; ++ks) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            x[i][ks][e] = (x[i][ks][e] * sc) * __ldg(o.qp.w + qdim(ks, e));
+                            x[ks][e] = (x[ks][e] * sc) * __ldg(o.qp.w + d0 + 4 * ks + e);
                         }
                     }
                 }
                 if (o.qp.rope) {
-                    // dim d + D/2 is this thread's (ks + KS/2, e)
+                    // dim d + D/2 sits on thread c ^ 2 at the same (ks, e)
+                    const int qpos = g < uc.rows ? __ldg(o.qp.pos + iq + (int64_t) uc.b * o.n_q) : 0;
 #pragma unroll
-                    for (int ks = 0; ks < KS / 2; ++ks) {
+                    for (int ks = 0; ks < KSQ; ++ks) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const float a = x[i][ks][e], bb = x[i][ks + KS / 2][e];
-                            x[i][ks][e]          = rn_rotate(o.qp, a, bb, true, qpos[i], qdim(ks, e));
-                            x[i][ks + KS / 2][e] = rn_rotate(o.qp, bb, a, false, qpos[i], qdim(ks, e));
+                            const float pt = __shfl_xor_sync(0xffffffffu, x[ks][e], 2);
+                            x[ks][e] = rn_rotate(o.qp, x[ks][e], pt, c < 2, qpos, (d0 + 4 * ks + e) & (D / 2 - 1));
                         }
                     }
                 }
             }
+#pragma unroll
+            for (int ks = 0; ks < KSQ; ++ks) {
+                qb[ks][0] = pack2<false>(x[ks][0], x[ks][1]);
+                qb[ks][1] = pack2<false>(x[ks][2], x[ks][3]);
+            }
         }
 #pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
+        for (int i = 0; i < 2; ++i) {
+            const int rr = 2 * c + i;
+            int       iq, hq;
+            row_coord<R>(P, uc, rr < uc.rows ? rr : 0, iq, hq);
+            mslot[i] = o.m_ne2 == 1 ? iq - (uc.rb * R) / o.G : (rr < uc.rows ? rr : 0);
+            slope[i] = alibi_slope(o, hq);
+            if (o.mg_kind) {
+                mg_range(o, uc.b, iq, vlo[i], vhi[i]);
+            }
+        }
+        const int      kd0      = c * (D / 4);  // this thread's K dims (scores)
+        const int      vd0      = g * (D / 8);  // this thread's V dims (PV)
+        const uint32_t sel_half = (g & 1) ? 0x7632u : 0x5410u;
+        const int      src1     = 8 * c + (g >> 1);  // lanes holding P[row g][keys 2c, 2c+8] and [2c+1, 2c+9]
+        const int      src2     = src1 + 4;
+
+        int      stage = 0;
+        uint32_t phase = 0;
+        while (true) {
+            const bool got =
+                mbar_wait_bounded(&full_bar[stage], phase, abort_f, P.dev_err, DEVERR_TIMEOUT_FULL, P.wait_limit_ns);
+            if (!__all_sync(0xffffffffu, got)) {  // the shuffles and MMAs below need the whole warp
+                break;
+            }
+            const int4 md = meta[stage];
+            if (md.z != kMetaData) {
+                break;
+            }
+            const uint8_t  *stg  = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
+            const uint32_t  sK   = smem_u32(stg) + (uint32_t) (md.w & 0xff);
+            const uint32_t  sV   = smem_u32(stg + Cfg::kTile) + (uint32_t) ((md.w >> 8) & 0xff);
+            const uint16_t *sM   = reinterpret_cast<const uint16_t *>(stg + 2 * Cfg::kTile);
+            const int       tile = md.y;
+            const int       key0 = 16 * warp + g;  // keys key0 and key0 + 8 of the tile
+            // ---- S^T = K Q^T
+            float s[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            {
+                uint32_t       k0[KSQ], k1[KSQ];
+                const uint16_t e0 = q8_load_run<KSQ>(sK + key0 * RB + 34 * (kd0 / 32), kd0 % 32, k0);
+                const uint16_t e1 = q8_load_run<KSQ>(sK + (key0 + 8) * RB + 34 * (kd0 / 32), kd0 % 32, k1);
+                const __half2  d0 = __half2half2(__ushort_as_half(e0));
+                const __half2  d1 = __half2half2(__ushort_as_half(e1));
 #pragma unroll
-            for (int rg = 0; rg < 4; ++rg) {
-                // fragment register rg: row rg & 1, value pair (rg >> 1)
-                const float x0 = x[rg & 1][ks][2 * (rg >> 1)], x1 = x[rg & 1][ks][2 * (rg >> 1) + 1];
-                qa[ks][rg]     = pack2<kBF16>(x0, x1);
-                if constexpr (kBF16) {
-                    qlo[ks][rg] = split_lo_bf16(x0, x1, qa[ks][rg]);
+                for (int ks = 0; ks < KSQ; ++ks) {
+                    const uint32_t a[4] = {i8x2_scaled(k0[ks], 0x4140u, d0), i8x2_scaled(k1[ks], 0x4140u, d1),
+                                           i8x2_scaled(k0[ks], 0x4342u, d0), i8x2_scaled(k1[ks], 0x4342u, d1)};
+                    mma_16816<false>((ks & 1) ? s2 : s, a, qb[ks][0], qb[ks][1]);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    s[e] += s2[e];
                 }
             }
-        }
-    }
-
-    // ---- S = Q K^T over this warp's 16 keys of a swizzled 16-bit tile
-    auto tile_scores = [&](const uint8_t *sK, float (&s)[2][4]) {
-        const int mi   = lane >> 3;
-        const int r8   = lane & 7;
-        const int krow = 16 * warp + (mi >> 1) * 8 + r8;
-        float     s2[2][4];  // second accumulator chain (odd k-steps) for more MMA overlap
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
+            // ---- scale, softcap, mask, bounds; online softmax over keys (rows 2c, 2c+1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                s[nt][e]  = 0.0f;
-                s2[nt][e] = 0.0f;
-            }
-        }
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            const int      dim  = 16 * ks + (mi & 1) * 8;
-            const uint32_t addr = smem_u32(sK) + (dim >> 6) * (kDecBN * 128) + krow * 128 +
-                                  ((((dim & 63) >> 3) ^ r8) << 4);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(addr, b0, b1, b2, b3);
-            float(&acc)[2][4] = (!kBF16 && (ks & 1)) ? s2 : s;  // BF16 already pairs hi+lo MMAs
-            mma_16816<kBF16>(acc[0], qa[ks], b0, b1);
-            mma_16816<kBF16>(acc[1], qa[ks], b2, b3);
-            if constexpr (kBF16) {
-                mma_16816<true>(acc[0], qlo[ks], b0, b1);
-                mma_16816<true>(acc[1], qlo[ks], b2, b3);
-            }
-        }
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                s[nt][e] += s2[nt][e];
-            }
-        }
-    };
-
-    // ---- scale, softcap, mask, bounds; online softmax; P as A fragments
-    auto tile_softmax = [&](float (&s)[2][4], const uint16_t *sM, int tile, uint32_t (&pa)[4], uint32_t (&palo)[4]) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i   = e >> 1;
-                const int pos = tile * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1);
-                float     x   = s[nt][e] * o.scale_eff;
+                const int i   = e & 1;
+                const int kk  = key0 + 8 * (e >> 1);
+                const int pos = tile * kDecBN + kk;
+                float     x   = s[e] * o.scale_eff;
                 if (o.softcap != 0.0f) {
                     x = o.softcap * tanhf(x);
                 }
                 if (pos < o.n_kv) {
                     if (o.mask) {
                         // a -inf entry removes the key outright, whatever K held there
-                        const float mv = slope[i] * __half2float(__ushort_as_half(
-                                                        sM[mslot[i] * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1)]));
+                        const float mv = slope[i] * __half2float(__ushort_as_half(sM[mslot[i] * kDecBN + kk]));
                         x              = mv == -INFINITY ? -INFINITY : x + mv;
                     } else if (o.mg_kind) {
                         // a visible key adds the rule's 0 like a 0 mask entry
@@ -894,105 +761,402 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                 } else {
                     x = -INFINITY;
                 }
-                s[nt][e] = x;
+                s[e] = x;
+            }
+            // A row's keys are spread over the 8 lanes of its column c, so its
+            // maximum takes three shuffles.  They run only when some score
+            // exceeds the running max by more than 2^8 (one vote); otherwise
+            // P = 2^(s - m) <= 2^8 against the running max, exact enough in f16
+            // (the dense kernel's rule).
+            const bool grow = s[0] > m_run[0] + kQ8RescaleLog2 || s[2] > m_run[0] + kQ8RescaleLog2 ||
+                              s[1] > m_run[1] + kQ8RescaleLog2 || s[3] > m_run[1] + kQ8RescaleLog2;
+            if (__any_sync(0xffffffffu, grow)) {
+                float alpha[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    float mx = fmaxf(s[i], s[2 + i]);
+                    mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float mnew = fmaxf(m_run[i], mx);
+                    alpha[i]         = mnew == -INFINITY ? 1.0f : fast_exp2(m_run[i] - mnew);
+                    m_run[i]         = mnew;
+                    l_run[i] *= alpha[i];
+                }
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    oacc[mt][0] *= alpha[0];
+                    oacc[mt][1] *= alpha[1];
+                    oacc[mt][2] *= alpha[0];
+                    oacc[mt][3] *= alpha[1];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float muse = m_run[i] == -INFINITY ? 0.0f : m_run[i];
+                s[i]             = fast_exp2(s[i] - muse);
+                s[2 + i]         = fast_exp2(s[2 + i] - muse);
+                l_run[i] += s[i] + s[2 + i];
+            }
+            // ---- P^T fragments: P[row g][keys 2c, 2c+1] and [2c+8, 2c+9], from
+            // the lanes whose S^T rows are those keys
+            const uint32_t hlo = pack2<false>(s[0], s[1]);  // key key0: rows 2c, 2c+1
+            const uint32_t hhi = pack2<false>(s[2], s[3]);  // key key0 + 8
+            const uint32_t x1  = __shfl_sync(0xffffffffu, hlo, src1);
+            const uint32_t x2  = __shfl_sync(0xffffffffu, hlo, src2);
+            const uint32_t y1  = __shfl_sync(0xffffffffu, hhi, src1);
+            const uint32_t y2  = __shfl_sync(0xffffffffu, hhi, src2);
+            const uint32_t pb0 = __byte_perm(x1, x2, sel_half);
+            const uint32_t pb1 = __byte_perm(y1, y2, sel_half);
+            // ---- O^T += V^T P^T
+            {
+                uint32_t vw[4][VW];
+                uint16_t dvb[4];
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int key = 16 * warp + 2 * c + (jj & 1) + 8 * (jj >> 1);
+                    dvb[jj]       = q8_load_run<VW>(sV + key * RB + 34 * (vd0 / 32), vd0 % 32, vw[jj]);
+                    // rows past n_kv in the last tile hold stale bytes: a zero scale
+                    // keeps them finite (their P is 0, but 0 * inf would be NaN)
+                    dvb[jj] = tile * kDecBN + key < o.n_kv ? dvb[jj] : (uint16_t) 0;
+                }
+                const __half2 dA = __halves2half2(__ushort_as_half(dvb[0]), __ushort_as_half(dvb[1]));
+                const __half2 dB = __halves2half2(__ushort_as_half(dvb[2]), __ushort_as_half(dvb[3]));
+                // the two keys of each pair interleaved byte by byte: word k holds
+                // run bytes 2k, 2k+1 of both keys ([A B A B])
+                uint32_t ia[2 * VW], ib[2 * VW];
+#pragma unroll
+                for (int q = 0; q < VW; ++q) {
+                    ia[2 * q]     = __byte_perm(vw[0][q], vw[1][q], 0x5140u);
+                    ia[2 * q + 1] = __byte_perm(vw[0][q], vw[1][q], 0x7362u);
+                    ib[2 * q]     = __byte_perm(vw[2][q], vw[3][q], 0x5140u);
+                    ib[2 * q + 1] = __byte_perm(vw[2][q], vw[3][q], 0x7362u);
+                }
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    constexpr int  kHalfRun = D / 16;
+                    const int      b0 = mt, b1 = kHalfRun + mt;  // run bytes of dims vd0 + mt, vd0 + D/16 + mt
+                    const uint32_t s0 = (b0 & 1) ? 0x4342u : 0x4140u;
+                    const uint32_t s1 = (b1 & 1) ? 0x4342u : 0x4140u;
+                    const uint32_t a[4] = {i8x2_scaled(ia[b0 >> 1], s0, dA), i8x2_scaled(ia[b1 >> 1], s1, dA),
+                                           i8x2_scaled(ib[b0 >> 1], s0, dB), i8x2_scaled(ib[b1 >> 1], s1, dB)};
+                    mma_16816<false>(oacc[mt], a, pb0, pb1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty_bar[stage]);
+            }
+            if (++stage == Cfg::kStages) {
+                stage = 0;
+                phase ^= 1u;
             }
         }
-        float alpha[2];
+
+        // ---- merge of the four warps' partial results
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-            float mx = fmaxf(fmaxf(s[0][2 * i], s[0][2 * i + 1]), fmaxf(s[1][2 * i], s[1][2 * i + 1]));
-            mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float mnew = fmaxf(m_run[i], mx);
-            const float muse = mnew == -INFINITY ? 0.0f : mnew;
-            alpha[i]         = fast_exp2(m_run[i] - muse);
-            m_run[i]         = mnew;
-            float rs         = 0.0f;
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 4);
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 8);
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 16);
+        }
+        if (g == 0) {
+            s_m[warp * kDecRows + 2 * c]     = m_run[0];
+            s_m[warp * kDecRows + 2 * c + 1] = m_run[1];
+            s_l[warp * kDecRows + 2 * c]     = l_run[0];
+            s_l[warp * kDecRows + 2 * c + 1] = l_run[1];
+        }
+        named_bar_sync(1, kDecWarps * 32);
+        float fac[2];
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                s[nt][2 * i]     = fast_exp2(s[nt][2 * i] - muse);
-                s[nt][2 * i + 1] = fast_exp2(s[nt][2 * i + 1] - muse);
-                rs += s[nt][2 * i] + s[nt][2 * i + 1];
-            }
-            l_run[i] = l_run[i] * alpha[i] + rs;
-        }
-        if (__any_sync(0xffffffffu, alpha[0] != 1.0f || alpha[1] != 1.0f)) {
+        for (int i = 0; i < 2; ++i) {
+            float mx = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                oacc[j][0] *= alpha[0];
-                oacc[j][1] *= alpha[0];
-                oacc[j][2] *= alpha[1];
-                oacc[j][3] *= alpha[1];
+            for (int w = 0; w < kDecWarps; ++w) {
+                mx = fmaxf(mx, s_m[w * kDecRows + 2 * c + i]);
             }
+            fac[i] = m_run[i] == -INFINITY ? 0.0f : fast_exp2(m_run[i] - mx);
         }
-        pa[0] = pack2<kBF16>(s[0][0], s[0][1]);
-        pa[1] = pack2<kBF16>(s[0][2], s[0][3]);
-        pa[2] = pack2<kBF16>(s[1][0], s[1][1]);
-        pa[3] = pack2<kBF16>(s[1][2], s[1][3]);
-        if constexpr (kBF16) {
-            palo[0] = split_lo_bf16(s[0][0], s[0][1], pa[0]);
-            palo[1] = split_lo_bf16(s[0][2], s[0][3], pa[1]);
-            palo[2] = split_lo_bf16(s[1][0], s[1][1], pa[2]);
-            palo[3] = split_lo_bf16(s[1][2], s[1][3], pa[3]);
-        }
-    };
-
-    // ---- O += P V over this warp's 16 keys
-    auto tile_pv = [&](const uint8_t *sV, const uint32_t (&pa)[4], const uint32_t (&palo)[4]) {
-        const int mi   = lane >> 3;
-        const int r8   = lane & 7;
-        const int vrow = 16 * warp + (mi & 1) * 8 + r8;
+        // four turns; in turn t warp w adds its m-tiles of block (w + t) % 4, so
+        // each element has one writer per turn (plain stores, no atomics)
+        constexpr int MTB = MT / 4;
 #pragma unroll
-        for (int dn = 0; dn < D / 16; ++dn) {
-            const int      dim  = 16 * dn + (mi >> 1) * 8;
-            const uint32_t addr = smem_u32(sV) + (dim >> 6) * (kDecBN * 128) + vrow * 128 +
-                                  ((((dim & 63) >> 3) ^ r8) << 4);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(addr, b0, b1, b2, b3);
-            mma_16816<kBF16>(oacc[2 * dn], pa, b0, b1);
-            mma_16816<kBF16>(oacc[2 * dn + 1], pa, b2, b3);
-            if constexpr (kBF16) {
-                mma_16816<true>(oacc[2 * dn], palo, b0, b1);
-                mma_16816<true>(oacc[2 * dn + 1], palo, b2, b3);
+        for (int t = 0; t < 4; ++t) {
+            const int bsel = (warp + t) & 3;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                if (bb == bsel) {
+#pragma unroll
+                    for (int jj = 0; jj < MTB; ++jj) {
+                        const int mt = bb * MTB + jj;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int   row = 2 * c + (e & 1);
+                            const int   dim = vd0 + (e >> 1) * (D / 16) + mt;
+                            float      *mp  = &merge[row * Cfg::kMergeStride + dim];
+                            const float v   = oacc[mt][e] * fac[e & 1];
+                            *mp             = t == 0 ? v : *mp + v;
+                        }
+                    }
+                }
             }
-        }
-    };
-
-    if constexpr (kQ8) {
-        for (int it = 0;; ++it) {
-            const int      ks  = Cfg::kKSlots == 2 ? (it & 1) : 0;
-            const uint32_t kph = (uint32_t) (Cfg::kKSlots == 2 ? (it >> 1) & 1 : it & 1);
-            bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&kfull[ks], kph, abort_f, P.dev_err,
-                                                                DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
-            if (!ok) {
-                break;
+            if (t == 0 && threadIdx.x < R) {
+                const int row = threadIdx.x;
+                float     mx  = -INFINITY;
+#pragma unroll
+                for (int ww = 0; ww < kDecWarps; ++ww) {
+                    mx = fmaxf(mx, s_m[ww * kDecRows + row]);
+                }
+                float l = 0.0f;
+#pragma unroll
+                for (int ww = 0; ww < kDecWarps; ++ww) {
+                    const float mw = s_m[ww * kDecRows + row];
+                    l += mw == -INFINITY ? 0.0f : s_l[ww * kDecRows + row] * fast_exp2(mw - mx);
+                }
+                s_fin[row]            = mx;
+                s_fin[kDecRows + row] = l;
             }
-            const int4 md = cvt_meta[ks];
-            if (md.z != kMetaData) {
-                break;
-            }
-            float s[2][4];
-            tile_scores(smem + Cfg::kOffCvtK + ks * Cfg::kF16Tile, s);
-            uint32_t pa[4], palo[4];
-            tile_softmax(s, reinterpret_cast<const uint16_t *>(smem + Cfg::kOffCvtM + ks * Cfg::kMaskBytes), md.y, pa,
-                         palo);
-            // the K slot and its mask segments are free once the softmax has read them
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&kempty[ks]);
-            }
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(vfull, (uint32_t) (it & 1), abort_f, P.dev_err,
-                                                           DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
-            if (!ok) {
-                break;
-            }
-            tile_pv(smem + Cfg::kOffCvtV, pa, palo);
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(vempty);
-            }
+            named_bar_sync(1, kDecWarps * 32);
         }
     } else {
+        // ======================= consumers, F16 / BF16 ========================
+        const int g = lane >> 2;  // fragment row group
+        const int c = lane & 3;   // fragment column pair
+
+        float    m_run[2], l_run[2];
+        float    oacc[NT][4];
+        uint32_t qa[KS][4];
+        // BF16 operands keep ~16 mantissa bits of Q and P by a hi + lo split
+        // (two MMAs each); the F16 and Q8_0 paths never touch qlo.
+        uint32_t qlo[kBF16 ? KS : 1][4];
+        int      mslot[2];        // mask slot (staged row) of fragment rows g and g+8
+        int      vlo[2], vhi[2];  // mask rule: visible keys [vlo, vhi) of rows g and g+8
+        float    slope[2];
+
+        // ---- Q fragments of rows g and g+8 (QK-norm + RoPE applied in the PRO instance)
+        {
+            m_run[0] = m_run[1] = -INFINITY;
+            l_run[0] = l_run[1] = 0.0f;
+    #pragma unroll
+            for (int j = 0; j < NT; ++j) {
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    oacc[j][e] = 0.0f;
+                }
+            }
+            const float *qrow[2];
+            int          qpos[2] = {0, 0};  // RoPE positions of rows g and g+8 (Q prologue)
+    #pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int rr = g + 8 * i;
+                int       iq, hq;
+                row_coord<R>(P, uc, rr < uc.rows ? rr : 0, iq, hq);
+                qrow[i]  = rr < uc.rows ? reinterpret_cast<const float *>(o.q + (int64_t) iq * o.q_nb1 +
+                                                                         (int64_t) hq * o.q_nb2 + (int64_t) uc.b * o.q_nb3)
+                                        : nullptr;
+                mslot[i] = o.m_ne2 == 1 ? iq - (uc.rb * R) / o.G : (rr < uc.rows ? rr : 0);
+                slope[i] = alibi_slope(o, hq);
+                if (o.mg_kind) {
+                    mg_range(o, uc.b, iq, vlo[i], vhi[i]);
+                }
+                if (PRO && o.qp.rope && rr < uc.rows) {
+                    qpos[i] = __ldg(o.qp.pos + iq + (int64_t) uc.b * o.n_q);
+                }
+            }
+            // This thread's Q values, x[i][ks][e] of row g + 8i: dims
+            // 16ks + 2c + (e & 1) + 8(e >> 1) (the m16n8k16 A fragment).
+            auto qdim = [&](int ks, int e) -> int { return 16 * ks + 2 * c + (e & 1) + 8 * (e >> 1); };
+            float x[2][KS][4];
+    #pragma unroll
+            for (int i = 0; i < 2; ++i) {
+    #pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+    #pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        x[i][ks][e] = qrow[i] ? __ldg(qrow[i] + qdim(ks, e)) : 0.0f;
+                    }
+                }
+            }
+            if (PRO && o.qp.on) {
+                // QK-norm + RoPE: a row's D values are spread over its quad (c = 0..3)
+    #pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    if (o.qp.w) {
+                        float ss = 0.0f;
+    #pragma unroll
+                        for (int ks = 0; ks < KS; ++ks) {
+    #pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                ss = fmaf(x[i][ks][e], x[i][ks][e], ss);
+                            }
+                        }
+                        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                        const float sc = rn_scale(o.qp, ss, D);
+    #pragma unroll
+                        for (int ks = 0; ks < KS; ++ks) {
+    #pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                x[i][ks][e] = (x[i][ks][e] * sc) * __ldg(o.qp.w + qdim(ks, e));
+                            }
+                        }
+                    }
+                    if (o.qp.rope) {
+                        // dim d + D/2 is this thread's (ks + KS/2, e)
+    #pragma unroll
+                        for (int ks = 0; ks < KS / 2; ++ks) {
+    #pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float a = x[i][ks][e], bb = x[i][ks + KS / 2][e];
+                                x[i][ks][e]          = rn_rotate(o.qp, a, bb, true, qpos[i], qdim(ks, e));
+                                x[i][ks + KS / 2][e] = rn_rotate(o.qp, bb, a, false, qpos[i], qdim(ks, e));
+                            }
+                        }
+                    }
+                }
+            }
+    #pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+    #pragma unroll
+                for (int rg = 0; rg < 4; ++rg) {
+                    // fragment register rg: row rg & 1, value pair (rg >> 1)
+                    const float x0 = x[rg & 1][ks][2 * (rg >> 1)], x1 = x[rg & 1][ks][2 * (rg >> 1) + 1];
+                    qa[ks][rg]     = pack2<kBF16>(x0, x1);
+                    if constexpr (kBF16) {
+                        qlo[ks][rg] = split_lo_bf16(x0, x1, qa[ks][rg]);
+                    }
+                }
+            }
+        }
+
+        // ---- S = Q K^T over this warp's 16 keys of a swizzled 16-bit tile
+        auto tile_scores = [&](const uint8_t *sK, float (&s)[2][4]) {
+            const int mi   = lane >> 3;
+            const int r8   = lane & 7;
+            const int krow = 16 * warp + (mi >> 1) * 8 + r8;
+            float     s2[2][4];  // second accumulator chain (odd k-steps) for more MMA overlap
+    #pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    s[nt][e]  = 0.0f;
+                    s2[nt][e] = 0.0f;
+                }
+            }
+    #pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int      dim  = 16 * ks + (mi & 1) * 8;
+                const uint32_t addr = smem_u32(sK) + (dim >> 6) * (kDecBN * 128) + krow * 128 +
+                                      ((((dim & 63) >> 3) ^ r8) << 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(addr, b0, b1, b2, b3);
+                float(&acc)[2][4] = (!kBF16 && (ks & 1)) ? s2 : s;  // BF16 already pairs hi+lo MMAs
+                mma_16816<kBF16>(acc[0], qa[ks], b0, b1);
+                mma_16816<kBF16>(acc[1], qa[ks], b2, b3);
+                if constexpr (kBF16) {
+                    mma_16816<true>(acc[0], qlo[ks], b0, b1);
+                    mma_16816<true>(acc[1], qlo[ks], b2, b3);
+                }
+            }
+    #pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    s[nt][e] += s2[nt][e];
+                }
+            }
+        };
+
+        // ---- scale, softcap, mask, bounds; online softmax; P as A fragments
+        auto tile_softmax = [&](float (&s)[2][4], const uint16_t *sM, int tile, uint32_t (&pa)[4], uint32_t (&palo)[4]) {
+    #pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i   = e >> 1;
+                    const int pos = tile * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1);
+                    float     x   = s[nt][e] * o.scale_eff;
+                    if (o.softcap != 0.0f) {
+                        x = o.softcap * tanhf(x);
+                    }
+                    if (pos < o.n_kv) {
+                        if (o.mask) {
+                            // a -inf entry removes the key outright, whatever K held there
+                            const float mv = slope[i] * __half2float(__ushort_as_half(
+                                                            sM[mslot[i] * kDecBN + 16 * warp + 8 * nt + 2 * c + (e & 1)]));
+                            x              = mv == -INFINITY ? -INFINITY : x + mv;
+                        } else if (o.mg_kind) {
+                            // a visible key adds the rule's 0 like a 0 mask entry
+                            x = pos >= vlo[i] && pos < vhi[i] ? x + 0.0f : -INFINITY;
+                        }
+                        x *= kLog2e;
+                    } else {
+                        x = -INFINITY;
+                    }
+                    s[nt][e] = x;
+                }
+            }
+            float alpha[2];
+    #pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                float mx = fmaxf(fmaxf(s[0][2 * i], s[0][2 * i + 1]), fmaxf(s[1][2 * i], s[1][2 * i + 1]));
+                mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx       = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mnew = fmaxf(m_run[i], mx);
+                const float muse = mnew == -INFINITY ? 0.0f : mnew;
+                alpha[i]         = fast_exp2(m_run[i] - muse);
+                m_run[i]         = mnew;
+                float rs         = 0.0f;
+    #pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    s[nt][2 * i]     = fast_exp2(s[nt][2 * i] - muse);
+                    s[nt][2 * i + 1] = fast_exp2(s[nt][2 * i + 1] - muse);
+                    rs += s[nt][2 * i] + s[nt][2 * i + 1];
+                }
+                l_run[i] = l_run[i] * alpha[i] + rs;
+            }
+            if (__any_sync(0xffffffffu, alpha[0] != 1.0f || alpha[1] != 1.0f)) {
+    #pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    oacc[j][0] *= alpha[0];
+                    oacc[j][1] *= alpha[0];
+                    oacc[j][2] *= alpha[1];
+                    oacc[j][3] *= alpha[1];
+                }
+            }
+            pa[0] = pack2<kBF16>(s[0][0], s[0][1]);
+            pa[1] = pack2<kBF16>(s[0][2], s[0][3]);
+            pa[2] = pack2<kBF16>(s[1][0], s[1][1]);
+            pa[3] = pack2<kBF16>(s[1][2], s[1][3]);
+            if constexpr (kBF16) {
+                palo[0] = split_lo_bf16(s[0][0], s[0][1], pa[0]);
+                palo[1] = split_lo_bf16(s[0][2], s[0][3], pa[1]);
+                palo[2] = split_lo_bf16(s[1][0], s[1][1], pa[2]);
+                palo[3] = split_lo_bf16(s[1][2], s[1][3], pa[3]);
+            }
+        };
+
+        // ---- O += P V over this warp's 16 keys
+        auto tile_pv = [&](const uint8_t *sV, const uint32_t (&pa)[4], const uint32_t (&palo)[4]) {
+            const int mi   = lane >> 3;
+            const int r8   = lane & 7;
+            const int vrow = 16 * warp + (mi & 1) * 8 + r8;
+    #pragma unroll
+            for (int dn = 0; dn < D / 16; ++dn) {
+                const int      dim  = 16 * dn + (mi >> 1) * 8;
+                const uint32_t addr = smem_u32(sV) + (dim >> 6) * (kDecBN * 128) + vrow * 128 +
+                                      ((((dim & 63) >> 3) ^ r8) << 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(addr, b0, b1, b2, b3);
+                mma_16816<kBF16>(oacc[2 * dn], pa, b0, b1);
+                mma_16816<kBF16>(oacc[2 * dn + 1], pa, b2, b3);
+                if constexpr (kBF16) {
+                    mma_16816<true>(oacc[2 * dn], palo, b0, b1);
+                    mma_16816<true>(oacc[2 * dn + 1], palo, b2, b3);
+                }
+            }
+        };
+
         int      stage = 0;
         uint32_t phase = 0;
         while (true) {
@@ -1010,8 +1174,8 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             float          s[2][4];
             uint32_t       pa[4], palo[4];
             tile_scores(sK, s);
-            tile_softmax(s, reinterpret_cast<const uint16_t *>(sK + 2 * Cfg::kRawTile), md.y, pa, palo);
-            tile_pv(sK + Cfg::kRawTile, pa, palo);
+            tile_softmax(s, reinterpret_cast<const uint16_t *>(sK + 2 * Cfg::kTile), md.y, pa, palo);
+            tile_pv(sK + Cfg::kTile, pa, palo);
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&empty_bar[stage]);
@@ -1021,80 +1185,81 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
                 phase ^= 1u;
             }
         }
-    }
 
-    // ---- merge of the four warps' partial results (rows of this CTA's range)
-    // Head-dim index held by accumulator element (j, e) (column part only).
-    auto out_dim = [&](int j, int e) -> int { return 8 * j + 2 * c + (e & 1); };
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
-        l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 2);
-    }
-    if (c == 0) {
-        s_m[warp * kDecRows + g]     = m_run[0];
-        s_m[warp * kDecRows + g + 8] = m_run[1];
-        s_l[warp * kDecRows + g]     = l_run[0];
-        s_l[warp * kDecRows + g + 8] = l_run[1];
-    }
-    named_bar_sync(1, kDecWarps * 32);
-    float fac[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int row = g + 8 * i;
-        float     mx  = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kDecWarps; ++w) {
-            mx = fmaxf(mx, s_m[w * kDecRows + row]);
+        // ---- merge of the four warps' partial results (rows of this CTA's range)
+        // Head-dim index held by accumulator element (j, e) (column part only).
+        auto out_dim = [&](int j, int e) -> int { return 8 * j + 2 * c + (e & 1); };
+    #pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
+            l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 2);
         }
-        fac[i] = m_run[i] == -INFINITY ? 0.0f : fast_exp2(m_run[i] - mx);
-    }
-    // The four warps' partial O, rescaled to the common row max, summed in
-    // shared memory in four turns; in turn t warp w adds its n8 tiles of
-    // column block (w + t) % 4, so every warp works in every turn and each
-    // element has one writer per turn (plain stores, no atomics).  Threads
-    // 0-15 also merge the row statistics.
-    constexpr int NTB = NT / 4;  // n8 tiles per column block
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const int bsel = (warp + t) & 3;
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-            if (bb == bsel) {
-#pragma unroll
-                for (int jj = 0; jj < NTB; ++jj) {
-                    const int j = bb * NTB + jj;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float      *mp = &merge[(g + 8 * (e >> 1)) * Cfg::kMergeStride + out_dim(j, e)];
-                        const float v  = oacc[j][e] * fac[e >> 1];
-                        *mp            = t == 0 ? v : *mp + v;
+        if (c == 0) {
+            s_m[warp * kDecRows + g]     = m_run[0];
+            s_m[warp * kDecRows + g + 8] = m_run[1];
+            s_l[warp * kDecRows + g]     = l_run[0];
+            s_l[warp * kDecRows + g + 8] = l_run[1];
+        }
+        named_bar_sync(1, kDecWarps * 32);
+        float fac[2];
+    #pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int row = g + 8 * i;
+            float     mx  = -INFINITY;
+    #pragma unroll
+            for (int w = 0; w < kDecWarps; ++w) {
+                mx = fmaxf(mx, s_m[w * kDecRows + row]);
+            }
+            fac[i] = m_run[i] == -INFINITY ? 0.0f : fast_exp2(m_run[i] - mx);
+        }
+        // The four warps' partial O, rescaled to the common row max, summed in
+        // shared memory in four turns; in turn t warp w adds its n8 tiles of
+        // column block (w + t) % 4, so every warp works in every turn and each
+        // element has one writer per turn (plain stores, no atomics).  Threads
+        // 0-15 also merge the row statistics.
+        constexpr int NTB = NT / 4;  // n8 tiles per column block
+    #pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int bsel = (warp + t) & 3;
+    #pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                if (bb == bsel) {
+    #pragma unroll
+                    for (int jj = 0; jj < NTB; ++jj) {
+                        const int j = bb * NTB + jj;
+    #pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            float      *mp = &merge[(g + 8 * (e >> 1)) * Cfg::kMergeStride + out_dim(j, e)];
+                            const float v  = oacc[j][e] * fac[e >> 1];
+                            *mp            = t == 0 ? v : *mp + v;
+                        }
                     }
                 }
             }
-        }
-        if (t == 0 && threadIdx.x < kDecRows) {
-            const int row = threadIdx.x;
-            float     mx  = -INFINITY;
-#pragma unroll
-            for (int ww = 0; ww < kDecWarps; ++ww) {
-                mx = fmaxf(mx, s_m[ww * kDecRows + row]);
+            if (t == 0 && threadIdx.x < kDecRows) {
+                const int row = threadIdx.x;
+                float     mx  = -INFINITY;
+    #pragma unroll
+                for (int ww = 0; ww < kDecWarps; ++ww) {
+                    mx = fmaxf(mx, s_m[ww * kDecRows + row]);
+                }
+                float l = 0.0f;
+    #pragma unroll
+                for (int ww = 0; ww < kDecWarps; ++ww) {
+                    const float mw = s_m[ww * kDecRows + row];
+                    l += mw == -INFINITY ? 0.0f : s_l[ww * kDecRows + row] * fast_exp2(mw - mx);
+                }
+                s_fin[row]            = mx;
+                s_fin[kDecRows + row] = l;
             }
-            float l = 0.0f;
-#pragma unroll
-            for (int ww = 0; ww < kDecWarps; ++ww) {
-                const float mw = s_m[ww * kDecRows + row];
-                l += mw == -INFINITY ? 0.0f : s_l[ww * kDecRows + row] * fast_exp2(mw - mx);
-            }
-            s_fin[row]            = mx;
-            s_fin[kDecRows + row] = l;
+            named_bar_sync(1, kDecWarps * 32);
         }
-        named_bar_sync(1, kDecWarps * 32);
     }
 
     // ---- merge across the cluster and write the output
-    // CTA r finishes head dims [r*D/C, (r+1)*D/C) of every row from all C
-    // partials (read from the peers' shared memory); C == 1 writes them all.
+    // CTA r finishes its share of the head dims (the r-th of C nearly equal
+    // ranges of float4 chunks) of every row from all C partials, read from the
+    // peers' shared memory; C == 1 writes them all.
     const bool cl_ok = C == 1 || [&] {
         if (threadIdx.x == 0) {
             for (int k = 0; k < C; ++k) {
@@ -1112,13 +1277,14 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
         }
         return true;
     }();
-    const int      dper   = D / C;        // dims per CTA (C divides D / 4)
-    const int      chunks = dper / 4;     // float4 chunks per row and CTA
+    // this CTA's float4 chunks of every row: [ch0, ch1) of the row's D / 4
+    const int      ch0    = r * (D / 4) / C;
+    const int      chunks = (r + 1) * (D / 4) / C - ch0;
     const uint32_t fin_a  = smem_u32(s_fin);
     const uint32_t mrg_a  = smem_u32(merge);
     for (int idx = threadIdx.x; cl_ok && idx < kDecRows * chunks; idx += kDecWarps * 32) {
         const int row = idx / chunks;
-        const int d   = r * dper + (idx % chunks) * 4;
+        const int d   = (ch0 + idx % chunks) * 4;
         if (row >= uc.rows) {
             continue;
         }
@@ -1142,7 +1308,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
             l += lk[k] * mk[k];
         }
         int iq, hq;
-        row_coord(P, uc, row, iq, hq);
+        row_coord<R>(P, uc, row, iq, hq);
         float fs = 1.0f;
         if (o.sinks) {
             const float ts = o.sinks[hq] * kLog2e;
@@ -1217,12 +1383,11 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, 2)
 namespace {
 
 // Per-device, per-instance launch set-up (shared-memory size, the
-// non-portable cluster size, the register pool check of the Q8_0 split) and
-// the largest cluster size the device schedules for it.
+// non-portable cluster size) and the cluster sizes the device schedules for it.
 struct InstInfo {
     bool ok = false;
-    // clusters of 2^i CTAs the device keeps resident at once (0 = not launchable)
-    int active[5] = {0, 0, 0, 0, 0};
+    // clusters of c CTAs the device keeps resident at once (0 = not launchable)
+    int active[kDecMaxCluster + 1] = {};
 };
 constexpr int kMaxDev = 64;
 std::mutex    g_inst_mutex;
@@ -1242,18 +1407,11 @@ const InstInfo &inst_info(int dev) {
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess) {
         return in;
     }
-    if (Cfg::kQ8) {
-        // setmaxnreg draws on the registers the CTA was launched with
-        cudaFuncAttributes fa;
-        if (cudaFuncGetAttributes(&fa, k) != cudaSuccess || fa.numRegs < (int) Cfg::kRegsLaunch) {
-            return in;
-        }
-    }
     in.ok = true;
     const bool big =
         ACEFA_DEC_MAX_CLUSTER > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
                                          cudaSuccess;
-    for (int i = 0, c = 1; c <= ACEFA_DEC_MAX_CLUSTER && c <= kDecMaxCluster; ++i, c *= 2) {
+    for (int c = 1; c <= ACEFA_DEC_MAX_CLUSTER && c <= kDecMaxCluster; ++c) {
         if (c > 8 && !big) {
             break;
         }
@@ -1270,7 +1428,7 @@ const InstInfo &inst_info(int dev) {
         cfg.numAttrs           = 1;
         int n                  = 0;
         if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess) {
-            in.active[i] = n;
+            in.active[c] = n;
         }
     }
     cudaGetLastError();  // a refused query leaves no sticky error
@@ -1324,8 +1482,8 @@ int cluster_for(bool pro, int units, int tiles_per_unit) {
     }
     const InstInfo &in = pro ? inst_info<KV_TYPE, D, true>(dev) : inst_info<KV_TYPE, D, false>(dev);
     int             best = 1;
-    for (int i = 1, c = 2; i < 5 && in.ok; ++i, c *= 2) {
-        if (c <= tiles_per_unit && units <= in.active[i]) {
+    for (int c = 2; c <= kDecMaxCluster && in.ok; ++c) {
+        if (c <= tiles_per_unit && units <= in.active[c]) {
             best = c;
         }
     }

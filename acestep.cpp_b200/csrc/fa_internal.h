@@ -113,6 +113,10 @@ constexpr int kDecStages     = 3;   // pipeline depth
 constexpr int kDecRows       = 16;  // rows per unit (one m16 MMA tile)
 constexpr int kDecMaxCluster = 16;  // CTAs per unit (16 needs the non-portable cluster size)
 
+// Rows per unit: one m16 MMA tile for F16/BF16; one n8 tile of the transposed
+// Q8_0 consumer.
+__host__ __device__ constexpr int decode_unit_rows(int kv_type) { return kv_type == ACEFA_TYPE_Q8_0 ? 8 : kDecRows; }
+
 struct DecodeParams {
     OpDesc  op;
     int     n_rb;            // row blocks per (b, hk)
@@ -137,8 +141,8 @@ struct DecodeLaunch {
 
 cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches);
 // CTAs per unit for the decode kernel of these operands on the current
-// device: the largest power of two (<= kDecMaxCluster, <= the unit's key
-// tiles) whose clusters for all `units` are resident at once; 1 otherwise.
+// device: the largest size (<= kDecMaxCluster, <= the unit's key tiles)
+// whose clusters for all `units` are resident at once; 1 otherwise.
 int         decode_cluster(int kv_type, int D, bool prologue, int units, int tiles_per_unit);
 
 // ------------------------------------------------------------------ dense
