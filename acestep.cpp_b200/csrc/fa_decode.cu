@@ -490,9 +490,87 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
                 append_load<KV_TYPE, D, PRO>(P, uc.hk, uc.bk, lane, app_k, app_v);
             }
         }
+        // Copies tile ti into the next stage (K, V, and the mask segments).
+        auto issue = [&](int ti) {
+            ok = acquire();
+            if (!ok) {
+                return;
+            }
+            uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
+            uint8_t *sV = sK + Cfg::kTile;
+            uint8_t *sM = sK + 2 * Cfg::kTile;
+            if constexpr (kQ8) {
+                // Rows are contiguous 34-B blocks; a tile starts at any even
+                // address.  Copy from the 16-B boundary below it (inside the
+                // tensor: its base is 16-B aligned) and let the consumers
+                // index from the lead; the last <16 bytes go by plain copies.
+                const int      j0     = ti * kDecBN;
+                const int      nrows  = min(kDecBN, o.n_kv - j0);
+                const uint32_t bytes  = (uint32_t) nrows * Cfg::kRowBytes;
+                const char    *kg     = kbase + (int64_t) j0 * Cfg::kRowBytes;
+                const char    *vg     = vbase + (int64_t) j0 * Cfg::kRowBytes;
+                const uint32_t lead_k = (uint32_t) (reinterpret_cast<uintptr_t>(kg) & 15u);
+                const uint32_t lead_v = (uint32_t) (reinterpret_cast<uintptr_t>(vg) & 15u);
+                const uint32_t bulk_k = (lead_k + bytes) & ~15u;
+                const uint32_t bulk_v = (lead_v + bytes) & ~15u;
+                if ((uint32_t) lane < lead_k + bytes - bulk_k) {
+                    sK[bulk_k + lane] = (uint8_t) kg[(int) (bulk_k + lane) - (int) lead_k];
+                }
+                if ((uint32_t) lane < lead_v + bytes - bulk_v) {
+                    sV[bulk_v + lane] = (uint8_t) vg[(int) (bulk_v + lane) - (int) lead_v];
+                }
+                const uint32_t mbytes = stage_mask(ti, sM);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (mbytes && lane < n_ms) {
+                    bulk_load(sM + lane * kDecBN * 2, my_mr + ti * kDecBN, kDecBN * 2, &full_bar[stage]);
+                }
+                if (lane == 0) {
+                    meta[stage] = make_int4(nrows, ti, kMetaData, (int) (lead_k | (lead_v << 8)));
+                    mbar_arrive_expect_tx(&full_bar[stage], bulk_k + bulk_v + mbytes);
+                    if (bulk_k) {
+                        bulk_load(sK, kg - lead_k, bulk_k, &full_bar[stage]);
+                    }
+                    if (bulk_v) {
+                        bulk_load(sV, vg - lead_v, bulk_v, &full_bar[stage]);
+                    }
+                }
+            } else {
+                const uint32_t mbytes = stage_mask(ti, sM);
+                if (lane == 0) {
+                    meta[stage] = make_int4(0, ti, kMetaData, 0);
+                    mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) (2 * Cfg::kTile) + mbytes);
+#pragma unroll
+                    for (int h = 0; h < D / 64; ++h) {
+                        tma_load_4d(sK + h * kDecBN * 128, &kmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
+                                    &full_bar[stage]);
+                        tma_load_4d(sV + h * kDecBN * 128, &vmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
+                                    &full_bar[stage]);
+                    }
+                }
+                __syncwarp();
+                if (mbytes && lane < n_ms) {
+                    bulk_load(sM + lane * kDecBN * 2, my_mr + ti * kDecBN, kDecBN * 2, &full_bar[stage]);
+                }
+            }
+            pend[stage] = (int) phase;
+            __syncwarp();
+            advance();
+        };
+        // The first stages go out before the liveness scan of the mask (a
+        // global-memory round trip) returns: a dead tile among them only adds
+        // keys of zero weight.  Not with a fused append, whose row must be
+        // written before its tile is read.
+        int spec_end = tlo;
+        if (!P.append_pos) {
+            spec_end = min(thi, tlo + Cfg::kStages);
+            for (int ti = tlo; ti < spec_end && ok; ++ti) {
+                issue(ti);
+            }
+        }
         for (int tb = tlo; tb < thi && ok; tb += 32) {
             const int  tile = tb + lane;
-            const bool live = tile < thi && tile_live<R>(P, uc, tile);
+            const bool live = tile >= spec_end && tile < thi && tile_live<R>(P, uc, tile);
             uint32_t   bits = __ballot_sync(0xffffffffu, live);
             while (bits && ok) {
                 const int i = __ffs(bits) - 1;
@@ -502,70 +580,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
                     append_store<KV_TYPE, D>(P, app_row, lane, kbase, vbase, app_k, app_v);
                     app_tile = -1;
                 }
-                ok = acquire();
-                if (!ok) {
-                    break;
-                }
-                uint8_t *sK = smem + Cfg::kOffStages + stage * Cfg::kStageBytes;
-                uint8_t *sV = sK + Cfg::kTile;
-                uint8_t *sM = sK + 2 * Cfg::kTile;
-                if constexpr (kQ8) {
-                    // Rows are contiguous 34-B blocks; a tile starts at any even
-                    // address.  Copy from the 16-B boundary below it (inside the
-                    // tensor: its base is 16-B aligned) and let the converters
-                    // index from the lead; the last <16 bytes go by plain copies.
-                    const int      j0     = ti * kDecBN;
-                    const int      nrows  = min(kDecBN, o.n_kv - j0);
-                    const uint32_t bytes  = (uint32_t) nrows * Cfg::kRowBytes;
-                    const char    *kg     = kbase + (int64_t) j0 * Cfg::kRowBytes;
-                    const char    *vg     = vbase + (int64_t) j0 * Cfg::kRowBytes;
-                    const uint32_t lead_k = (uint32_t) (reinterpret_cast<uintptr_t>(kg) & 15u);
-                    const uint32_t lead_v = (uint32_t) (reinterpret_cast<uintptr_t>(vg) & 15u);
-                    const uint32_t bulk_k = (lead_k + bytes) & ~15u;
-                    const uint32_t bulk_v = (lead_v + bytes) & ~15u;
-                    if ((uint32_t) lane < lead_k + bytes - bulk_k) {
-                        sK[bulk_k + lane] = (uint8_t) kg[(int) (bulk_k + lane) - (int) lead_k];
-                    }
-                    if ((uint32_t) lane < lead_v + bytes - bulk_v) {
-                        sV[bulk_v + lane] = (uint8_t) vg[(int) (bulk_v + lane) - (int) lead_v];
-                    }
-                    const uint32_t mbytes = stage_mask(ti, sM);
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (mbytes && lane < n_ms) {
-                        bulk_load(sM + lane * kDecBN * 2, my_mr + ti * kDecBN, kDecBN * 2, &full_bar[stage]);
-                    }
-                    if (lane == 0) {
-                        meta[stage] = make_int4(nrows, ti, kMetaData, (int) (lead_k | (lead_v << 8)));
-                        mbar_arrive_expect_tx(&full_bar[stage], bulk_k + bulk_v + mbytes);
-                        if (bulk_k) {
-                            bulk_load(sK, kg - lead_k, bulk_k, &full_bar[stage]);
-                        }
-                        if (bulk_v) {
-                            bulk_load(sV, vg - lead_v, bulk_v, &full_bar[stage]);
-                        }
-                    }
-                } else {
-                    const uint32_t mbytes = stage_mask(ti, sM);
-                    if (lane == 0) {
-                        meta[stage] = make_int4(0, ti, kMetaData, 0);
-                        mbar_arrive_expect_tx(&full_bar[stage], (uint32_t) (2 * Cfg::kTile) + mbytes);
-#pragma unroll
-                        for (int h = 0; h < D / 64; ++h) {
-                            tma_load_4d(sK + h * kDecBN * 128, &kmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
-                                        &full_bar[stage]);
-                            tma_load_4d(sV + h * kDecBN * 128, &vmap, 64 * h, ti * kDecBN, uc.hk, uc.bk,
-                                        &full_bar[stage]);
-                        }
-                    }
-                    __syncwarp();
-                    if (mbytes && lane < n_ms) {
-                        bulk_load(sM + lane * kDecBN * 2, my_mr + ti * kDecBN, kDecBN * 2, &full_bar[stage]);
-                    }
-                }
-                pend[stage] = (int) phase;
-                __syncwarp();
-                advance();
+                issue(ti);
             }
         }
         if (app_tile >= 0) {  // the row's tile is dead for this unit: no read to order
