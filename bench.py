@@ -115,7 +115,7 @@ class ClockSampler:
 
 
 # -------------------------------------------------------------------------
-def cpu_baseline(budget_s=12.0, threads=None):
+def cpu_baseline(budget_s=12.0, threads=None, half=False):
     """The reference operator's CPU arithmetic (oracle, ggml-cpu mode) on a
     bounded sample of the same workload: whole layers of config 2."""
     import numpy as np
@@ -137,7 +137,11 @@ def cpu_baseline(budget_s=12.0, threads=None):
         if dt >= budget_s or n >= 5000:
             break
     gbs = n * algo_bytes_per_op() / dt / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+    hw2 = None
+    if threads > 1 and not half:
+        hw2 = cpu_baseline(budget_s=budget_s / 2, threads=max(1, threads // 2), half=True)
+        hw2 = {"value": hw2["value"], "cores": hw2["cores"]}
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "hw2": hw2,
             "sample": f"{n} layer(s) of the config-2 decode op (16 sets x 8192 keys, F16 KV) in {dt:.1f} s; "
                       f"oracle/fa_oracle.c ggml-cpu arithmetic, OpenMP"}
 
@@ -387,7 +391,7 @@ def run_ours(args):
 
     if rank == 0 and not args.no_extras:
         out["extras"] = extras(device, stream, args)
-        out["extras"]["dense"] = dense_extras(device, stream)
+        out["extras"]["dense"] = dense_extras(device, stream, cpu=not args.no_cpu_baseline)
         out["extras"]["config2_sweep"] = decode_sweep(device, stream)
     if world > 1 and not args.no_extras:
         sharded = sharded_dit(device, stream, world, rank)  # collective: every rank
@@ -455,13 +459,92 @@ def extras(device, stream, args):
             s1.record(stream)
             torch.cuda.synchronize()
             us = s0.elapsed_time(s1) * 1e3 / (10 * reps)
-            res[key] = {"us_per_op": round(us, 2), "gbs": round(b1 / (us / 1e6) / 1e9, 1),
+            gbs = b1 / (us / 1e6) / 1e9
+            res[key] = {"us_per_op": round(us, 2), "gbs": round(gbs, 1),
+                        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                     "frac": round(gbs / peak, 4),
+                                     "traffic": read_traffic("fa_decode_kernel_f16_config1"),
+                                     "algo_bytes_per_launch": b1},
                         "note": "64 distinct ops back to back in one CUDA graph (8.4 MB each)" +
                                 ("; mask by rule" if rule else "")}
+            if not rule:
+                res[key]["e2e"] = config1_e2e(ops, stream, b1)
             del graph, ops
+        if not getattr(args, "no_cpu_baseline", False):
+            res["config1_single_op"]["cpu_baseline"] = config1_cpu_baseline()
         res["config1_append"] = append_step(device, stream)
         res["dit6000_prologue"] = dit_prologue(device, stream)
     return res
+
+
+def config1_e2e(ops, stream, nbytes, iters=5):
+    """Config 1 through the C ABI with host buffers: per op the pinned H2D of
+    Q and the mask, the call, the D2H of the output (64 ops per round, copies
+    on their own streams as a serving loop issues them)."""
+    import torch
+
+    up, down = torch.cuda.Stream(device=stream.device), torch.cuda.Stream(device=stream.device)
+    qh = [torch.empty_like(op.q, device="cpu").pin_memory() for op in ops]
+    mh = [torch.empty_like(op.mask, device="cpu").pin_memory() for op in ops]
+    oh = [torch.empty_like(op.out, device="cpu").pin_memory() for op in ops]
+    ev_in = [torch.cuda.Event() for _ in ops]
+    ev_ran = [torch.cuda.Event() for _ in ops]
+
+    def rnd():
+        with torch.cuda.stream(up):
+            for i, op in enumerate(ops):
+                op.q.copy_(qh[i], non_blocking=True)
+                op.mask.copy_(mh[i], non_blocking=True)
+                ev_in[i].record(up)
+        for i, op in enumerate(ops):
+            stream.wait_event(ev_in[i])
+            op(stream=stream)
+            ev_ran[i].record(stream)
+        with torch.cuda.stream(down):
+            for i, op in enumerate(ops):
+                down.wait_event(ev_ran[i])
+                oh[i].copy_(op.out, non_blocking=True)
+
+    rnd()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    up.wait_event(e0)
+    for _ in range(iters):
+        rnd()
+        torch.cuda.synchronize()  # rounds do not overlap: every buffer is reused
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (iters * len(ops))
+    h2d = ops[0].q.numel() * 4 + ops[0].mask.numel() * 2
+    return {"us_per_op": round(us, 2), "gbs": round(nbytes / (us / 1e6) / 1e9, 1), "h2d_bytes_per_op": int(h2d),
+            "d2h_bytes_per_op": int(ops[0].out.numel() * 4),
+            "how": "pinned H2D of Q + mask, C-ABI call, D2H of the output per op; copies on their own streams"}
+
+
+def config1_cpu_baseline(budget_s=2.0):
+    """The config-1 op on the host cores (oracle, ggml-cpu arithmetic), at nproc
+    and at the reference's default of hw/2 threads (src/backend.h:28-31)."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(42 + 1000)
+    q = rng.standard_normal((1, 16, 1, D), dtype=np.float32)
+    k = rng.standard_normal((1, 8, 2048, D), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((1, 8, 2048, D), dtype=np.float32).astype(np.float16)
+    m = np.zeros((1, 1, 1, 2048), np.float16)
+    out = {}
+    for label, th in (("nproc", os.cpu_count()), ("hw2", max(1, (os.cpu_count() or 2) // 2))):
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.flash_attn_ext(q, k, v, m, scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=th)
+            n += 1
+        dt = time.perf_counter() - t0
+        out[label] = {"us_per_op": round(dt / n * 1e6, 1), "gbs": round(n * 8_409_088 / dt / 1e9, 2), "cores": th}
+    return {"value": out["nproc"]["gbs"], "unit": "GB/s", "cores": out["nproc"]["cores"], "kind": "port",
+            "us_per_op": out["nproc"]["us_per_op"], "hw2": out["hw2"],
+            "sample": "the config-1 op repeated for ~2 s per thread count; oracle/fa_oracle.c ggml-cpu arithmetic"}
 
 
 def append_step(device, stream, reps=64, kv_len=2048):
@@ -687,7 +770,15 @@ DENSE_WORKLOADS = {
     "dit6000": (2, 16, 16, 6000, 6000, None, None),
     "dit6000_window128": (2, 16, 16, 6000, 6000, "window", 128),
     "cross6000": (2, 16, 16, 6000, 512, "padding", 461),
+    # the real DiT has 8 K/V heads (GQA-2) and S = T / patch_size: S = 1085 in
+    # the reference's logs, 750 / 3000 for 30 s / 120 s of audio
+    "dit1085_gqa8": (2, 16, 8, 1085, 1085, None, None),
+    "dit750": (2, 16, 16, 750, 750, None, None),
+    "dit3000": (2, 16, 16, 3000, 3000, None, None),
+    "dit6000_gqa8": (2, 16, 8, 6000, 6000, None, None),
 }
+# workloads whose CPU baseline (oracle on sampled query rows) is timed too
+DENSE_CPU_SAMPLED = ("prefill4096", "dit6000", "cross6000")
 
 
 def dense_pairs(S_q, S_kv, kind, extra):
@@ -763,15 +854,24 @@ def time_dense(device, stream, name, iters=10, warmup=3, rule=False):
             "path": "dense tcgen05" if path == 2 else "decode"}
 
 
-def dense_extras(device, stream):
-    peak = 1635.6
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
-        peak = float(json.load(open(p))["bf16_tflops"])
+def dense_extras(device, stream, cpu=True):
+    """BASELINE configs 3 and 4: each dense workload timed alone (CUDA graph,
+    10 replays), with its roofline (tensor bound, measured bf16 burst peak;
+    DRAM traffic of one launch from profiles/ncu_traffic.json when captured),
+    the same op through the C ABI with host buffers (e2e), and for the
+    headline shapes the CPU port on sampled query rows."""
+    peak = read_tflops_peak()
     res = {"peak_tflops": peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; kernel timed alone)"}
     for name in DENSE_WORKLOADS:
         r = time_dense(device, stream, name)
         r["frac_of_peak"] = round(r["tflops"] / peak, 4)
+        r["roofline"] = {"bound": "tensor", "achieved": r["tflops"], "peak": peak, "unit": "TFLOP/s",
+                         "frac": r["frac_of_peak"], "traffic": read_traffic(f"fa_dense_kernel_{name}"),
+                         "peak_source": "measured bf16_tflops (burst)", "algo_flop_per_launch": int(r["gflop"] * 1e9)}
+        if name in ("prefill4096", "dit6000", "cross6000", "prefill1024", "dit1500"):
+            r["e2e"] = dense_e2e(device, stream, name)
+        if cpu and name in DENSE_CPU_SAMPLED:
+            r["cpu_baseline"] = dense_cpu_baseline(name)
         res[name] = r
     # the masked workloads again with the mask given by rule (no mask tensor,
     # no classification pass)
@@ -781,6 +881,79 @@ def dense_extras(device, stream):
             r["frac_of_peak"] = round(r["tflops"] / peak, 4)
             res[name + "_rule"] = r
     return res
+
+
+def dense_e2e(device, stream, name, iters=5):
+    """The dense op through the C ABI with host buffers: per call the pinned
+    H2D of Q, K, V (and mask), acefa_flash_attn_ext, the D2H of the output, in
+    stream order (the copies cannot overlap a single op's own attention)."""
+    import torch
+
+    op, flops = build_dense(device, name)
+    host = {k: torch.empty_like(t, device="cpu").pin_memory() for k, t in
+            (("q", op.q), ("k", op.k), ("v", op.v), ("m", op.mask)) if t is not None}
+    for k, t in (("q", op.q), ("k", op.k), ("v", op.v), ("m", op.mask)):
+        if t is not None:
+            host[k].copy_(t)
+    out_h = torch.empty_like(op.out, device="cpu").pin_memory()
+    dev = {"q": op.q, "k": op.k, "v": op.v, "m": op.mask}
+
+    def step():
+        for k, h in host.items():
+            dev[k].copy_(h, non_blocking=True)
+        op(stream=stream)
+        out_h.copy_(op.out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    h2d = sum(h.numel() * h.element_size() for h in host.values())
+    del op
+    return {"ms": round(ms, 3), "tflops": round(flops / (ms / 1e3) / 1e12, 1), "h2d_bytes_per_call": int(h2d),
+            "d2h_bytes_per_call": int(out_h.numel() * 4), "how": "pinned H2D of Q/K/V/mask, C-ABI call, D2H of "
+            "the output, stream-ordered; CUDA events"}
+
+
+def dense_cpu_baseline(name, rows_per=24, budget_s=1.5):
+    """The oracle (ggml-cpu arithmetic) on `rows_per` sampled query rows of the
+    workload (all heads and batches, the rows' full key ranges), at nproc and
+    at the reference's default of hw/2 threads (src/backend.h:28-31)."""
+    import numpy as np
+
+    import oracle
+
+    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name]
+    rng = np.random.default_rng(SEED + 3)
+    rows = np.sort(rng.choice(S_q, rows_per, replace=False))
+    q = rng.standard_normal((B, Hq, rows_per, D), dtype=np.float32)
+    k = rng.standard_normal((B, Hkv, S_kv, D), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, S_kv, D), dtype=np.float32).astype(np.float16)
+    m, vis = None, np.full((rows_per,), S_kv)
+    if kind is not None:
+        j = np.arange(S_kv)[None, :]
+        ri = rows[:, None] + (S_kv - S_q)
+        ok = {"causal": j <= ri, "window": np.abs(ri - j) <= (extra or 0),
+              "padding": np.broadcast_to(j < (extra or 0), (rows_per, S_kv))}[kind]
+        vis = ok.sum(1)
+        m = np.where(ok, 0.0, -np.inf).astype(np.float16).reshape(1, 1, rows_per, S_kv)
+    flops = 4 * D * Hq * B * int(vis.sum())
+    out = {}
+    for label, th in (("nproc", os.cpu_count()), ("hw2", max(1, (os.cpu_count() or 2) // 2))):
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.flash_attn_ext(q, k, v, m, scale=D ** -0.5, mode=oracle.MODE_GGML_CPU, nthreads=th)
+            n += 1
+        out[label] = {"tflops": round(n * flops / (time.perf_counter() - t0) / 1e12, 5), "cores": th}
+    return {"value": out["nproc"]["tflops"], "unit": "TFLOP/s", "cores": out["nproc"]["cores"], "kind": "port",
+            "hw2": out["hw2"], "sample": f"{rows_per} sampled query rows x {Hq} heads x B={B} over their visible keys; "
+                                           "oracle/fa_oracle.c ggml-cpu arithmetic, OpenMP"}
 
 
 def sharded_dit(device, stream, world, rank, iters=10, warmup=3):
@@ -1083,6 +1256,30 @@ def run_dense_workload(args):
     if args.workload == "config5":
         emit({"workload": args.workload, **config5(device, stream, gen=args.c5_gen)})
         return 0
+    if args.workload == "config1":
+        # 64 distinct Qwen3-0.6B decode ops back to back
+        # (also the ncu profiling case of the op)
+        import acefa
+
+        g = torch.Generator(device=device).manual_seed(42 + 1000)
+        ops = []
+        for _ in range(64):
+            q = torch.randn(1, 16, 1, D, device=device, generator=g)
+            k = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
+            v = torch.randn(1, 8, 2048, D, device=device, generator=g, dtype=torch.float16)
+            ops.append(acefa.Op(q, k, v, mask=torch.zeros(1, 1, 1, 2048, device=device, dtype=torch.float16),
+                                scale=D ** -0.5))
+        graph = time_graph(ops, args.steps, args.warmup, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (args.steps * len(ops))
+        emit({"workload": "config1", "us_per_op": round(us, 2), "gbs": round(8_409_088 / (us / 1e6) / 1e9, 1)})
+        return 0
     r = time_dense(device, stream, args.workload, iters=args.steps, warmup=args.warmup, rule=args.mask_rule)
     emit({"workload": args.workload, "mask_rule": bool(args.mask_rule), **r})
     return 0
@@ -1122,7 +1319,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (36 = the headline stack)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
     ap.add_argument("--workload", default="decode4b",
-                    help="decode4b (headline), config5, dit6000_prologue, or one dense op: " + ", ".join(DENSE_WORKLOADS))
+                    help="decode4b (headline), config1, config5, dit6000_prologue, or one dense op: " + ", ".join(DENSE_WORKLOADS))
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 end-to-end workload extra")
     ap.add_argument("--c5-gen", type=int, default=C5_GEN, help="config-5 decode steps (2000 = the BASELINE workload)")
     ap.add_argument("--mask-rule", action="store_true",
