@@ -257,15 +257,15 @@ DecodePlan plan_decode(const OpDesc &o, bool prologue) {
 }
 
 // ------------------------------------------------------------------ dense plan
-// The dense tcgen05 kernel serves F16 K/V with D = 128 when a K/V head has
-// more than 64 rows of queries (G * n_q) -- prefill, encoders, DiT.  A function
-// of shapes only, so the choice (and the workspace) is fixed before capture.
+// The dense tcgen05 kernel serves D = 128 (F16, BF16 or Q8_0 K/V) when a K/V
+// head has more than 64 rows of queries (G * n_q) -- prefill, encoders, DiT.  A
+// function of shapes only, so the choice (and the workspace) is fixed before
+// capture.
 bool use_dense(const OpDesc &o) {
     const int64_t rows = (int64_t) o.G * o.n_q;
     const int64_t n_kt = ((int64_t) o.n_kv + kDenseBN - 1) / kDenseBN;
     const int64_t n_pairs = ((rows + kDenseBM - 1) / kDenseBM + 1) / 2;
-    return o.kv_type == ACEFA_TYPE_F16 && o.D == 128 && rows > 64 && n_kt <= kDenseMaxKT &&
-           n_pairs * o.Hkv * o.B < (1ll << 31);
+    return o.D == 128 && rows > 64 && n_kt <= kDenseMaxKT && n_pairs * o.Hkv * o.B < (1ll << 31);
 }
 
 struct DensePlan {
@@ -509,8 +509,9 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         L.p.dev_err       = di->err_ptr;
         L.p.wait_limit_ns = wait_limit_ns();
         L.classify        = dp.classify;
-        if ((rc = encode_kv_map(&L.kmap, k, c.op.D, kDenseBN)) != ACEFA_OK ||
-            (rc = encode_kv_map(&L.vmap, v, c.op.D, kDenseBN)) != ACEFA_OK) {
+        if (c.op.kv_type != ACEFA_TYPE_Q8_0 &&  // Q8_0 rows are staged by bulk copies
+            ((rc = encode_kv_map(&L.kmap, k, c.op.D, kDenseBN)) != ACEFA_OK ||
+             (rc = encode_kv_map(&L.vmap, v, c.op.D, kDenseBN)) != ACEFA_OK)) {
             return rc;
         }
         int launches = 0;

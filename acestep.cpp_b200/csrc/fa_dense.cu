@@ -26,6 +26,7 @@
 // Every wait is bounded (error word + drain on expiry).
 #include "fa_internal.h"
 #include "ptx.cuh"
+#include "q8.cuh"
 #include "rope_norm.cuh"
 
 namespace acefa {
@@ -54,6 +55,33 @@ static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= 384 * 168, "register sp
 
 
 constexpr uint16_t kHalfNegInf = 0xFC00u;
+
+// K/V element type of an instance.  F16 tiles go from TMA straight to the
+// tensor core.  BF16 tiles land by TMA and warps 2-3 convert them in place to
+// F16 (exact for values inside F16's range, as ggml's CUDA backend converts
+// BF16 K/V to F16 for its tensor-core attention).  Q8_0 rows are staged raw, in
+// half tiles of 64 keys, by bulk copies, and warps 2-3 dequantise them into the
+// F16 tiles the MMAs read (f16(d * q), one rounding).
+constexpr int kKvF16 = 0, kKvBF16 = 1, kKvQ8 = 2;
+constexpr int kConvWarps = 2;                                       // warps 2 and 3
+constexpr int kRawRows   = kDenseBN / 2;                            // Q8_0 keys per staged half tile
+constexpr int kRawRowBytes = 136;                                   // D = 128: 4 blocks of 34 B
+constexpr int kRawBytes  = (kRawRows * kRawRowBytes + 16 + 15) / 16 * 16;  // + up to 15 lead bytes
+constexpr int kRawStages = 3;
+constexpr int kOffExt     = (kOffMisc + 16 + 15) / 16 * 16;
+// ready[kRing] (BF16: converted), raw_full / raw_empty [kRawStages] (Q8_0)
+constexpr int kNumExtBars = kRing + 2 * kRawStages;
+constexpr int kOffRawMeta = kOffExt + kNumExtBars * 8;             // int4 [kRawStages]
+constexpr int kOffRaw     = kOffRawMeta + kRawStages * 16;
+static_assert(kOffRaw % 16 == 0, "bulk copies need 16-B aligned staging");
+template <int KVT>
+constexpr int dense_smem_bytes() {
+    // (+ 16: the converters' last 4-B loads of a staged row may reach 3 bytes
+    // past the staging ring; + 1024: alignment of the dynamic base)
+    return KVT == kKvF16 ? kSmemBytes
+                         : (KVT == kKvBF16 ? kOffRawMeta + 1024 : kOffRaw + kRawStages * kRawBytes + 16 + 1024);
+}
+static_assert(dense_smem_bytes<kKvQ8>() <= 232448, "Q8_0 staging exceeds the 227 KB per CTA");
 
 
 __device__ __forceinline__ void row_to_query(int gr, int G, int hk, int &iq, int &hq) {
@@ -165,6 +193,44 @@ __device__ __forceinline__ uint32_t range_bits(int a, int b) {
         return 0u;
     }
     return (b >= 32 ? ~0u : ((1u << b) - 1u)) & ~((1u << a) - 1u);
+}
+
+// ---------------------------------------------------------------------------
+// K/V conversion into the F16 tiles the MMAs read (warps 2-3).
+
+// bf16x2 -> f16x2 (exact for values inside F16's range)
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
+    return cvt_f16x2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// kRawRows staged Q8_0 rows (136 B each, any 2-B alignment) -> rows
+// [row0, row0 + kRawRows) of a 128-key F16 tile in the 128-B swizzled layout of
+// the TMA boxes {64 dims, 128 keys}.  A warp iteration converts 8 rows, lane =
+// (row, 32-value block).  Rows at or past `nvalid` become zeros.
+__device__ __forceinline__ void q8_rows_to_f16(uint32_t src, uint32_t tile, int row0, int nvalid, int cw, int lane) {
+    const int blk = lane & 3;
+    const int rr  = lane >> 2;
+#pragma unroll 1
+    for (int it = cw; it < kRawRows / 8; it += kConvWarps) {
+        const int j  = it * 8 + rr;
+        uint32_t  q[8];
+        const uint16_t dbits = q8_load_run<8>(src + (uint32_t) (j * kRawRowBytes + 34 * blk), 0, q);
+        const __half2  d2    = __half2half2(__ushort_as_half(j < nvalid ? dbits : (uint16_t) 0));
+        uint32_t       o[16];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            o[2 * k]     = i8x2_scaled(q[k], 0x4140u, d2);
+            o[2 * k + 1] = i8x2_scaled(q[k], 0x4342u, d2);
+        }
+        const int row = row0 + j;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int cc = 4 * blk + m;  // 16-B chunk (8 dims) of the row
+            const uint32_t a =
+                tile + (uint32_t) ((cc >> 3) * (kDenseBN * 128) + row * 128 + (((cc & 7) ^ (row & 7)) << 4));
+            sts128(a, o[4 * m], o[4 * m + 1], o[4 * m + 2], o[4 * m + 3]);
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -377,8 +443,9 @@ __device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4],
 }
 
 // ---------------------------------------------------------------------------
-// PRO: the instance that applies the QK-norm + RoPE prologue to Q rows.
-template <bool PRO>
+// PRO: the instance that applies the QK-norm + RoPE prologue to Q rows; KVT:
+// the K/V element type (kKvF16 / kKvBF16 / kKvQ8).
+template <bool PRO, int KVT>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap) {
@@ -392,6 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t     *p_ready = s_ready + 2;
     uint64_t     *o_done  = p_ready + 2;
     uint64_t     *fin     = o_done + 2;
+    uint64_t     *ready     = reinterpret_cast<uint64_t *>(smem + kOffExt);  // [kRing] BF16 tile converted
+    uint64_t     *raw_full  = ready + kRing;                                  // [kRawStages] Q8_0 half tile staged
+    uint64_t     *raw_empty = raw_full + kRawStages;                         // [kRawStages] staging free again
+    int4         *raw_meta  = reinterpret_cast<int4 *>(smem + kOffRawMeta);  // (rows, lead bytes) per staging
     uint8_t      *s_cls   = smem + kOffCls;  // [2][kDenseMaxKT]
     uint32_t     *s_tmem  = reinterpret_cast<uint32_t *>(smem + kOffMisc);
     volatile int *abort_f = reinterpret_cast<volatile int *>(smem + kOffMisc + 4);
@@ -425,8 +496,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRing; ++i) {
-            mbar_init(&full[i], 1);
+            mbar_init(&full[i], KVT == kKvQ8 ? kConvWarps : 1);
             mbar_init(&empty[i], 1);
+            if constexpr (KVT == kKvBF16) {
+                mbar_init(&ready[i], kConvWarps);
+            }
+        }
+        if constexpr (KVT == kKvQ8) {
+            for (int i = 0; i < kRawStages; ++i) {
+                mbar_init(&raw_full[i], 1);
+                mbar_init(&raw_empty[i], kConvWarps);
+            }
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_ready[i], 1);
@@ -437,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_f = 0;
         fence_barrier_init();
     }
-    if (warp == 0 && lane == 0) {
+    if (KVT != kKvQ8 && warp == 0 && lane == 0) {
         prefetch_tensormap(&kmap);
         prefetch_tensormap(&vmap);
     }
@@ -615,7 +695,75 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp < 4) {
       setmaxnreg_dec<kRegsControl>();
-      if (warp == 0) {
+      if (KVT == kKvQ8 && warp == 0) {
+        // ======================= Q8_0 staging producer ========================
+        // Each live key tile's K then V rows, in halves of 64 keys, by bulk
+        // copies into the staging ring (from the 16-B boundary below each half,
+        // inside the tensor; the ragged last bytes by plain copies).
+        const char *kb    = o.k + (int64_t) hk * o.k_nb2 + (int64_t) bk * o.k_nb3;
+        const char *vb    = o.v + (int64_t) hk * o.v_nb2 + (int64_t) bk * o.v_nb3;
+        int         rs    = 0;
+        uint32_t    rph   = 0;
+        int         rpend[kRawStages];
+        bool        ok    = true;
+        for (int i = 0; i < kRawStages; ++i) {
+            rpend[i] = -1;
+        }
+        for (int j = 0; j < P.n_kt && ok; ++j) {
+            if (!any_live(j)) {
+                continue;
+            }
+            for (int h = 0; h < 2 && ok; ++h) {
+                for (int q = 0; q < 2 && ok; ++q) {
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&raw_empty[rs], rph ^ 1u, abort_f, P.dev_err,
+                                                                   DEVERR_TIMEOUT_EMPTY, P.wait_limit_ns));
+                    if (!ok) {
+                        break;
+                    }
+                    const int      row0  = j * kDenseBN + q * kRawRows;
+                    const int      nrows = max(0, min(kRawRows, o.n_kv - row0));
+                    const char    *src   = (h ? vb : kb) + (int64_t) row0 * kRawRowBytes;
+                    const uint32_t lead  = (uint32_t) (reinterpret_cast<uintptr_t>(src) & 15u);
+                    const uint32_t bytes = (uint32_t) nrows * kRawRowBytes;
+                    const uint32_t bulk  = (lead + bytes) & ~15u;
+                    uint8_t       *dst   = smem + kOffRaw + rs * kRawBytes;
+                    if (nrows > 0 && (uint32_t) lane < lead + bytes - bulk && bulk + (uint32_t) lane >= lead) {
+                        dst[bulk + lane] = (uint8_t) src[(int) (bulk + lane) - (int) lead];
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        raw_meta[rs] = make_int4(nrows, (int) lead, 0, 0);
+                        mbar_arrive_expect_tx(&raw_full[rs], bulk);
+                        if (bulk) {
+                            bulk_load(dst, src - lead, bulk, &raw_full[rs]);
+                        }
+                    }
+                    rpend[rs] = (int) rph;
+                    __syncwarp();
+                    if (++rs == kRawStages) {
+                        rs = 0;
+                        rph ^= 1u;
+                    }
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            // let the copies in flight land before the CTA exits
+            for (int i = 0; i < kRawStages; ++i) {
+                if (rpend[i] < 0) {
+                    continue;
+                }
+                const uint64_t ts = globaltimer_ns();
+                while (!mbar_try_wait(&raw_full[i], (uint32_t) rpend[i])) {
+                    if (globaltimer_ns() - ts > P.wait_limit_ns) {
+                        atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_DRAIN);
+                        break;
+                    }
+                }
+            }
+        }
+      } else if (warp == 0) {
         // ============================ TMA producer ============================
         if (lane == 0) {
             produce(P.n_kt);
@@ -651,9 +799,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t       p_ph0 = 0, p_ph1 = 0, has_o0 = 0, has_o1 = 0;
             bool           ok    = true;
 
+            // a ring slot is ready once its tile landed (F16) or was converted
+            // to F16 (BF16: `ready`; Q8_0: the converters arrive on `full`)
             auto wait_full = [&](int seq) -> bool {
-                return mbar_wait_bounded(&full[seq % kRing], (uint32_t) ((seq / kRing) & 1), abort_f, P.dev_err,
-                                         DEVERR_TIMEOUT_FULL, P.wait_limit_ns);
+                uint64_t *bar = KVT == kKvBF16 ? &ready[seq % kRing] : &full[seq % kRing];
+                return mbar_wait_bounded(bar, (uint32_t) ((seq / kRing) & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_FULL,
+                                         P.wait_limit_ns);
             };
             auto issue_s = [&](uint32_t tS, uint64_t qd, int slot) {
                 const uint64_t kd = kd0 + (uint64_t) (slot * (kTileBytes >> 4));
@@ -769,6 +920,80 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
             }
+        }
+      } else if (KVT != kKvF16) {
+        // ============================ converters (warps 2-3) ===================
+        // Ring slots in the producer's order: each live key tile's K, then V.
+        const int cw  = warp - 2;
+        const int ct  = cw * 32 + lane;
+        bool      ok  = true;
+        int       use = 0;
+        int       rs  = 0;  // Q8_0 staging position
+        uint32_t  rph = 0;
+        for (int j = 0; j < P.n_kt && ok; ++j) {
+            if (!any_live(j)) {
+                continue;
+            }
+            for (int h = 0; h < 2 && ok; ++h) {
+                const int seq  = 2 * use + h;
+                const int buf  = seq % kRing;
+                const int u    = seq / kRing;
+                uint8_t  *tile = smem + kOffRing + buf * kTileBytes;
+                if constexpr (KVT == kKvBF16) {
+                    // the TMA-landed bf16 tile, converted in place, 16 B at a time
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[buf], (uint32_t) (u & 1), abort_f, P.dev_err,
+                                                                   DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
+                    if (!ok) {
+                        break;
+                    }
+#pragma unroll 4
+                    for (int x = ct; x < kTileBytes / 16; x += 32 * kConvWarps) {
+                        uint4 w = *reinterpret_cast<const uint4 *>(tile + 16 * x);
+                        w.x     = bf16x2_to_f16x2(w.x);
+                        w.y     = bf16x2_to_f16x2(w.y);
+                        w.z     = bf16x2_to_f16x2(w.z);
+                        w.w     = bf16x2_to_f16x2(w.w);
+                        *reinterpret_cast<uint4 *>(tile + 16 * x) = w;
+                    }
+                    fence_proxy_async_smem();  // read next by the tensor core (async proxy)
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&ready[buf]);
+                    }
+                } else {
+                    // the slot's previous tile is no longer read by the MMAs;
+                    // fill it from two staged halves
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&empty[buf], (uint32_t) ((u & 1) ^ 1), abort_f,
+                                                                   P.dev_err, DEVERR_TIMEOUT_EMPTY, P.wait_limit_ns));
+                    for (int q = 0; q < 2 && ok; ++q) {
+                        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&raw_full[rs], rph, abort_f, P.dev_err,
+                                                                       DEVERR_TIMEOUT_FULL, P.wait_limit_ns));
+                        if (!ok) {
+                            break;
+                        }
+                        const int4 md = raw_meta[rs];
+                        q8_rows_to_f16(smem_u32(smem + kOffRaw + rs * kRawBytes) + (uint32_t) md.y, smem_u32(tile),
+                                       q * kRawRows, md.x, cw, lane);
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&raw_empty[rs]);
+                        }
+                        if (++rs == kRawStages) {
+                            rs = 0;
+                            rph ^= 1u;
+                        }
+                    }
+                    if (!ok) {
+                        break;
+                    }
+                    fence_proxy_async_smem();  // read next by the tensor core (async proxy)
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&full[buf]);
+                    }
+                }
+            }
+            ++use;
         }
       }
     } else {
@@ -1177,16 +1402,35 @@ __global__ void __launch_bounds__(kDenseBM) fa_dense_combine(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------
+namespace {
+
+template <int KVT>
+cudaError_t configure_dense() {
+    for (auto k : {fa_dense_kernel<false, KVT>, fa_dense_kernel<true, KVT>}) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dense_smem_bytes<KVT>());
+        if (e != cudaSuccess) {
+            return e;
+        }
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
 cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     static thread_local int configured_dev = -1;
     int                     dev            = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
-        for (auto k : {fa_dense_kernel<false>, fa_dense_kernel<true>}) {
-            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-            if (e != cudaSuccess) {
-                return e;
-            }
+        cudaError_t e = configure_dense<kKvF16>();
+        if (e == cudaSuccess) {
+            e = configure_dense<kKvBF16>();
+        }
+        if (e == cudaSuccess) {
+            e = configure_dense<kKvQ8>();
+        }
+        if (e != cudaSuccess) {
+            return e;
         }
         configured_dev = dev;
     }
@@ -1207,15 +1451,21 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
         }
         ++n;
     }
+    const int   kvt = L.p.op.kv_type == ACEFA_TYPE_Q8_0 ? kKvQ8 : (L.p.op.kv_type == ACEFA_TYPE_BF16 ? kKvBF16 : kKvF16);
+    const bool  pro = L.p.op.qp.on;
+    auto        kern = kvt == kKvQ8    ? (pro ? fa_dense_kernel<true, kKvQ8> : fa_dense_kernel<false, kKvQ8>)
+                       : kvt == kKvBF16 ? (pro ? fa_dense_kernel<true, kKvBF16> : fa_dense_kernel<false, kKvBF16>)
+                                        : (pro ? fa_dense_kernel<true, kKvF16> : fa_dense_kernel<false, kKvF16>);
+    const int   smem = kvt == kKvQ8 ? dense_smem_bytes<kKvQ8>()
+                                    : (kvt == kKvBF16 ? dense_smem_bytes<kKvBF16>() : dense_smem_bytes<kKvF16>());
     cudaLaunchConfig_t c = {};
     c.gridDim            = dim3((unsigned) (L.p.n_full + (int64_t) L.p.n_tail * L.p.n_split));
     c.blockDim           = dim3(kThreads);
-    c.dynamicSmemBytes   = kSmemBytes;
+    c.dynamicSmemBytes   = (size_t) smem;
     c.stream             = s;
     c.attrs              = attr;
     c.numAttrs           = 1;
-    cudaError_t e        = cudaLaunchKernelEx(&c, L.p.op.qp.on ? fa_dense_kernel<true> : fa_dense_kernel<false>, L.p,
-                                          L.kmap, L.vmap);
+    cudaError_t e        = cudaLaunchKernelEx(&c, kern, L.p, L.kmap, L.vmap);
     if (e != cudaSuccess) {
         return e;
     }

@@ -776,6 +776,10 @@ DENSE_WORKLOADS = {
     "dit750": (2, 16, 16, 750, 750, None, None),
     "dit3000": (2, 16, 16, 3000, 3000, None, None),
     "dit6000_gqa8": (2, 16, 8, 6000, 6000, None, None),
+    # BF16 inputs (config 4 names "BF16/F16 inputs") and the config-5 prompt
+    # prefill over a Q8_0 KV cache (one set: Q [128, 512, 32], K/V [128, 512, 8])
+    "dit6000_bf16": (2, 16, 16, 6000, 6000, None, None, "bf16"),
+    "prefill512_q8_0": (1, 32, 8, 512, 512, "causal", None, "q8_0"),
 }
 # workloads whose CPU baseline (oracle on sampled query rows) is timed too
 DENSE_CPU_SAMPLED = ("prefill4096", "dit6000", "cross6000")
@@ -800,11 +804,17 @@ def build_dense(device, name, seed=SEED + 3, rule=False):
 
     import acefa
 
-    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name]
+    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name][:7]
+    kv = DENSE_WORKLOADS[name][7] if len(DENSE_WORKLOADS[name]) > 7 else "f16"
     g = torch.Generator(device=device).manual_seed(seed)
     q = torch.randn(B, Hq, S_q, D, device=device, generator=g)
     k = torch.randn(B, Hkv, S_kv, D, device=device, generator=g, dtype=torch.float16)
     v = torch.randn(B, Hkv, S_kv, D, device=device, generator=g, dtype=torch.float16)
+    kv_type = None
+    if kv == "bf16":
+        k, v = k.bfloat16(), v.bfloat16()
+    elif kv == "q8_0":
+        k, v, kv_type = acefa.quantize_q8_0(k), acefa.quantize_q8_0(v), acefa.GGML_Q8_0
     mask = None
     if kind is not None:
         qi = torch.arange(S_q, device=device)[:, None]
@@ -820,9 +830,9 @@ def build_dense(device, name, seed=SEED + 3, rule=False):
         mg = {"causal": lambda: acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[S_kv - S_q] * B),
               "window": lambda: acefa.mask_gen(acefa.MASK_WINDOW, window=extra),
               "padding": lambda: acefa.mask_gen(acefa.MASK_PADDING, lens=[extra] * B)}[kind]()
-        op = acefa.Op(q, k, v, mask_gen=mg, scale=D ** -0.5)
+        op = acefa.Op(q, k, v, mask_gen=mg, kv_type=kv_type, scale=D ** -0.5)
     else:
-        op = acefa.Op(q, k, v, mask=mask, scale=D ** -0.5)
+        op = acefa.Op(q, k, v, mask=mask, kv_type=kv_type, scale=D ** -0.5)
     flops = 4 * D * dense_pairs(S_q, S_kv, kind, extra) * Hq * B
     return op, flops
 
@@ -876,7 +886,7 @@ def dense_extras(device, stream, cpu=True):
     # the masked workloads again with the mask given by rule (no mask tensor,
     # no classification pass)
     for name, wl in DENSE_WORKLOADS.items():
-        if wl[5] is not None:
+        if wl[5] is not None and len(wl) == 7:
             r = time_dense(device, stream, name, rule=True)
             r["frac_of_peak"] = round(r["tflops"] / peak, 4)
             res[name + "_rule"] = r
@@ -929,7 +939,7 @@ def dense_cpu_baseline(name, rows_per=24, budget_s=1.5):
 
     import oracle
 
-    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name]
+    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name][:7]
     rng = np.random.default_rng(SEED + 3)
     rows = np.sort(rng.choice(S_q, rows_per, replace=False))
     q = rng.standard_normal((B, Hq, rows_per, D), dtype=np.float32)

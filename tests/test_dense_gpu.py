@@ -28,10 +28,10 @@ def run_case(case, rows=None, **kw):
 def oracle_rows(case, rows, scale=None, max_bias=0.0, softcap=0.0):
     """Oracle on a subset of query rows (mask rows follow), full K/V."""
     scale = case.D ** -0.5 if scale is None else scale
-    kt = {"f16": oracle.GGML_F16}[case.kv]
+    kt = {"f16": oracle.GGML_F16, "bf16": oracle.GGML_BF16, "q8_0": oracle.GGML_Q8_0}[case.kv]
     q = case.q_cpu.numpy()[:, :, rows]
-    kc = case.k_cache_cpu.numpy()[case.s0:case.s0 + case.Bk, :, :case.n_kv]
-    vc = case.v_cache_cpu.numpy()[case.s0:case.s0 + case.Bk, :, :case.n_kv]
+    kc = case._np(case.k_cache_cpu)[case.s0:case.s0 + case.Bk, :, :case.n_kv]
+    vc = case._np(case.v_cache_cpu)[case.s0:case.s0 + case.Bk, :, :case.n_kv]
     m = None if case.mask_cpu is None else np.ascontiguousarray(case.mask_cpu.numpy()[:, :, rows])
     s = None if case.sinks_cpu is None else case.sinks_cpu.numpy()
     return oracle.flash_attn_ext(np.ascontiguousarray(q), kc, vc, m, s, scale=scale, max_bias=max_bias,
@@ -229,3 +229,55 @@ def test_binary_mask_rows_with_holes():
 
     c = Case(4901, B=2, Hq=8, Hkv=4, n_q=n_q, n_kv=n_kv, mask=mk, m_batch=1)
     assert_close(c.gpu(), c.oracle(), what="binary mask rows with holes")
+
+
+# ---------------------------------------------------------------------------
+# BF16 and Q8_0 K/V on the tcgen05 path: BF16 tiles converted to F16 in
+# shared memory, Q8_0 rows staged raw and dequantised (f16(d * q)) by warps
+# 2-3 before the MMAs read them.
+
+@pytest.mark.parametrize("kv", ["bf16", "q8_0"])
+@pytest.mark.parametrize("S,H,Hkv", [(300, 16, 16), (600, 16, 8)])
+def test_dense_bf16_q8_unmasked(kv, S, H, Hkv):
+    c = Case(42 + 1000 * 4 + S + 7, B=2, Hq=H, Hkv=Hkv, n_q=S, n_kv=S, kv=kv, mask=None)
+    run_case(c)
+
+
+@pytest.mark.parametrize("kv", ["bf16", "q8_0"])
+@pytest.mark.parametrize("n_q,n_kv", [(129, 130), (250, 127), (333, 1000), (512, 515)])
+def test_dense_bf16_q8_ragged_masked(kv, n_q, n_kv):
+    """Ragged key counts (half tiles of 64 keys partly or wholly past n_kv),
+    random masks with -inf and finite entries, GQA 2."""
+    c = Case(42 + n_q * 11 + n_kv, B=1, Hq=4, Hkv=2, n_q=n_q, n_kv=n_kv, kv=kv, mask="random")
+    run_case(c)
+
+
+@pytest.mark.parametrize("kv", ["bf16", "q8_0"])
+def test_dense_bf16_q8_causal_prefill_cache_view(kv):
+    """The reference's prefill over its KV cache: views [128, PAD(S,256), 8] of a
+    cache of max_seq rows at set 2, causal mask."""
+    S = 300
+    c = Case(42 + 3000 + S, B=1, Hq=16, Hkv=8, n_q=S, n_kv=512, kv=kv, max_seq=2560, s0=2,
+             mask=lambda m: causal_mask(m, S))
+    run_case(c)
+
+
+@pytest.mark.parametrize("kv", ["bf16", "q8_0"])
+def test_dense_bf16_q8_split_tail_units(kv):
+    """Unmasked node whose last-wave units are split over key ranges (the
+    combine kernel merges them)."""
+    c = Case(72, B=1, Hq=10, Hkv=10, n_q=4096, n_kv=4096, kv=kv, mask=None, sinks=True)
+    run_case(c, rows=[0, 1, 255, 256, 2048, 4095])
+
+
+def test_full_size_dit_bf16_sampled_rows():
+    """BASELINE config 4 with BF16 inputs: DiT self-attention S = 6000, B = 2,
+    16 x 128, and the cross-attention padding case."""
+    S = 6000
+    rng = np.random.default_rng(42 + 1000 * 4 + 5)
+    rows = np.unique(np.concatenate([np.sort(rng.choice(S, 40, replace=False)), [0, 127, 128, S - 1]]))
+    c = Case(42 + 1000 * 4 + 11, B=2, Hq=16, Hkv=16, n_q=S, n_kv=S, kv="bf16", mask=None)
+    run_case(c, rows=rows)
+    cx = Case(42 + 1000 * 4 + 13, B=2, Hq=16, Hkv=16, n_q=S, n_kv=512, kv="bf16", mask=padding_mask((461, 461)),
+              m_batch=2)
+    run_case(cx, rows=rows)
