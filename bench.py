@@ -1026,8 +1026,10 @@ def sharded_dit(device, stream, world, rank, iters=10, warmup=3):
 # window on even layers, src/dit.h:400) and cross-attention to 512 text tokens
 # (461 valid), B = 2 (CFG), 16 x 128 heads (src/dit-sampler.h:415).  Masks are
 # f16 tensors filled the way the reference fills them.  At N GPUs the 16 KV
-# sets split N ways (no collective) and the DiT heads split N ways with one
-# NCCL all-gather per node (strong scaling: the total work is fixed).
+# sets split N ways (no collective) and the DiT heads split N ways, each
+# rank's kernel storing its heads into every rank's output over NVLink, one
+# one-element NCCL all-reduce per node as completion barrier (strong scaling:
+# the total work is fixed).
 C5_LAYERS, C5_SETS, C5_PROMPT, C5_GEN, C5_MAXSEQ = 36, 16, 512, 2000, 2560
 C5_DIT_STEPS, C5_DIT_LAYERS, C5_DIT_S, C5_DIT_ENC, C5_DIT_VALID, C5_DIT_WIN = 8, 24, 6000, 512, 461, 128
 Q8_ROW = D // 32 * 34
@@ -1061,7 +1063,7 @@ def config5(device, stream, world=1, rank=0, gen=C5_GEN):
     import torch.distributed as dist
 
     import acefa
-    from acefa.dist import ShardedOp, head_shard
+    from acefa.dist import MirroredShardedOp, head_shard
 
     sets = C5_SETS // world
     g = torch.Generator(device=device).manual_seed(SEED + 5000 + 7919 * rank)
@@ -1138,8 +1140,8 @@ def config5(device, stream, world=1, rank=0, gen=C5_GEN):
         for kk, vv, mm in ((ks, vs, mwin if l % 2 == 0 else None), (kc, vc, mpad)):
             if world == 1:  # the full output directly, no gather
                 dit_ops.append(acefa.Op(qx, kk, vv, mask=mm, out=out1, scale=D ** -0.5))
-            else:
-                dit_ops.append(ShardedOp(qx, kk, vv, mm, world, scale=D ** -0.5))
+            else:  # each rank's kernel stores its heads into every rank's full output
+                dit_ops.append(MirroredShardedOp(qx, kk, vv, mm, world, scale=D ** -0.5))
 
     def run_dit(steps):
         for _ in range(steps):
@@ -1176,6 +1178,9 @@ def config5(device, stream, world=1, rank=0, gen=C5_GEN):
     full, win, cross = c5_dit_flops()
     dit_fl = C5_DIT_STEPS * (C5_DIT_LAYERS // 2) * (full + win) + C5_DIT_STEPS * C5_DIT_LAYERS * cross
     dec_total = dec_bytes * world
+    for op in dit_ops:
+        if world > 1:
+            op.close()
     del graphs, pre_graph, keep, pre_ops, dit_ops, caches
     torch.cuda.empty_cache()
     return {
@@ -1192,7 +1197,8 @@ def config5(device, stream, world=1, rank=0, gen=C5_GEN):
         "dit": {"ms": round(ms_dit, 2), "steps": C5_DIT_STEPS, "layers": C5_DIT_LAYERS,
                 "tflop": round(dit_fl / 1e12, 2), "tflops": round(dit_fl / (ms_dit / 1e3) / 1e12, 1),
                 "frac_of_bf16_peak": round(dit_fl / (ms_dit / 1e3) / 1e12 / tf_peak, 4),
-                "assembly": "NCCL all_gather_into_tensor + permute" if world > 1 else "single GPU"},
+                "assembly": ("kernel stores its heads into every rank's output over NVLink + one-element "
+                             "NCCL all-reduce per op") if world > 1 else "single GPU"},
         "note": "device time per part (CUDA events, max over ranks); decode bytes count valid K/V rows; "
                 "f16 masks filled like the reference's; LM KV sets and DiT heads split over the GPUs",
     }
