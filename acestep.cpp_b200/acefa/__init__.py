@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "acefa_flash_attn_ext_gen",
     "acefa_flash_attn_ext_fused",
     "acefa_kv_prologue",
+    "acefa_cfg_logit_combine",
 )
 
 MAX_MIRRORS = 7
@@ -190,6 +191,10 @@ def load_library(path: str | None = None):
     lib.acefa_flash_attn_ext_fused.restype = ctypes.c_int
     lib.acefa_kv_prologue.argtypes = [T, T, T, T, ctypes.POINTER(RopeNormC), ctypes.c_void_p]
     lib.acefa_kv_prologue.restype = ctypes.c_int
+    lib.acefa_cfg_logit_combine.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                            ctypes.c_void_p, ctypes.c_void_p]
+    lib.acefa_cfg_logit_combine.restype = ctypes.c_int
     lib.acefa_peer_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
     lib.acefa_peer_export.restype = ctypes.c_int
     lib.acefa_peer_import.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
@@ -438,6 +443,30 @@ def kv_prologue(k_src, k_dst, v_src=None, v_dst=None, prologue: RopeNorm | None 
     if st != OK:
         raise AcefaError(st, "acefa_kv_prologue")
     return k_dst, v_dst
+
+
+def cfg_logit_combine(cond: torch.Tensor, uncond: torch.Tensor | None, eos_idx: int, code_offset: int,
+                      code_count: int, cfg_scale: float, out: torch.Tensor | None = None, stream=None):
+    """acefa_cfg_logit_combine: CFG mix + compaction of n logit rows
+    (src/pipeline-lm.cpp:471-492).  cond / uncond: (n, row_stride) f32 on the
+    device, rows contiguous (uncond None: no CFG).  Returns (n, code_count +
+    (eos_idx >= 0)) f32: [EOS, codes...] of uncond + cfg_scale * (cond - uncond)."""
+    assert cond.dtype == torch.float32 and cond.dim() == 2 and cond.stride(1) == 1
+    n, stride = cond.shape
+    if uncond is not None:
+        assert uncond.dtype == torch.float32 and uncond.shape == cond.shape and uncond.stride() == cond.stride()
+    cols = code_count + (1 if eos_idx >= 0 else 0)
+    if out is None:
+        out = torch.empty((n, cols), dtype=torch.float32, device=cond.device)
+    assert out.is_contiguous() and out.shape == (n, cols)
+    lib = load_library()
+    st = lib.acefa_cfg_logit_combine(ctypes.c_void_p(cond.data_ptr()),
+                                     ctypes.c_void_p(uncond.data_ptr() if uncond is not None else 0),
+                                     cond.stride(0), n, eos_idx, code_offset, code_count, cfg_scale,
+                                     ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(_stream_ptr(stream)))
+    if st != OK:
+        raise AcefaError(st, "acefa_cfg_logit_combine")
+    return out
 
 
 # input preparation helpers (torch ops; not on the attention path)

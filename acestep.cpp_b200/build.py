@@ -18,7 +18,8 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libacefa.so")
 BUILD = os.path.join(HERE, "_build")
 
-SOURCES = ["fa_api.cu", "fa_decode.cu", "fa_dense.cu", "fa_noalloc.cu", "fa_peer.cu", "fa_prologue.cu"]
+SOURCES = ["fa_api.cu", "fa_decode.cu", "fa_dense.cu", "fa_noalloc.cu", "fa_peer.cu", "fa_prologue.cu",
+           "cfg_combine.cu"]
 HEADERS = ["fa_internal.h", "ptx.cuh", "q8.cuh", "rope_norm.cuh"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -708,6 +708,51 @@ ACEFA_API int acefa_kv_prologue(const acefa_tensor *k_src, const acefa_tensor *v
     return rc;
 }
 
+ACEFA_API int acefa_cfg_logit_combine(const float *cond, const float *uncond, int64_t row_stride, int n,
+                                      int eos_idx, int code_offset, int code_count, float cfg_scale,
+                                      float *compact, void *stream) {
+    if (n != 0 && (!cond || !compact)) {  // n == 0 reads and writes nothing
+        return ACEFA_ERR_NULL;
+    }
+    if (n < 0 || n > 65535 || row_stride <= 0 || code_count < 0 || code_offset < 0 ||
+        (int64_t) code_offset + code_count > row_stride || eos_idx >= row_stride ||
+        (int64_t) code_count + 1 > INT32_MAX) {
+        return ACEFA_ERR_SHAPE;
+    }
+    if (!aligned(cond, 4) || !aligned(compact, 4) || (uncond && !aligned(uncond, 4))) {
+        return ACEFA_ERR_LAYOUT;
+    }
+    const int cols = code_count + (eos_idx >= 0 ? 1 : 0);
+    const auto lo = reinterpret_cast<uintptr_t>(compact), hi = lo + (uintptr_t) n * cols * sizeof(float);
+    const bool in_place = compact == cond && eos_idx < 0 && code_offset == 0 && code_count == row_stride;
+    auto overlaps = [&](const float *rows) {  // the byte range n rows of row_stride floats span
+        if (!rows || n == 0) {
+            return false;
+        }
+        const auto b = reinterpret_cast<uintptr_t>(rows);
+        const auto e = b + ((uintptr_t) (n - 1) * row_stride + row_stride) * sizeof(float);
+        return b < hi && lo < e;
+    };
+    if ((!in_place && overlaps(cond)) || overlaps(uncond)) {
+        return ACEFA_ERR_LAYOUT;
+    }
+    DevInfo *di = nullptr;
+    int      rc = dev_info(&di);
+    if (rc != ACEFA_OK) {
+        return rc;
+    }
+    if (n == 0 || cols == 0) {
+        t_last_launches = 0;
+        return ACEFA_OK;
+    }
+    rc = cfg_combine_launch(cond, uncond, row_stride, n, eos_idx, code_offset, cols, cfg_scale, compact,
+                            static_cast<cudaStream_t>(stream));
+    if (rc == ACEFA_OK) {
+        t_last_launches = 1;
+    }
+    return rc;
+}
+
 ACEFA_API int acefa_device_error(void *stream) {
     DevInfo *di = nullptr;
     int      rc = dev_info(&di);

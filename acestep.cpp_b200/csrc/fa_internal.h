@@ -205,4 +205,9 @@ size_t workspace_bytes_within(const acefa_tensor *q, const acefa_tensor *k, cons
 int kv_prologue_launch(const acefa_tensor *k_src, const acefa_tensor *v_src, const acefa_tensor *k_dst,
                        const acefa_tensor *v_dst, const RopeNorm &kp, int sm_count, cudaStream_t stream);
 
+// ------------------------------------------------------------------ CFG logit combine
+// Launch for arguments validated by acefa_cfg_logit_combine (fa_api.cu).
+int cfg_combine_launch(const float *cond, const float *uncond, int64_t row_stride, int n, int eos_idx,
+                       int code_offset, int cols, float cfg_scale, float *compact, cudaStream_t stream);
+
 }  // namespace acefa

@@ -291,6 +291,29 @@ ACEFA_API int acefa_peer_export(const void *ptr, void *handle, uint64_t *offset)
 ACEFA_API int acefa_peer_import(const void *handle, uint64_t offset, void **ptr);
 ACEFA_API int acefa_peer_release(void *ptr);
 
+/*
+ * CFG combine + logit compaction of a batched LM decode step on the device:
+ * the host loop of src/pipeline-lm.cpp:471-492 (and, with eos_idx < 0 and the
+ * range [0, V), the full-vocabulary combines of :104-108, :193-199, :364-370),
+ * so that only the compact rows cross to the host.  cond / uncond: F32 logits,
+ * sequence a's rows at cond + a * row_stride and uncond + a * row_stride (in
+ * the reference's batch layout uncond = cond + n * row_stride); uncond NULL:
+ * no CFG (the reference's use_cfg false), a plain gather.  compact: n rows of
+ * cols = code_count + (eos_idx >= 0) floats, contiguous:
+ *   column 0            <- logit eos_idx            (only when eos_idx >= 0)
+ *   following columns   <- logits code_offset .. code_offset + code_count - 1
+ * each u + cfg_scale * (c - u) with every operation rounded to F32 on its own
+ * (no FMA), bit-identical to the reference's x86-64 host arithmetic.
+ * compact must not overlap cond or uncond, except compact == cond with
+ * eos_idx < 0, code_offset 0 and code_count == row_stride (the in-place
+ * full-row combine).  n <= 65535.  Stream-ordered, one launch (none for
+ * n == 0, which accepts NULL buffers).  Returns ACEFA_ERR_NULL, ACEFA_ERR_SHAPE (a column outside the row,
+ * n out of range), ACEFA_ERR_LAYOUT (misaligned or overlapping buffers).
+ */
+ACEFA_API int acefa_cfg_logit_combine(const float *cond, const float *uncond, int64_t row_stride, int n,
+                                      int eos_idx, int code_offset, int code_count, float cfg_scale,
+                                      float *compact, void *stream);
+
 /* Workspace acefa_flash_attn_ext() needs for these operands on the current device
  * (split-KV partial results, mask tile classes).  A function of shapes, types
  * and the device only -- never of tensor contents -- so it can be sized once

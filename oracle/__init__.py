@@ -9,7 +9,10 @@ kernel lives in the absent ggml submodule (acestep.cpp ``.gitmodules:1-3``) and
 the reference ships no op-level golden vectors.  The Q8_0 block format is pinned
 bit-exactly against gguf 0.19.0 (``tests/golden/q8_0_*.npy``).  The
 RMSNorm + RoPE prologue (``rope_norm``) is pinned against the Qwen3 model
-definition in HF transformers (``tests/golden/rope_norm_*.npz``).
+definition in HF transformers (``tests/golden/rope_norm_*.npz``).  The CFG
+logit combine (``cfg_logit_combine``) is the reference's own host loop
+(src/pipeline-lm.cpp:471-492) in f32 arithmetic, checked against a numpy
+restatement of that loop.
 """
 from .oracle import (  # noqa: F401
     GGML_F16,
@@ -24,4 +27,5 @@ from .oracle import (  # noqa: F401
     dequantize_q8_0,
     lib_path,
     rope_norm,
+    cfg_logit_combine,
 )

@@ -626,3 +626,28 @@ void ora_rope_norm(float *x, int64_t rows, int D, const float *weight, float eps
         }
     }
 }
+
+/* CFG logit combine + compaction (see fa_oracle.h), the host loop of
+ * src/pipeline-lm.cpp:471-492: lc[i] = lu[i] + cfg_scale * (lc[i] - lu[i]) on
+ * the EOS column and the audio-code range, then the compact copy.  Each
+ * operation rounds to f32 on its own, as the reference's x86-64 build computes
+ * it (its baseline ISA has no FMA, so nothing is contracted). */
+void ora_cfg_logit_combine(const float *cond, const float *uncond, int64_t row_stride, int n, int eos_idx,
+                           int code_offset, int code_count, float cfg_scale, float *compact) {
+    const int cols = code_count + (eos_idx >= 0 ? 1 : 0);
+    for (int a = 0; a < n; ++a) {
+        const float *lc = cond + (int64_t) a * row_stride;
+        const float *lu = uncond ? uncond + (int64_t) a * row_stride : NULL;
+        float       *o  = compact + (int64_t) a * cols;
+        for (int j = 0; j < cols; ++j) {
+            const int64_t col = eos_idx >= 0 ? (j == 0 ? eos_idx : code_offset + j - 1) : code_offset + j;
+            float         r   = lc[col];
+            if (lu) {
+                const float d = lc[col] - lu[col];
+                const float m = cfg_scale * d;
+                r             = lu[col] + m;
+            }
+            o[j] = r;
+        }
+    }
+}

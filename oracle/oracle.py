@@ -64,6 +64,10 @@ def _load():
         lib.ora_rope_norm.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
                                       ctypes.c_float, ctypes.c_float, ctypes.c_void_p]
         lib.ora_rope_norm.restype = None
+        lib.ora_cfg_logit_combine.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                              ctypes.c_void_p]
+        lib.ora_cfg_logit_combine.restype = None
         _lib = lib
     return _lib
 
@@ -162,3 +166,21 @@ def dequantize_q8_0(y: np.ndarray) -> np.ndarray:
     x = np.empty(y.shape[:-1] + (n,), dtype=np.float32)
     lib.ora_dequantize_q8_0(y.ctypes.data, x.ctypes.data, x.size)
     return x
+
+
+def cfg_logit_combine(cond: np.ndarray, uncond: np.ndarray | None, eos_idx: int, code_offset: int,
+                      code_count: int, cfg_scale: float) -> np.ndarray:
+    """CFG combine + compaction of n logit rows (cond / uncond: (n, row_stride)
+    f32).  Returns (n, code_count + (eos_idx >= 0)) f32."""
+    lib = _load()
+    c = np.ascontiguousarray(cond, dtype=np.float32)
+    u = None if uncond is None else np.ascontiguousarray(uncond, dtype=np.float32)
+    n, stride = c.shape
+    if u is not None:
+        assert u.shape == c.shape
+    cols = code_count + (1 if eos_idx >= 0 else 0)
+    assert code_offset >= 0 and code_offset + code_count <= stride and eos_idx < stride
+    out = np.empty((n, cols), dtype=np.float32)
+    lib.ora_cfg_logit_combine(c.ctypes.data, None if u is None else u.ctypes.data, stride, n, eos_idx,
+                              code_offset, code_count, cfg_scale, out.ctypes.data)
+    return out

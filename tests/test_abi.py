@@ -268,6 +268,27 @@ def test_kv_prologue_validates_before_launch(lib):
         assert lib.acefa_kv_prologue(r(src), None, r(dst), None, None, None) in (-6, -7)  # plain conversion
 
 
+def test_cfg_combine_validates_before_launch(lib):
+    f = lib.acefa_cfg_logit_combine
+    P = ctypes.c_void_p
+    c, u, o = P(1 << 20), P((1 << 20) + 8 * 65559 * 4), P(1 << 26)
+    assert f(None, u, 65559, 8, 0, 24, 65535, 2.0, o, None) == -1
+    if not torch.cuda.is_available():
+        assert f(None, None, 65559, 0, 0, 24, 65535, 2.0, None, None) in (-6, -7)  # n == 0: no buffers needed
+    assert f(c, u, 65559, 8, 0, 24, 65535, 2.0, None, None) == -1
+    assert f(c, u, 65559, 8, 0, 25, 65535, 2.0, o, None) == -3          # code range past the row
+    assert f(c, u, 65559, 8, 65559, 24, 65535, 2.0, o, None) == -3      # EOS column past the row
+    assert f(c, u, 65559, -1, 0, 24, 65535, 2.0, o, None) == -3
+    assert f(c, u, 65559, 65536, 0, 24, 65535, 2.0, o, None) == -3      # one grid row per sequence
+    assert f(c, u, 0, 8, -1, 0, 0, 2.0, o, None) == -3
+    assert f(P((1 << 20) + 2), u, 65559, 8, 0, 24, 65535, 2.0, o, None) == -4  # f32 alignment
+    assert f(c, u, 65559, 8, 0, 24, 65535, 2.0, P((1 << 20) + 64), None) == -4  # compact overlaps cond
+    assert f(c, u, 65559, 8, 0, 24, 65535, 2.0, P((1 << 20) + 9 * 65559 * 4), None) == -4  # ... uncond
+    if not torch.cuda.is_available():
+        assert f(c, u, 65559, 8, 0, 24, 65535, 2.0, o, None) in (-6, -7)
+        assert f(c, u, 100, 8, -1, 0, 100, 2.0, c, None) in (-6, -7)  # in place, full rows: accepted
+
+
 def test_peer_entry_points_reject_null(lib):
     assert lib.acefa_peer_export(None, None, None) == -1
     assert lib.acefa_peer_import(None, 0, None) == -1

@@ -148,3 +148,38 @@ def test_oracle_matches_torch_sdpa(oracle_mod, B, Hq, Hkv, nq, nkv, kind):
     sel = np.broadcast_to(rows[:, :, None, None], want.shape)
     assert np.isfinite(got).all()
     np.testing.assert_allclose(got[sel], want[sel], rtol=0, atol=2e-5)
+
+
+def _reference_cfg_loop(batch_logits, n_active, out_V, eos_idx, code_offset, code_count, cfg_scale, use_cfg):
+    """The host loop of src/pipeline-lm.cpp:471-492 restated with numpy f32
+    scalars (each operation rounded to f32, as the reference's C++ computes
+    it): combine in place on the EOS column and the code range, then copy the
+    compact array of each active sequence."""
+    lg = batch_logits.copy()
+    s = np.float32(cfg_scale)
+    out = np.empty((n_active, code_count + 1), dtype=np.float32)
+    for a in range(n_active):
+        lc = lg[a * out_V:(a + 1) * out_V]
+        if use_cfg:
+            lu = lg[(n_active + a) * out_V:(n_active + a + 1) * out_V]
+            lc[eos_idx] = lu[eos_idx] + s * (lc[eos_idx] - lu[eos_idx])
+            for c in range(code_count):
+                i = code_offset + c
+                lc[i] = lu[i] + s * (lc[i] - lu[i])
+        out[a, 0] = lc[eos_idx]
+        out[a, 1:] = lc[code_offset:code_offset + code_count]
+    return out
+
+
+@pytest.mark.parametrize("use_cfg", [True, False])
+def test_cfg_logit_combine_matches_reference_loop(oracle_mod, use_cfg):
+    """Small partial-head layout (EOS at column 0, codes from column 24 as with
+    lm_offset = TOKEN_IM_END) with extreme values in the mix."""
+    n, V, eos, off, cnt = 3, 97, 0, 24, 70
+    r = np.random.default_rng(11)
+    logits = (r.standard_normal(2 * n * V) * 30).astype(np.float32)
+    logits[[5, 40, 300, 400]] = [np.inf, -np.inf, 3.0e38, -1.0e9]
+    want = _reference_cfg_loop(logits, n, V, eos, off, cnt, 3.5, use_cfg)
+    rows = logits.reshape(2 * n, V)
+    got = oracle_mod.cfg_logit_combine(rows[:n], rows[n:] if use_cfg else None, eos, off, cnt, 3.5)
+    assert np.array_equal(got, want, equal_nan=True)
