@@ -139,8 +139,11 @@ Checked check_operands(const acefa_tensor *q, const acefa_tensor *k, const acefa
     if (dst->ne[0] != D || dst->ne[1] != Hq || dst->ne[2] != n_q || dst->ne[3] != B) {
         return fail(ACEFA_ERR_SHAPE);
     }
-    if (D != 64 && D != 128) {
+    if (D != 64 && D != 128 && D != 256) {
         return fail(ACEFA_ERR_SHAPE);
+    }
+    if (D == 256 && k->type == ACEFA_TYPE_Q8_0) {
+        return fail(ACEFA_ERR_TYPE);  // D = 256 serves F16 and BF16 K/V
     }
     if (n_kv > (1ll << 30) || n_q > (1ll << 30) || Hq > 4096 || B > (1ll << 20) ||
         (Hq / Hkv) * n_q > (1ll << 30)) {
@@ -257,7 +260,7 @@ DecodePlan plan_decode(const OpDesc &o, bool prologue) {
 }
 
 // ------------------------------------------------------------------ dense plan
-// The dense tcgen05 kernel serves D = 128 (F16, BF16 or Q8_0 K/V) when a K/V
+// The dense tcgen05 kernel serves D = 64 and 128 (F16, BF16 or Q8_0 K/V) when a K/V
 // head has more than 64 rows of queries (G * n_q) -- prefill, encoders, DiT.  A
 // function of shapes only, so the choice (and the workspace) is fixed before
 // capture.
@@ -265,7 +268,7 @@ bool use_dense(const OpDesc &o) {
     const int64_t rows = (int64_t) o.G * o.n_q;
     const int64_t n_kt = ((int64_t) o.n_kv + kDenseBN - 1) / kDenseBN;
     const int64_t n_pairs = ((rows + kDenseBM - 1) / kDenseBM + 1) / 2;
-    return o.D == 128 && rows > 64 && n_kt <= kDenseMaxKT && n_pairs * o.Hkv * o.B < (1ll << 31);
+    return (o.D == 128 || o.D == 64) && rows > 64 && n_kt <= kDenseMaxKT && n_pairs * o.Hkv * o.B < (1ll << 31);
 }
 
 struct DensePlan {
@@ -440,6 +443,9 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         }
         if (kn->type != ACEFA_TYPE_F32 || vn->type != ACEFA_TYPE_F32) {
             return ACEFA_ERR_TYPE;
+        }
+        if (c.op.D > 128) {
+            return ACEFA_ERR_SHAPE;  // one warp lane holds four values of the new row
         }
         for (const acefa_tensor *t : {kn, vn}) {
             if (t->ne[0] != k->ne[0] || t->ne[1] != 1 || t->ne[2] != k->ne[2] || t->ne[3] != k->ne[3]) {

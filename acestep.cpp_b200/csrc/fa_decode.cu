@@ -92,8 +92,11 @@ struct DecCfg {
     static constexpr int kOffMeta   = kOffBars + kNumBars * 8;
     static constexpr int kOffFlags  = kOffMeta + kStages * 16;
     static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
-    static constexpr int kCtasPerSm = kQ8 ? ACEFA_Q8_CTAS : 2;
+    // D = 256: a 66 KB stage, one CTA per SM
+    static constexpr int kCtasPerSm = D > 128 ? 1 : (kQ8 ? ACEFA_Q8_CTAS : 2);
     static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024, "CTAs per SM exceed shared memory");
+    static_assert(kSmemBytes <= 232448, "stages exceed the 227 KB per CTA");
+    static_assert(D <= 128 || !kQ8, "D = 256 serves F16 and BF16 K/V");
 };
 
 struct UnitCoord {
@@ -1408,16 +1411,39 @@ const InstInfo &inst_info(int dev) {
     return in;
 }
 
+// The instance with the prologue exists for D <= 128 (the host refuses
+// prologues and appends at D = 256).
+template <int KV_TYPE, int D>
+constexpr bool kHasPro = D <= 128;
+
+template <int KV_TYPE, int D>
+const InstInfo &pro_info(bool pro, int dev) {
+    if constexpr (kHasPro<KV_TYPE, D>) {
+        if (pro) {
+            return inst_info<KV_TYPE, D, true>(dev);
+        }
+    }
+    return inst_info<KV_TYPE, D, false>(dev);
+}
+
 template <int KV_TYPE, int D>
 cudaError_t launch_impl(const DecodeLaunch &L, cudaStream_t s, int *launches) {
     using Cfg      = DecCfg<KV_TYPE, D>;
     const bool pro = L.p.op.qp.on || L.p.kp.on;
-    auto       kern = pro ? fa_decode_kernel<KV_TYPE, D, true> : fa_decode_kernel<KV_TYPE, D, false>;
-    int        dev  = 0;
+    if (pro && !kHasPro<KV_TYPE, D>) {
+        return cudaErrorInvalidValue;
+    }
+    auto kern = fa_decode_kernel<KV_TYPE, D, false>;
+    if constexpr (kHasPro<KV_TYPE, D>) {
+        if (pro) {
+            kern = fa_decode_kernel<KV_TYPE, D, true>;
+        }
+    }
+    int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
         return cudaErrorInvalidDevice;
     }
-    const InstInfo &in = pro ? inst_info<KV_TYPE, D, true>(dev) : inst_info<KV_TYPE, D, false>(dev);
+    const InstInfo &in = pro_info<KV_TYPE, D>(pro, dev);
     if (!in.ok) {
         return cudaErrorInvalidConfiguration;
     }
@@ -1453,7 +1479,7 @@ int cluster_for(bool pro, int units, int tiles_per_unit) {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
         return 1;
     }
-    const InstInfo &in = pro ? inst_info<KV_TYPE, D, true>(dev) : inst_info<KV_TYPE, D, false>(dev);
+    const InstInfo &in   = pro_info<KV_TYPE, D>(pro, dev);
     int             best = 1;
     for (int c = 2; c <= kDecMaxCluster && in.ok; ++c) {
         if (c <= tiles_per_unit && units <= in.active[c]) {
@@ -1473,16 +1499,21 @@ cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches) 
     if (t == ACEFA_TYPE_BF16 && D == 64) return launch_impl<ACEFA_TYPE_BF16, 64>(L, s, launches);
     if (t == ACEFA_TYPE_Q8_0 && D == 128) return launch_impl<ACEFA_TYPE_Q8_0, 128>(L, s, launches);
     if (t == ACEFA_TYPE_Q8_0 && D == 64) return launch_impl<ACEFA_TYPE_Q8_0, 64>(L, s, launches);
+    if (t == ACEFA_TYPE_F16 && D == 256) return launch_impl<ACEFA_TYPE_F16, 256>(L, s, launches);
+    if (t == ACEFA_TYPE_BF16 && D == 256) return launch_impl<ACEFA_TYPE_BF16, 256>(L, s, launches);
     return cudaErrorInvalidValue;
 }
 
 int decode_cluster(int kv_type, int D, bool pro, int units, int tiles_per_unit) {
     const int u = units, t = tiles_per_unit;
     if (kv_type == ACEFA_TYPE_F16) {
-        return D == 128 ? cluster_for<ACEFA_TYPE_F16, 128>(pro, u, t) : cluster_for<ACEFA_TYPE_F16, 64>(pro, u, t);
+        return D == 128 ? cluster_for<ACEFA_TYPE_F16, 128>(pro, u, t)
+                        : (D == 64 ? cluster_for<ACEFA_TYPE_F16, 64>(pro, u, t) : cluster_for<ACEFA_TYPE_F16, 256>(pro, u, t));
     }
     if (kv_type == ACEFA_TYPE_BF16) {
-        return D == 128 ? cluster_for<ACEFA_TYPE_BF16, 128>(pro, u, t) : cluster_for<ACEFA_TYPE_BF16, 64>(pro, u, t);
+        return D == 128 ? cluster_for<ACEFA_TYPE_BF16, 128>(pro, u, t)
+                        : (D == 64 ? cluster_for<ACEFA_TYPE_BF16, 64>(pro, u, t)
+                                   : cluster_for<ACEFA_TYPE_BF16, 256>(pro, u, t));
     }
     return D == 128 ? cluster_for<ACEFA_TYPE_Q8_0, 128>(pro, u, t) : cluster_for<ACEFA_TYPE_Q8_0, 64>(pro, u, t);
 }

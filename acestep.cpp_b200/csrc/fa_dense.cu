@@ -65,7 +65,7 @@ constexpr uint16_t kHalfNegInf = 0xFC00u;
 constexpr int kKvF16 = 0, kKvBF16 = 1, kKvQ8 = 2;
 constexpr int kConvWarps = 2;                                       // warps 2 and 3
 constexpr int kRawRows   = kDenseBN / 2;                            // Q8_0 keys per staged half tile
-constexpr int kRawRowBytes = 136;                                   // D = 128: 4 blocks of 34 B
+constexpr int kRawRowBytes = 136;                                   // largest row (D = 128): 4 blocks of 34 B
 constexpr int kRawBytes  = (kRawRows * kRawRowBytes + 16 + 15) / 16 * 16;  // + up to 15 lead bytes
 constexpr int kRawStages = 3;
 constexpr int kOffExt     = (kOffMisc + 16 + 15) / 16 * 16;
@@ -203,18 +203,22 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
     return cvt_f16x2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-// kRawRows staged Q8_0 rows (136 B each, any 2-B alignment) -> rows
-// [row0, row0 + kRawRows) of a 128-key F16 tile in the 128-B swizzled layout of
-// the TMA boxes {64 dims, 128 keys}.  A warp iteration converts 8 rows, lane =
-// (row, 32-value block).  Rows at or past `nvalid` become zeros.
+// kRawRows staged Q8_0 rows (HD/32 blocks of 34 B each, any 2-B alignment) ->
+// rows [row0, row0 + kRawRows) of a 128-key F16 tile in the 128-B swizzled
+// layout of the TMA boxes {64 dims, 128 keys}.  A warp iteration converts
+// 32 / (HD/32) rows, lane = (row, 32-value block).  Rows at or past `nvalid`
+// become zeros.
+template <int HD>
 __device__ __forceinline__ void q8_rows_to_f16(uint32_t src, uint32_t tile, int row0, int nvalid, int cw, int lane) {
-    const int blk = lane & 3;
-    const int rr  = lane >> 2;
+    constexpr int kBlk  = HD / 32;      // blocks per row
+    constexpr int kRows = 32 / kBlk;    // rows per warp iteration
+    const int     blk   = lane % kBlk;
+    const int     rr    = lane / kBlk;
 #pragma unroll 1
-    for (int it = cw; it < kRawRows / 8; it += kConvWarps) {
-        const int j  = it * 8 + rr;
+    for (int it = cw; it < kRawRows / kRows; it += kConvWarps) {
+        const int j  = it * kRows + rr;
         uint32_t  q[8];
-        const uint16_t dbits = q8_load_run<8>(src + (uint32_t) (j * kRawRowBytes + 34 * blk), 0, q);
+        const uint16_t dbits = q8_load_run<8>(src + (uint32_t) (j * kBlk * 34 + 34 * blk), 0, q);
         const __half2  d2    = __half2half2(__ushort_as_half(j < nvalid ? dbits : (uint16_t) 0));
         uint32_t       o[16];
 #pragma unroll
@@ -445,7 +449,9 @@ __device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4],
 // ---------------------------------------------------------------------------
 // PRO: the instance that applies the QK-norm + RoPE prologue to Q rows; KVT:
 // the K/V element type (kKvF16 / kKvBF16 / kKvQ8).
-template <bool PRO, int KVT>
+// HD = head dim, 64 or 128: D = 64 reads one 64-dim box per K/V tile, runs
+// half the S k-steps and an N = 64 PV MMA, and leaves O in 64 TMEM columns.
+template <bool PRO, int KVT, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap) {
@@ -570,9 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 uint8_t           *dst = smem + kOffRing + buf * kTileBytes;
                 const CUtensorMap *map = h == 0 ? &kmap : &vmap;
-                mbar_arrive_expect_tx(&full[buf], kTileBytes);
+                mbar_arrive_expect_tx(&full[buf], kTileBytes * HD / 128);
                 tma_load_4d(dst, map, 0, p_j * kDenseBN, hk, bk, &full[buf]);
-                tma_load_4d(dst + kDenseBN * 128, map, 64, p_j * kDenseBN, hk, bk, &full[buf]);
+                if constexpr (HD == 128) {
+                    tma_load_4d(dst + kDenseBN * 128, map, 64, p_j * kDenseBN, hk, bk, &full[buf]);
+                }
                 pend[buf] = u & 1;
             }
             ++p_use;
@@ -585,17 +593,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
-    // ---- Q: f32 rows -> f16, 128-B swizzled K-major tiles [2 x 64 dims][128 rows].
+    // ---- Q: f32 rows -> f16, 128-B swizzled K-major tiles [HD/64 x 64 dims][128 rows].
     // 16-B chunks, eight loads in flight per thread before any is converted.
-    // A warp's chunks of one load step are one row (lane l: dims 4l..4l+3).
+    // A warp's chunks of one load step are 32 / kCpr rows (chunk c of a row:
+    // dims 4c..4c+3).
     {
-        constexpr int kChunks = 2 * kDenseBM * 32;
+        constexpr int kCpr    = HD / 4;  // chunks per row
+        constexpr int kChunks = 2 * kDenseBM * kCpr;
         constexpr int kUnroll = 8;
         auto store_q = [&](int ch, float4 x) {
-            const int      rr = ch >> 5;
+            const int      rr = ch / kCpr;
             const int      i  = rr / kDenseBM;
             const int      r  = rr % kDenseBM;
-            const int      d  = 4 * (ch & 31);
+            const int      d  = 4 * (ch % kCpr);
             const uint32_t lo = pack2<false>(x.x, x.y), hi = pack2<false>(x.z, x.w);
             uint8_t *dst = smem + kOffQ + i * kQBytes + (d >> 6) * (kDenseBM * 128) + r * 128 +
                            ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
@@ -607,14 +617,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int u = 0; u < kUnroll; ++u) {
                 const int ch = base + u * kThreads;
                 v[u]         = make_float4(0.f, 0.f, 0.f, 0.f);
-                const int rr = ch >> 5;
+                const int rr = ch / kCpr;
                 const int i  = rr / kDenseBM;
                 const int gr = (t0 + i) * kDenseBM + rr % kDenseBM;
                 if (ch < kChunks && has_tile[i] && gr < P.rows_total) {
                     int iq, hq;
                     row_to_query(gr, o.G, hk, iq, hq);
                     const char  *qrow = o.q + (int64_t) iq * o.q_nb1 + (int64_t) hq * o.q_nb2 + (int64_t) b * o.q_nb3;
-                    const float *qf   = reinterpret_cast<const float *>(qrow) + 4 * (ch & 31);
+                    const float *qf   = reinterpret_cast<const float *>(qrow) + 4 * (ch % kCpr);
                     if ((reinterpret_cast<uintptr_t>(qf) & 15u) == 0) {
                         v[u] = __ldg(reinterpret_cast<const float4 *>(qf));
                     } else {
@@ -644,9 +654,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ch >= kChunks) {
                     break;
                 }
-                const int rr  = ch >> 5;
+                const int rr  = ch / kCpr;
                 const int i   = rr / kDenseBM;
                 const int gr  = (t0 + i) * kDenseBM + rr % kDenseBM;
+                const int cr  = lane % kCpr;  // this lane's chunk of its row
                 int       pos = 0;
                 if (o.qp.rope && has_tile[i] && gr < P.rows_total) {
                     int iq, hq;
@@ -661,25 +672,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ss = fmaf(x[e], x[e], ss);
                     }
 #pragma unroll
-                    for (int off = 16; off; off >>= 1) {
+                    for (int off = kCpr / 2; off; off >>= 1) {
                         ss += __shfl_xor_sync(0xffffffffu, ss, off);
                     }
-                    const float sc = rn_scale(o.qp, ss, kDenseBM);
+                    const float sc = rn_scale(o.qp, ss, HD);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        x[e] = (x[e] * sc) * __ldg(o.qp.w + 4 * lane + e);
+                        x[e] = (x[e] * sc) * __ldg(o.qp.w + 4 * cr + e);
                     }
                 }
                 if (o.qp.rope) {
                     float2 cs[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        cs[e] = rn_cos_sin((float) pos * o.qp.inv_freq[(4 * lane + e) & 63]);
+                        cs[e] = rn_cos_sin((float) pos * o.qp.inv_freq[(4 * cr + e) & (HD / 2 - 1)]);
                     }
-                    const bool first = lane < 16;
+                    const bool first = cr < kCpr / 2;  // dim d < HD/2 pairs with d + HD/2
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float pt = __shfl_xor_sync(0xffffffffu, x[e], 16);
+                        const float pt = __shfl_xor_sync(0xffffffffu, x[e], kCpr / 2);
                         x[e] = first ? x[e] * cs[e].x - pt * cs[e].y : pt * cs[e].y + x[e] * cs[e].x;
                     }
                 }
@@ -722,9 +733,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const int      row0  = j * kDenseBN + q * kRawRows;
                     const int      nrows = max(0, min(kRawRows, o.n_kv - row0));
-                    const char    *src   = (h ? vb : kb) + (int64_t) row0 * kRawRowBytes;
+                    const char    *src   = (h ? vb : kb) + (int64_t) row0 * (HD / 32 * 34);
                     const uint32_t lead  = (uint32_t) (reinterpret_cast<uintptr_t>(src) & 15u);
-                    const uint32_t bytes = (uint32_t) nrows * kRawRowBytes;
+                    const uint32_t bytes = (uint32_t) nrows * (HD / 32 * 34);
                     const uint32_t bulk  = (lead + bytes) & ~15u;
                     uint8_t       *dst   = smem + kOffRaw + rs * kRawBytes;
                     if (nrows > 0 && (uint32_t) lane < lead + bytes - bulk && bulk + (uint32_t) lane >= lead) {
@@ -786,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ============================ MMA issuer ==============================
         if (lane == 0) {
             constexpr uint32_t idS = umma_idesc_f16(128, 128, false, false, false);
-            constexpr uint32_t idO = umma_idesc_f16(128, 128, false, true, false);
+            constexpr uint32_t idO = umma_idesc_f16(128, HD, false, true, false);
             // Base descriptors, built once.  Advancing a descriptor is a 64-bit add
             // to its start-address field (16-B units): k-step ks of a K-major
             // operand sits at (ks/4)*16 KB + (ks%4)*32 B; of the MN-major V at
@@ -809,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             auto issue_s = [&](uint32_t tS, uint64_t qd, int slot) {
                 const uint64_t kd = kd0 + (uint64_t) (slot * (kTileBytes >> 4));
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
+                for (int ks = 0; ks < HD / 16; ++ks) {
                     const uint64_t off = (uint64_t) ((ks >> 2) * (kDenseBM * 128 >> 4) + (ks & 3) * 2);
                     umma_ss(tS, qd + off, kd + off, idS, ks > 0 ? 1u : 0u);
                 }
@@ -947,7 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
 #pragma unroll 4
-                    for (int x = ct; x < kTileBytes / 16; x += 32 * kConvWarps) {
+                    for (int x = ct; x < kTileBytes * HD / 128 / 16; x += 32 * kConvWarps) {
                         uint4 w = *reinterpret_cast<const uint4 *>(tile + 16 * x);
                         w.x     = bf16x2_to_f16x2(w.x);
                         w.y     = bf16x2_to_f16x2(w.y);
@@ -972,7 +983,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         const int4 md = raw_meta[rs];
-                        q8_rows_to_f16(smem_u32(smem + kOffRaw + rs * kRawBytes) + (uint32_t) md.y, smem_u32(tile),
+                        q8_rows_to_f16<HD>(smem_u32(smem + kOffRaw + rs * kRawBytes) + (uint32_t) md.y, smem_u32(tile),
                                        q * kRawRows, md.x, cw, lane);
                         __syncwarp();
                         if (lane == 0) {
@@ -1053,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-                for (int ch = 0; ch < 8; ++ch) {
+                for (int ch = 0; ch < HD / 16; ++ch) {
                     uint32_t x[16];
                     tmem_ld16(tO + 16 * ch, x);
                     tmem_ld_wait16(x);
@@ -1213,7 +1224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // sum to this range's slot; fa_dense_combine finishes the rows
             float *slot = P.part + ((int64_t) ((unit_id - P.n_full) * P.n_split + sp) * 2 + i) * dense_part_floats();
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < HD / 32; ++ch) {
                 uint32_t xo[32];
                 if (ok && cnt > 0) {
                     tmem_ld32(tO + 32 * ch, xo);
@@ -1262,7 +1273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                             4 * st + (lane >> 3)));
         }
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < HD / 32; ++ch) {
             uint32_t x[32];
             if (ok && cnt > 0) {
                 tmem_ld32(tO + 32 * ch, x);
@@ -1406,7 +1417,8 @@ namespace {
 
 template <int KVT>
 cudaError_t configure_dense() {
-    for (auto k : {fa_dense_kernel<false, KVT>, fa_dense_kernel<true, KVT>}) {
+    for (auto k : {fa_dense_kernel<false, KVT, 128>, fa_dense_kernel<true, KVT, 128>, fa_dense_kernel<false, KVT, 64>,
+                   fa_dense_kernel<true, KVT, 64>}) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dense_smem_bytes<KVT>());
         if (e != cudaSuccess) {
             return e;
@@ -1453,9 +1465,16 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     }
     const int   kvt = L.p.op.kv_type == ACEFA_TYPE_Q8_0 ? kKvQ8 : (L.p.op.kv_type == ACEFA_TYPE_BF16 ? kKvBF16 : kKvF16);
     const bool  pro = L.p.op.qp.on;
-    auto        kern = kvt == kKvQ8    ? (pro ? fa_dense_kernel<true, kKvQ8> : fa_dense_kernel<false, kKvQ8>)
-                       : kvt == kKvBF16 ? (pro ? fa_dense_kernel<true, kKvBF16> : fa_dense_kernel<false, kKvBF16>)
-                                        : (pro ? fa_dense_kernel<true, kKvF16> : fa_dense_kernel<false, kKvF16>);
+    const bool  d64  = L.p.op.D == 64;
+    auto        kern = d64 ? (kvt == kKvQ8    ? (pro ? fa_dense_kernel<true, kKvQ8, 64> : fa_dense_kernel<false, kKvQ8, 64>)
+                              : kvt == kKvBF16 ? (pro ? fa_dense_kernel<true, kKvBF16, 64>
+                                                      : fa_dense_kernel<false, kKvBF16, 64>)
+                                               : (pro ? fa_dense_kernel<true, kKvF16, 64> : fa_dense_kernel<false, kKvF16, 64>))
+                           : (kvt == kKvQ8    ? (pro ? fa_dense_kernel<true, kKvQ8, 128> : fa_dense_kernel<false, kKvQ8, 128>)
+                              : kvt == kKvBF16 ? (pro ? fa_dense_kernel<true, kKvBF16, 128>
+                                                      : fa_dense_kernel<false, kKvBF16, 128>)
+                                               : (pro ? fa_dense_kernel<true, kKvF16, 128>
+                                                      : fa_dense_kernel<false, kKvF16, 128>));
     const int   smem = kvt == kKvQ8 ? dense_smem_bytes<kKvQ8>()
                                     : (kvt == kKvBF16 ? dense_smem_bytes<kKvBF16>() : dense_smem_bytes<kKvF16>());
     cudaLaunchConfig_t c = {};
@@ -1472,7 +1491,7 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     ++n;
     if (L.p.n_tail > 0) {
         cudaLaunchConfig_t cc = {};
-        cc.gridDim            = dim3((unsigned) L.p.n_tail, 2, 128 / kCombineDims);
+        cc.gridDim            = dim3((unsigned) L.p.n_tail, 2, (unsigned) (L.p.op.D / kCombineDims));
         cc.blockDim           = dim3(kDenseBM);
         cc.stream             = s;
         cc.attrs              = attr;

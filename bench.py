@@ -860,6 +860,10 @@ DENSE_WORKLOADS = {
     # prefill over a Q8_0 KV cache (one set: Q [128, 512, 32], K/V [128, 512, 8])
     "dit6000_bf16": (2, 16, 16, 6000, 6000, None, None, "bf16"),
     "prefill512_q8_0": (1, 32, 8, 512, 512, "causal", None, "q8_0"),
+    # head dims 64 (tcgen05, N = 64 PV) and 256 (F16 / BF16 only, on the
+    # split-KV kernel): operator shapes ggml accepts, not used by acestep.cpp
+    "dit6000_d64": (2, 16, 16, 6000, 6000, None, None, "f16", 64),
+    "dit1500_d256": (2, 16, 16, 1500, 1500, None, None, "f16", 256),
 }
 # workloads whose CPU baseline (oracle on sampled query rows) is timed too
 DENSE_CPU_SAMPLED = ("prefill4096", "dit6000", "cross6000")
@@ -886,10 +890,11 @@ def build_dense(device, name, seed=SEED + 3, rule=False):
 
     B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name][:7]
     kv = DENSE_WORKLOADS[name][7] if len(DENSE_WORKLOADS[name]) > 7 else "f16"
+    hd = DENSE_WORKLOADS[name][8] if len(DENSE_WORKLOADS[name]) > 8 else D
     g = torch.Generator(device=device).manual_seed(seed)
-    q = torch.randn(B, Hq, S_q, D, device=device, generator=g)
-    k = torch.randn(B, Hkv, S_kv, D, device=device, generator=g, dtype=torch.float16)
-    v = torch.randn(B, Hkv, S_kv, D, device=device, generator=g, dtype=torch.float16)
+    q = torch.randn(B, Hq, S_q, hd, device=device, generator=g)
+    k = torch.randn(B, Hkv, S_kv, hd, device=device, generator=g, dtype=torch.float16)
+    v = torch.randn(B, Hkv, S_kv, hd, device=device, generator=g, dtype=torch.float16)
     kv_type = None
     if kv == "bf16":
         k, v = k.bfloat16(), v.bfloat16()
@@ -910,10 +915,10 @@ def build_dense(device, name, seed=SEED + 3, rule=False):
         mg = {"causal": lambda: acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[S_kv - S_q] * B),
               "window": lambda: acefa.mask_gen(acefa.MASK_WINDOW, window=extra),
               "padding": lambda: acefa.mask_gen(acefa.MASK_PADDING, lens=[extra] * B)}[kind]()
-        op = acefa.Op(q, k, v, mask_gen=mg, kv_type=kv_type, scale=D ** -0.5)
+        op = acefa.Op(q, k, v, mask_gen=mg, kv_type=kv_type, scale=hd ** -0.5)
     else:
-        op = acefa.Op(q, k, v, mask=mask, kv_type=kv_type, scale=D ** -0.5)
-    flops = 4 * D * dense_pairs(S_q, S_kv, kind, extra) * Hq * B
+        op = acefa.Op(q, k, v, mask=mask, kv_type=kv_type, scale=hd ** -0.5)
+    flops = 4 * hd * dense_pairs(S_q, S_kv, kind, extra) * Hq * B
     return op, flops
 
 
@@ -1085,14 +1090,41 @@ def sharded_dit(device, stream, world, rank, iters=10, warmup=3):
     t = torch.tensor([ev[i].elapsed_time(ev[i + 1]) / iters for i in range(3)], device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     mop.close()
+    del op, mop, q, k, v
+    # the same node unsharded on one GPU (every rank alone, no collective): the
+    # denominator of the strong-scaling efficiency
+    import acefa
+
+    qf = torch.randn(B, Hq, S, D, device=device, generator=g)
+    kf = torch.randn(B, Hkv, S, D, device=device, generator=g, dtype=torch.float16)
+    vf = torch.randn(B, Hkv, S, D, device=device, generator=g, dtype=torch.float16)
+    full = acefa.Op(qf, kf, vf, scale=D ** -0.5)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            full(stream)
+        e0.record(stream)
+        for _ in range(iters):
+            full(stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    t1 = torch.tensor([e0.elapsed_time(e1) / iters], device=device)
+    dist.all_reduce(t1, op=dist.ReduceOp.MAX)
+    t1 = float(t1[0])
+    del full, qf, kf, vf
     flops = 4 * D * S * S * Hq * B
     tf = lambda ms: round(flops / (ms / 1e3) / 1e12, 1)  # noqa: E731
-    return {"gpus": world, "ms_attention_only": round(float(t[0]), 4),
+    eff = lambda ms: round(t1 / (world * ms), 4)  # noqa: E731
+    return {"gpus": world, "ms_one_gpu_unsharded": round(t1, 4), "ms_attention_only": round(float(t[0]), 4),
             "ms_with_nccl_allgather": round(float(t[1]), 4), "ms_p2p_mirrored": round(float(t[2]), 4),
             "tflops_total_nccl_allgather": tf(float(t[1])), "tflops_total_p2p_mirrored": tf(float(t[2])),
+            "strong_scaling_efficiency": {"attention_only": eff(float(t[0])),
+                                          "nccl_allgather": eff(float(t[1])),
+                                          "p2p_mirrored": eff(float(t[2]))},
             "note": "heads sharded by K/V group; full output on every rank either by NCCL "
                     "all_gather_into_tensor + permute, or by the kernel storing its rows into every "
-                    "rank's buffer over NVLink (one-element all-reduce as completion barrier)"}
+                    "rank's buffer over NVLink (one-element all-reduce as completion barrier); "
+                    "efficiency = one GPU's unsharded time / (N x the sharded time)"}
 
 
 # -------------------------------------------------------------------------

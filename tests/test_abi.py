@@ -96,6 +96,9 @@ def test_check_accepts_reference_shapes(lib):
     assert _check(lib, *_ops(nq=1500, Hq=16, Hkv=16, B=2, Bk=2, nkv=1500, mask=False)) == 0
     assert _check(lib, *_ops(nq=6000, Hq=16, Hkv=16, B=2, Bk=2, nkv=512)) == 0
     assert _check(lib, *_ops(D=64, kt=acefa.GGML_BF16)) == 0
+    assert _check(lib, *_ops(D=256)) == 0                      # D = 256: F16 and BF16 K/V
+    assert _check(lib, *_ops(D=256, kt=acefa.GGML_BF16)) == 0
+    assert _check(lib, *_ops(D=256, kt=acefa.GGML_Q8_0)) == -2
 
 
 def test_check_rejects_contract_violations(lib):
@@ -183,6 +186,10 @@ def test_append_entry_validates_before_launch(lib):
     assert call(bad_t, vn, 4096) == -2                # new rows are f32
     bad_s = _td([128, 2, 8, 4], _contig([128, 2, 8, 4], 4), acefa.GGML_F32, ptr=8192)
     assert call(bad_s, vn, 4096) == -3                # one row per (head, set)
+    q2, k2, v2, m2, d2 = _ops(D=256, Hq=32, B=4, Bk=4, nkv=700)
+    kn2 = _td([256, 1, 8, 4], _contig([256, 1, 8, 4], 4), acefa.GGML_F32, ptr=8192)
+    assert lib.acefa_flash_attn_ext_append(r(q2), r(k2), r(v2), r(m2), None, r(d2), 0.06, 0.0, 0.0, 10, r(kn2),
+                                           r(kn2), 4096, None, None, 0) == -3  # D = 256: no fused append
     if not torch.cuda.is_available():
         assert call(kn, vn, 4096) in (-6, -7)         # valid: fails only at the device step
 

@@ -57,6 +57,34 @@ def test_head_dim_64(kv):
     run_case(c)
 
 
+@pytest.mark.parametrize("kv", ["f16", "bf16"])
+def test_head_dim_256(kv):
+    """D = 256 (F16 and BF16 K/V, on this kernel at one CTA per SM): batched
+    decode over cache views with per-set lengths, GQA 2, a prefill-sized node
+    with a causal mask, and sinks / softcap / ALiBi."""
+    c = Case(310, B=4, Hq=8, Hkv=4, n_q=1, n_kv=700, D=256, kv=kv, max_seq=1024, s0=1, mask="valid",
+             valid=[700, 333, 64, 65])
+    run_case(c)
+    assert acefa.last_path() == 1
+    c2 = Case(311, B=1, Hq=8, Hkv=4, n_q=200, n_kv=256, D=256, kv=kv, mask="causal")
+    run_case(c2)
+    c3 = Case(312, B=2, Hq=8, Hkv=4, n_q=2, n_kv=300, D=256, kv=kv, mask="random", sinks=True)
+    run_case(c3, max_bias=8.0, softcap=20.0)
+
+
+def test_head_dim_256_refusals():
+    """Q8_0 K/V and the Q prologue are refused at D = 256 (before any launch)."""
+    c = Case(313, B=1, Hq=8, Hkv=4, n_q=1, n_kv=128, D=256, mask="zeros")
+    q8 = acefa.quantize_q8_0(c.k.float())
+    with pytest.raises(acefa.AcefaError) as e:
+        acefa.Op(c.q, q8, q8, mask=c.mask, kv_type=acefa.GGML_Q8_0)()
+    assert e.value.status == -2
+    pro = acefa.RopeNorm(torch.ones(256, device="cuda"), 1e-6, 1.0e6, torch.zeros(1, dtype=torch.int32, device="cuda"))
+    with pytest.raises(acefa.AcefaError) as e:
+        acefa.Op(c.q, c.k, c.v, mask=c.mask, q_prologue=pro)()
+    assert e.value.status == -3
+
+
 @pytest.mark.parametrize("n_q", [2, 5, 6, 20])
 def test_short_query_blocks(n_q):
     """FSQ tokenizer/detokenizer (S=5/6, no mask) and multi row-block units."""

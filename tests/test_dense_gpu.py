@@ -281,3 +281,35 @@ def test_full_size_dit_bf16_sampled_rows():
     cx = Case(42 + 1000 * 4 + 13, B=2, Hq=16, Hkv=16, n_q=S, n_kv=512, kv="bf16", mask=padding_mask((461, 461)),
               m_batch=2)
     run_case(cx, rows=rows)
+
+
+# ---- D = 64 on the tcgen05 path: one 64-dim box per K/V tile, four S k-steps,
+# an N = 64 PV MMA.
+
+@pytest.mark.parametrize("kv", ["f16", "bf16", "q8_0"])
+@pytest.mark.parametrize("S,H,Hkv", [(300, 16, 16), (600, 16, 8)])
+def test_dense_d64_unmasked(kv, S, H, Hkv):
+    c = Case(42 + 6400 + S + H + Hkv, B=2, Hq=H, Hkv=Hkv, n_q=S, n_kv=S, D=64, kv=kv, mask=None)
+    run_case(c)
+
+
+@pytest.mark.parametrize("kv", ["f16", "bf16", "q8_0"])
+@pytest.mark.parametrize("n_q,n_kv", [(129, 130), (333, 1000)])
+def test_dense_d64_ragged_masked(kv, n_q, n_kv):
+    c = Case(42 + 6401 + n_q + n_kv, B=1, Hq=4, Hkv=2, n_q=n_q, n_kv=n_kv, D=64, kv=kv, mask="random")
+    run_case(c)
+
+
+def test_dense_d64_causal_cache_view_and_split_tail():
+    S = 300
+    c = Case(42 + 6402, B=1, Hq=16, Hkv=8, n_q=S, n_kv=512, D=64, max_seq=2560, s0=1,
+             mask=lambda m: causal_mask(m, S))
+    run_case(c)
+    c2 = Case(42 + 6403, B=1, Hq=10, Hkv=10, n_q=4096, n_kv=4096, D=64, mask=None, sinks=True)
+    run_case(c2, rows=[0, 1, 255, 256, 2048, 4095])
+    assert acefa.last_launch_count() == 2  # attention, combine
+
+
+def test_dense_d64_sinks_softcap_alibi():
+    c = Case(42 + 6404, B=2, Hq=8, Hkv=4, n_q=200, n_kv=300, D=64, mask="random", sinks=True)
+    run_case(c, max_bias=8.0, softcap=20.0)

@@ -67,12 +67,13 @@ def _q_case(c, pos_np, w):
     return c
 
 
+@pytest.mark.parametrize("D", [128, 64])
 @pytest.mark.parametrize("mask", [None, "causal"])
-def test_dense_q_prologue(mask):
+def test_dense_q_prologue(mask, D):
     # DiT-like (unmasked) and prefill-like (causal, GQA 2) nodes on the dense path
     Hq, Hkv = (16, 16) if mask is None else (16, 8)
-    c = Case(101, B=2, Hq=Hq, Hkv=Hkv, n_q=300, n_kv=300, mask=mask)
-    w = _weights(128, 1)
+    c = Case(101 + D, B=2, Hq=Hq, Hkv=Hkv, n_q=300, n_kv=300, D=D, mask=mask)
+    w = _weights(D, 1)
     pos = np.tile(np.arange(300, dtype=np.int32) + 1000, 2)  # positions[iq + b * n_q]
     pro = acefa.RopeNorm(w.cuda(), EPS, THETA, torch.from_numpy(pos).cuda())
     got = acefa.Op(c.q, c.k, c.v, mask=c.mask, q_prologue=pro)()
