@@ -88,7 +88,7 @@ struct DecCfg {
     static constexpr int kOffStats  = kOffMerge + kDecRows * kMergeStride * 4;  // m,l per warp per row
     static constexpr int kOffFin    = kOffStats + 2 * kDecWarps * kDecRows * 4;  // merged m,l per row
     static constexpr int kOffBars   = kOffFin + 2 * kDecRows * 4;
-    static constexpr int kNumBars   = 2 * kStages + 2;  // full/empty per stage; cluster ready / done
+    static constexpr int kNumBars   = 2 * kStages;  // full / empty per stage
     static constexpr int kOffMeta   = kOffBars + kNumBars * 8;
     static constexpr int kOffFlags  = kOffMeta + kStages * 16;
     static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
@@ -320,8 +320,6 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
 
     uint64_t     *full_bar  = reinterpret_cast<uint64_t *>(smem + Cfg::kOffBars);
     uint64_t     *empty_bar = full_bar + Cfg::kStages;
-    uint64_t     *peer_rdy  = empty_bar + Cfg::kStages;  // every CTA of the cluster published its partial
-    uint64_t     *peer_done = peer_rdy + 1;              // every CTA of the cluster finished reading this one's
     int4         *meta      = reinterpret_cast<int4 *>(smem + Cfg::kOffMeta);
     volatile int *abort_f   = reinterpret_cast<volatile int *>(smem + Cfg::kOffFlags);
     float        *merge     = reinterpret_cast<float *>(smem + Cfg::kOffMerge);
@@ -338,8 +336,6 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
             mbar_init(&full_bar[i], 1);
             mbar_init(&empty_bar[i], kDecWarps);
         }
-        mbar_init(peer_rdy, C);
-        mbar_init(peer_done, C);
         *abort_f = 0;
         fence_barrier_init();
     }
@@ -349,8 +345,11 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
         __syncthreads();
     }
 
-    // Everything below reads tensors that an earlier kernel may have written.
-    pdl_wait_primary();
+    // The next kernel of the stream may start its own set-up now.  Each role
+    // waits for the previous kernel (pdl_wait_primary) just before its first
+    // read of a tensor that kernel may have written: the address arithmetic
+    // before that reads kernel parameters only and overlaps the previous
+    // kernel's tail.
     pdl_launch_dependents();
 
     const OpDesc   &o   = P.op;
@@ -433,6 +432,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
         };
         const char *kbase = o.k + (int64_t) uc.hk * o.k_nb2 + (int64_t) uc.bk * o.k_nb3;
         const char *vbase = o.v + (int64_t) uc.hk * o.v_nb2 + (int64_t) uc.bk * o.v_nb3;
+        pdl_wait_primary();  // K/V, the mask and the append rows below
         // Fused append: the row is written by the CTA whose range holds its
         // tile, just before that tile's copy is issued (after the earlier
         // tiles' copies, so its latency overlaps them), or after the range's
@@ -573,6 +573,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
         return;
     }
 
+    pdl_wait_primary();  // consumers: Q (and, at the end, the output)
     if constexpr (kQ8) {
         // ======================= consumers, Q8_0 (transposed) ========================
         // S^T = K Q^T and O^T += V^T P^T on mma.sync m16n8k16: the warp's 16 keys
@@ -1235,51 +1236,63 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
     // ---- merge across the cluster and write the output
     // CTA r finishes its share of the head dims (the r-th of C nearly equal
     // ranges of float4 chunks) of every row from all C partials, read from the
-    // peers' shared memory; C == 1 writes them all.
-    const bool cl_ok = C == 1 || [&] {
-        if (threadIdx.x == 0) {
-            for (int k = 0; k < C; ++k) {
-                mbar_arrive_cluster(mapa_shared(smem_u32(peer_rdy), (uint32_t) k));
-            }
-        }
-        // (a peer whose pipeline gave up still arrives, one wait limit or
-        // two later: wait longer than that before giving up here)
-        const uint64_t t_start = globaltimer_ns();
-        while (!mbar_try_wait_cluster(peer_rdy, 0)) {
-            if (globaltimer_ns() - t_start > 4 * P.wait_limit_ns) {
-                atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_PEER);
-                return false;
-            }
-        }
-        return true;
-    }();
+    // peers' shared memory; C == 1 writes them all.  Two phases of the
+    // hardware cluster barrier order it: every partial is published before any
+    // CTA reads, and every read is done before any CTA exits (this CTA arrives
+    // once its reads have returned, then stores, then waits).  Every CTA
+    // reaches both phases: each wait of the pipeline before them is bounded,
+    // and the producer warps have exited.
+    if (C > 1) {
+        cluster_arrive();
+        cluster_wait();
+    }
     // this CTA's float4 chunks of every row: [ch0, ch1) of the row's D / 4
     const int      ch0    = r * (D / 4) / C;
     const int      chunks = (r + 1) * (D / 4) / C - ch0;
     const uint32_t fin_a  = smem_u32(s_fin);
     const uint32_t mrg_a  = smem_u32(merge);
-    for (int idx = threadIdx.x; cl_ok && idx < kDecRows * chunks; idx += kDecWarps * 32) {
+    constexpr int  kItems = (kDecRows * (D / 4) + kDecWarps * 32 - 1) / (kDecWarps * 32);  // per thread at C == 1
+    constexpr int  kMaxC  = ACEFA_DEC_MAX_CLUSTER < kDecMaxCluster ? ACEFA_DEC_MAX_CLUSTER : kDecMaxCluster;
+    float4         res[kItems];
+    char          *res_dp[kItems];
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        const int idx = (int) threadIdx.x + it * kDecWarps * 32;
+        res_dp[it]    = nullptr;
         const int row = idx / chunks;
         const int d   = (ch0 + idx % chunks) * 4;
-        if (row >= uc.rows) {
+        if (idx >= kDecRows * chunks || row >= uc.rows) {
             continue;
         }
-        float mk[kDecMaxCluster], lk[kDecMaxCluster];
-        float mx = -INFINITY;
+        // every part's statistics and values requested before any is used:
+        // one round trip of distributed shared memory, not two
+        float  mk[kMaxC], lk[kMaxC];
+        float4 vk[kMaxC];
 #pragma unroll
-        for (int k = 0; k < kDecMaxCluster; ++k) {
+        for (int k = 0; k < kMaxC; ++k) {
             mk[k] = -INFINITY;
             lk[k] = 0.0f;
+            vk[k] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (k < C) {
-                mk[k] = C == 1 ? s_fin[row] : ld_cluster_f32(mapa_shared(fin_a + 4 * row, (uint32_t) k));
-                lk[k] = C == 1 ? s_fin[kDecRows + row]
-                               : ld_cluster_f32(mapa_shared(fin_a + 4 * (kDecRows + row), (uint32_t) k));
-                mx    = fmaxf(mx, mk[k]);
+                if (C == 1) {
+                    mk[k] = s_fin[row];
+                    lk[k] = s_fin[kDecRows + row];
+                    vk[k] = *reinterpret_cast<const float4 *>(&merge[row * Cfg::kMergeStride + d]);
+                } else {
+                    mk[k] = ld_cluster_f32(mapa_shared(fin_a + 4 * row, (uint32_t) k));
+                    lk[k] = ld_cluster_f32(mapa_shared(fin_a + 4 * (kDecRows + row), (uint32_t) k));
+                    vk[k] = ld_cluster_f32x4(mapa_shared(mrg_a + 4 * (row * Cfg::kMergeStride + d), (uint32_t) k));
+                }
             }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kMaxC; ++k) {
+            mx = fmaxf(mx, mk[k]);
         }
         float l = 0.0f;
 #pragma unroll
-        for (int k = 0; k < kDecMaxCluster; ++k) {
+        for (int k = 0; k < kMaxC; ++k) {
             mk[k] = mk[k] == -INFINITY ? 0.0f : fast_exp2(mk[k] - mx);  // now the part's weight
             l += lk[k] * mk[k];
         }
@@ -1298,20 +1311,28 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
         const float inv = l == 0.0f ? 0.0f : fs / l;
         float4      acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int k = 0; k < kDecMaxCluster; ++k) {
+        for (int k = 0; k < kMaxC; ++k) {
             if (k < C) {
-                const uint32_t a = mrg_a + 4 * (row * Cfg::kMergeStride + d);
-                const float4   v = C == 1 ? *reinterpret_cast<const float4 *>(&merge[row * Cfg::kMergeStride + d])
-                                          : ld_cluster_f32x4(mapa_shared(a, (uint32_t) k));
-                acc.x += mk[k] * v.x;
-                acc.y += mk[k] * v.y;
-                acc.z += mk[k] * v.z;
-                acc.w += mk[k] * v.w;
+                acc.x += mk[k] * vk[k].x;
+                acc.y += mk[k] * vk[k].y;
+                acc.z += mk[k] * vk[k].z;
+                acc.w += mk[k] * vk[k].w;
             }
         }
-        acc      = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        char *dp = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
-                   (int64_t) uc.b * o.d_nb3;
+        res[it]    = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        res_dp[it] = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
+                     (int64_t) uc.b * o.d_nb3;
+    }
+    if (C > 1) {
+        cluster_arrive();  // this CTA's reads of the peers' partials have returned
+    }
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        char *dp = res_dp[it];
+        if (!dp) {
+            continue;
+        }
+        const float4 acc = res[it];
         if (o.d_nb0 == 4 && (reinterpret_cast<uintptr_t>(dp) & 15u) == 0) {
             // mirrors are congruent to dst modulo 16 B
             *reinterpret_cast<float4 *>(dp) = acc;
@@ -1334,22 +1355,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
         __threadfence_system();
     }
     if (C > 1) {
-        // This CTA's partial must stay readable until every peer is done.
-        named_bar_sync(1, kDecWarps * 32);
-        if (threadIdx.x == 0) {
-            for (int k = 0; k < C; ++k) {
-                mbar_arrive_cluster(mapa_shared(smem_u32(peer_done), (uint32_t) k));
-            }
-            // longer than any peer can still be reading (its pipeline, its
-            // own ready wait, then a few microseconds of loads)
-            const uint64_t t_start = globaltimer_ns();
-            while (!mbar_try_wait_cluster(peer_done, 0)) {
-                if (globaltimer_ns() - t_start > 8 * P.wait_limit_ns) {
-                    atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_PEER);
-                    break;
-                }
-            }
-        }
+        cluster_wait();  // this CTA's partial stays readable until every peer is done
     }
 }
 
