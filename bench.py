@@ -1384,6 +1384,9 @@ def run_dense_workload(args):
     if args.workload == "config5":
         emit({"workload": args.workload, **config5(device, stream, gen=args.c5_gen)})
         return 0
+    if args.workload == "cfg_combine":
+        emit({"workload": args.workload, **cfg_combine_step(device, stream, iters=args.steps)})
+        return 0
     if args.workload == "config1":
         # 64 distinct Qwen3-0.6B decode ops back to back
         # (also the ncu profiling case of the op)
@@ -1447,7 +1450,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (36 = the headline stack)")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"])
     ap.add_argument("--workload", default="decode4b",
-                    help="decode4b (headline), config1, config5, dit6000_prologue, or one dense op: " + ", ".join(DENSE_WORKLOADS))
+                    help="decode4b (headline), config1, config5, dit6000_prologue, cfg_combine, or one dense op: " +
+                         ", ".join(DENSE_WORKLOADS))
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 end-to-end workload extra")
     ap.add_argument("--c5-gen", type=int, default=C5_GEN, help="config-5 decode steps (2000 = the BASELINE workload)")
     ap.add_argument("--mask-rule", action="store_true",
