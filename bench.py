@@ -701,7 +701,8 @@ def cfg_combine_step(device, stream, n=8, reps=64, iters=10):
     del bufs, outs
     return {"us_per_launch": round(us, 3), "gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "algo_bytes_per_launch": algo},
+                         "frac": round(gbs / peak, 4), "algo_bytes_per_launch": algo,
+                         "traffic": read_traffic("cfg_logit_combine_kernel")},
             "d2h_bytes_per_step": {"reference": 2 * n * out_v * 4, "device_combine": n * (cnt + 1) * 4},
             **res,
             "note": "64 distinct 4.2 MB logit buffers back to back in one CUDA graph; host steps by wall "
