@@ -65,17 +65,60 @@ def read_traffic(kernel_key):
 
 
 class ClockSampler:
+    """SM clock and clock-event reasons of this rank's GPU sampled DURING the
+    timed region: an NVML polling thread (every 2 ms; reads only), so even a
+    timed region of a few tens of milliseconds gets samples.  Falls back to
+    `nvidia-smi -lms 200` when NVML is unavailable."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.rows = []
+        self.nvml = None
+        self.handle = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(index).uuid)
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.nvml = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nvml = None
         self.tmpdir = tempfile.mkdtemp(prefix="acefa_clocks_")
         self.path = os.path.join(self.tmpdir, f"clocks_rank{index}.csv")
 
+    def _poll(self):
+        import time
+
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop:
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                bits = int(get_reasons(self.handle))
+                self.rows.append((mhz, self.max_mhz, [n for n, b in self.REASONS.items() if bits & b]))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
     def __enter__(self):
+        if self.nvml is not None:
+            import threading
+
+            self.stop = False
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -86,6 +129,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        if self.nvml is not None:
+            self.stop = True
+            self.thread.join(timeout=5)
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -95,23 +142,25 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
-            return None
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
-            except ValueError:
-                continue
+        rows = list(self.rows)
+        if self.nvml is None:
+            if self.proc is None or not os.path.exists(self.path):
+                return None
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]),
+                                 [names[i] for i, v in enumerate(parts[5:9]) if v.lower() == "active"]))
+                except ValueError:
+                    continue
         if not rows:
             return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        reasons = sorted({n for _, _, r in rows for n in r})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # -------------------------------------------------------------------------
@@ -377,7 +426,7 @@ def run_ours(args):
             "config": config_dict(args),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": read_traffic(f"fa_decode_kernel_{args.kv}_d128"),
-                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": f"fa_decode_kernel<{args.kv},128> (+combine)",
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": f"fa_decode_kernel<{args.kv},128>",
                          "algo_bytes_per_launch": per_op},
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h),
