@@ -81,7 +81,13 @@ struct DecCfg {
     static constexpr int  kStages     = kQ8 ? ACEFA_Q8_STAGES : kDecStages;
     static_assert(kQ8 || kStageBytes % 1024 == 0, "TMA stages must stay 1 KB aligned");
     static constexpr int  kThreads     = (kDecWarps + 1) * 32;  // 4 consumer warps + the producer
-    static constexpr int  kMergeStride = D + 8;                   // floats per merge row (bank spread)
+    // Merge rows: F16/BF16 D + 8 floats.  Q8_0 threads write dims 16g + k
+    // (g = lane / 4) of rows 2c + e: with a plain layout 16g aliases on two
+    // banks (a 16-way conflict), so every 16-dim group is skewed by one float
+    // (merge_at) and the row stride is 4 (mod 16) -- the 32 lanes of a store
+    // then hit 32 banks.
+    static constexpr int  kMergeStride = kQ8 ? ((D + D / 16 - 4 + 15) / 16) * 16 + 4 : D + 8;
+    __device__ static int merge_at(int row, int dim) { return row * kMergeStride + (kQ8 ? dim + (dim >> 4) : dim); }
     // shared memory carve-up (offsets from the 1024-B aligned base)
     static constexpr int kOffStages = 0;
     static constexpr int kOffMerge  = kStages * kStageBytes;
@@ -870,7 +876,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
                         for (int e = 0; e < 4; ++e) {
                             const int   row = 2 * c + (e & 1);
                             const int   dim = vd0 + (e >> 1) * (D / 16) + mt;
-                            float      *mp  = &merge[row * Cfg::kMergeStride + dim];
+                            float      *mp  = &merge[Cfg::merge_at(row, dim)];
                             const float v   = oacc[mt][e] * fac[e & 1];
                             *mp             = t == 0 ? v : *mp + v;
                         }
@@ -1206,7 +1212,7 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
                         const int j = bb * NTB + jj;
     #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            float      *mp = &merge[(g + 8 * (e >> 1)) * Cfg::kMergeStride + out_dim(j, e)];
+                            float      *mp = &merge[Cfg::merge_at(g + 8 * (e >> 1), out_dim(j, e))];
                             const float v  = oacc[j][e] * fac[e >> 1];
                             *mp            = t == 0 ? v : *mp + v;
                         }
@@ -1277,11 +1283,22 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
                 if (C == 1) {
                     mk[k] = s_fin[row];
                     lk[k] = s_fin[kDecRows + row];
-                    vk[k] = *reinterpret_cast<const float4 *>(&merge[row * Cfg::kMergeStride + d]);
+                    if constexpr (kQ8) {  // four dims of one skewed group: contiguous, 4-B aligned
+                        const float *mp = &merge[Cfg::merge_at(row, d)];
+                        vk[k]           = make_float4(mp[0], mp[1], mp[2], mp[3]);
+                    } else {
+                        vk[k] = *reinterpret_cast<const float4 *>(&merge[Cfg::merge_at(row, d)]);
+                    }
                 } else {
                     mk[k] = ld_cluster_f32(mapa_shared(fin_a + 4 * row, (uint32_t) k));
                     lk[k] = ld_cluster_f32(mapa_shared(fin_a + 4 * (kDecRows + row), (uint32_t) k));
-                    vk[k] = ld_cluster_f32x4(mapa_shared(mrg_a + 4 * (row * Cfg::kMergeStride + d), (uint32_t) k));
+                    const uint32_t a = mapa_shared(mrg_a + 4 * Cfg::merge_at(row, d), (uint32_t) k);
+                    if constexpr (kQ8) {
+                        vk[k] = make_float4(ld_cluster_f32(a), ld_cluster_f32(a + 4), ld_cluster_f32(a + 8),
+                                            ld_cluster_f32(a + 12));
+                    } else {
+                        vk[k] = ld_cluster_f32x4(a);
+                    }
                 }
             }
         }
