@@ -1341,7 +1341,9 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
                      (int64_t) uc.b * o.d_nb3;
     }
     if (C > 1) {
-        cluster_arrive();  // this CTA's reads of the peers' partials have returned
+        // this CTA's reads of the peers' partials have returned (their values
+        // are in res): the arrive needs no memory ordering
+        cluster_arrive_relaxed();
     }
 #pragma unroll
     for (int it = 0; it < kItems; ++it) {
