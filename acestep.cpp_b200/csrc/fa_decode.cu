@@ -1258,59 +1258,23 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
     const uint32_t fin_a  = smem_u32(s_fin);
     const uint32_t mrg_a  = smem_u32(merge);
     constexpr int  kItems = (kDecRows * (D / 4) + kDecWarps * 32 - 1) / (kDecWarps * 32);  // per thread at C == 1
+    static_assert((kDecRows * ((D / 4 + 1) / 2) + kDecWarps * 32 - 1) / (kDecWarps * 32) <= kItems, "item count");
     constexpr int  kMaxC  = ACEFA_DEC_MAX_CLUSTER < kDecMaxCluster ? ACEFA_DEC_MAX_CLUSTER : kDecMaxCluster;
     float4         res[kItems];
     char          *res_dp[kItems];
-#pragma unroll
-    for (int it = 0; it < kItems; ++it) {
-        const int idx = (int) threadIdx.x + it * kDecWarps * 32;
-        res_dp[it]    = nullptr;
-        const int row = idx / chunks;
-        const int d   = (ch0 + idx % chunks) * 4;
-        if (idx >= kDecRows * chunks || row >= uc.rows) {
-            continue;
-        }
-        // every part's statistics and values requested before any is used:
-        // one round trip of distributed shared memory, not two
-        float  mk[kMaxC], lk[kMaxC];
-        float4 vk[kMaxC];
-#pragma unroll
-        for (int k = 0; k < kMaxC; ++k) {
-            mk[k] = -INFINITY;
-            lk[k] = 0.0f;
-            vk[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k < C) {
-                if (C == 1) {
-                    mk[k] = s_fin[row];
-                    lk[k] = s_fin[kDecRows + row];
-                    if constexpr (kQ8) {  // four dims of one skewed group: contiguous, 4-B aligned
-                        const float *mp = &merge[Cfg::merge_at(row, d)];
-                        vk[k]           = make_float4(mp[0], mp[1], mp[2], mp[3]);
-                    } else {
-                        vk[k] = *reinterpret_cast<const float4 *>(&merge[Cfg::merge_at(row, d)]);
-                    }
-                } else {
-                    mk[k] = ld_cluster_f32(mapa_shared(fin_a + 4 * row, (uint32_t) k));
-                    lk[k] = ld_cluster_f32(mapa_shared(fin_a + 4 * (kDecRows + row), (uint32_t) k));
-                    const uint32_t a = mapa_shared(mrg_a + 4 * Cfg::merge_at(row, d), (uint32_t) k);
-                    if constexpr (kQ8) {
-                        vk[k] = make_float4(ld_cluster_f32(a), ld_cluster_f32(a + 4), ld_cluster_f32(a + 8),
-                                            ld_cluster_f32(a + 12));
-                    } else {
-                        vk[k] = ld_cluster_f32x4(a);
-                    }
-                }
-            }
-        }
+    // Row r's result from the C parts' statistics (m, l) and values v.
+    auto finish = [&](int it, int row, int d, const float (&mk0)[kMaxC], const float (&lk)[kMaxC],
+                      const float4 (&vk)[kMaxC]) {
+        float mk[kMaxC];
         float mx = -INFINITY;
 #pragma unroll
         for (int k = 0; k < kMaxC; ++k) {
-            mx = fmaxf(mx, mk[k]);
+            mx = fmaxf(mx, mk0[k]);
         }
         float l = 0.0f;
 #pragma unroll
         for (int k = 0; k < kMaxC; ++k) {
-            mk[k] = mk[k] == -INFINITY ? 0.0f : fast_exp2(mk[k] - mx);  // now the part's weight
+            mk[k] = mk0[k] == -INFINITY ? 0.0f : fast_exp2(mk0[k] - mx);  // the part's weight
             l += lk[k] * mk[k];
         }
         int iq, hq;
@@ -1339,6 +1303,88 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, 
         res[it]    = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         res_dp[it] = o.dst + (int64_t) d * o.d_nb0 + (int64_t) hq * o.d_nb1 + (int64_t) iq * o.d_nb2 +
                      (int64_t) uc.b * o.d_nb3;
+    };
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+        res_dp[it] = nullptr;
+    }
+    if (C == 1) {
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+            const int idx = (int) threadIdx.x + it * kDecWarps * 32;
+            const int row = idx / chunks;
+            const int d   = (ch0 + idx % chunks) * 4;
+            if (idx >= kDecRows * chunks || row >= uc.rows) {
+                continue;
+            }
+            float  mk[kMaxC], lk[kMaxC];
+            float4 vk[kMaxC];
+#pragma unroll
+            for (int k = 0; k < kMaxC; ++k) {
+                mk[k] = k == 0 ? s_fin[row] : -INFINITY;
+                lk[k] = k == 0 ? s_fin[kDecRows + row] : 0.0f;
+                vk[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if constexpr (kQ8) {  // four dims of one skewed group: contiguous, 4-B aligned
+                const float *mp = &merge[Cfg::merge_at(row, d)];
+                vk[0]           = make_float4(mp[0], mp[1], mp[2], mp[3]);
+            } else {
+                vk[0] = *reinterpret_cast<const float4 *>(&merge[Cfg::merge_at(row, d)]);
+            }
+            finish(it, row, d, mk, lk, vk);
+        }
+    } else {
+        // The parts' values for this thread's items are requested first, then
+        // each part's row statistics once per (part, row) into a table in the
+        // (now idle) first pipeline stage, so both kinds of distributed
+        // shared-memory loads are in flight together and no statistic is
+        // fetched more than once.
+        constexpr int kItemsC = (kDecRows * ((D / 4 + 1) / 2) + kDecWarps * 32 - 1) / (kDecWarps * 32);
+        float4        vk[kItemsC][kMaxC];
+#pragma unroll
+        for (int it = 0; it < kItemsC; ++it) {
+            const int idx = (int) threadIdx.x + it * kDecWarps * 32;
+            const int row = idx / chunks;
+            const int d   = (ch0 + idx % chunks) * 4;
+            const bool live = idx < kDecRows * chunks && row < uc.rows;
+#pragma unroll
+            for (int k = 0; k < kMaxC; ++k) {
+                vk[it][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live && k < C) {
+                    const uint32_t a = mapa_shared(mrg_a + 4 * Cfg::merge_at(row, d), (uint32_t) k);
+                    if constexpr (kQ8) {
+                        vk[it][k] = make_float4(ld_cluster_f32(a), ld_cluster_f32(a + 4), ld_cluster_f32(a + 8),
+                                                ld_cluster_f32(a + 12));
+                    } else {
+                        vk[it][k] = ld_cluster_f32x4(a);
+                    }
+                }
+            }
+        }
+        float2 *stab = reinterpret_cast<float2 *>(smem + Cfg::kOffStages);  // [C][kDecRows] (m, l)
+        for (int t = threadIdx.x; t < C * kDecRows; t += kDecWarps * 32) {
+            const int k = t / kDecRows, row = t % kDecRows;
+            stab[t]     = make_float2(ld_cluster_f32(mapa_shared(fin_a + 4 * row, (uint32_t) k)),
+                                      ld_cluster_f32(mapa_shared(fin_a + 4 * (kDecRows + row), (uint32_t) k)));
+        }
+        named_bar_sync(1, kDecWarps * 32);
+#pragma unroll
+        for (int it = 0; it < kItemsC; ++it) {
+            const int idx = (int) threadIdx.x + it * kDecWarps * 32;
+            const int row = idx / chunks;
+            const int d   = (ch0 + idx % chunks) * 4;
+            if (idx >= kDecRows * chunks || row >= uc.rows) {
+                continue;
+            }
+            float mk[kMaxC], lk[kMaxC];
+#pragma unroll
+            for (int k = 0; k < kMaxC; ++k) {
+                const float2 st = k < C ? stab[k * kDecRows + row] : make_float2(-INFINITY, 0.0f);
+                mk[k]           = st.x;
+                lk[k]           = st.y;
+            }
+            finish(it, row, d, mk, lk, vk[it]);
+        }
     }
     if (C > 1) {
         // this CTA's reads of the peers' partials have returned (their values
