@@ -245,7 +245,8 @@ void set_scalars(OpDesc &o, float scale, float max_bias, float softcap) {
 // unit's cluster resident at once, so the op runs in one wave; units beyond
 // that run one CTA each.  A function of shapes and the device only.
 struct DecodePlan {
-    int n_rb, units, tpu, cluster;
+    int  n_rb, units, tpu, cluster;
+    bool wide;
 };
 
 DecodePlan plan_decode(const OpDesc &o, bool prologue) {
@@ -255,7 +256,8 @@ DecodePlan plan_decode(const OpDesc &o, bool prologue) {
     p.n_rb         = (rows + R - 1) / R;
     p.units        = o.B * o.Hkv * p.n_rb;
     p.tpu          = (o.n_kv + kDecBN - 1) / kDecBN;
-    p.cluster      = decode_cluster(o.kv_type, o.D, prologue, p.units, p.tpu);
+    p.wide         = decode_wide(o.kv_type, o.D, p.tpu, p.units);
+    p.cluster      = decode_cluster(o.kv_type, o.D, prologue, p.units, p.tpu, p.wide);
     return p;
 }
 
@@ -542,6 +544,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
     L.p.units          = plan.units;
     L.p.tiles_per_unit = plan.tpu;
     L.p.cluster        = plan.cluster;
+    L.p.wide           = plan.wide;
     if (app) {
         L.p.k_new      = app->k_new;
         L.p.v_new      = app->v_new;

@@ -64,7 +64,11 @@ constexpr int kMetaTerm = 3;
 constexpr uint16_t kHalfNegInf = 0xFC00u;
 constexpr float    kQ8RescaleLog2 = 8.0f;  // Q8_0 consumer: rescale when the max grows by > 2^8
 
-template <int KV_TYPE, int D>
+// WIDE (Q8_0, D = 128): three CTAs per SM with three stages each instead of
+// two with four -- more warps to hide the dequantisation's latency; chosen by
+// decode_wide for ops with many long units (elsewhere the shallower pipeline
+// and the larger cluster merge cost more than the extra warps gain).
+template <int KV_TYPE, int D, bool WIDE = false>
 struct DecCfg {
     static constexpr bool kQ8         = KV_TYPE == ACEFA_TYPE_Q8_0;
     static constexpr bool kBF16       = KV_TYPE == ACEFA_TYPE_BF16;
@@ -78,7 +82,7 @@ struct DecCfg {
     static constexpr int  kTile       = kQ8 ? (kDecBN * kRowBytes + 16 + 15) / 16 * 16 : kDecBN * D * 2;
     static constexpr int  kMaskBytes  = kDecRows * kDecBN * 2;  // up to 16 mask rows x 64 keys (f16)
     static constexpr int  kStageBytes = 2 * kTile + kMaskBytes;
-    static constexpr int  kStages     = kQ8 ? ACEFA_Q8_STAGES : kDecStages;
+    static constexpr int  kStages     = kQ8 ? (WIDE ? 3 : ACEFA_Q8_STAGES) : kDecStages;
     static_assert(kQ8 || kStageBytes % 1024 == 0, "TMA stages must stay 1 KB aligned");
     static constexpr int  kThreads     = (kDecWarps + 1) * 32;  // 4 consumer warps + the producer
     // Merge rows: F16/BF16 D + 8 floats.  Q8_0 threads write dims 16g + k
@@ -99,7 +103,7 @@ struct DecCfg {
     static constexpr int kOffFlags  = kOffMeta + kStages * 16;
     static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
     // D = 256: a 66 KB stage, one CTA per SM
-    static constexpr int kCtasPerSm = D > 128 ? 1 : (kQ8 ? ACEFA_Q8_CTAS : 2);
+    static constexpr int kCtasPerSm = D > 128 ? 1 : (kQ8 ? (WIDE ? 3 : ACEFA_Q8_CTAS) : 2);
     static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024, "CTAs per SM exceed shared memory");
     static_assert(kSmemBytes <= 232448, "stages exceed the 227 KB per CTA");
     static_assert(D <= 128 || !kQ8, "D = 256 serves F16 and BF16 K/V");
@@ -310,11 +314,11 @@ __device__ __forceinline__ void append_store(const DecodeParams &P, int64_t pr, 
 
 // PRO: the instance that applies the QK-norm + RoPE prologues (Q rows, the
 // appended K row); the others carry none of that code.
-template <int KV_TYPE, int D, bool PRO>
-__global__ void __launch_bounds__(DecCfg<KV_TYPE, D>::kThreads, DecCfg<KV_TYPE, D>::kCtasPerSm)
+template <int KV_TYPE, int D, bool PRO, bool WIDE = false>
+__global__ void __launch_bounds__(DecCfg<KV_TYPE, D, WIDE>::kThreads, DecCfg<KV_TYPE, D, WIDE>::kCtasPerSm)
     fa_decode_kernel(const __grid_constant__ DecodeParams P, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
-    using Cfg            = DecCfg<KV_TYPE, D>;
+    using Cfg            = DecCfg<KV_TYPE, D, WIDE>;
     constexpr bool kQ8   = Cfg::kQ8;
     constexpr bool kBF16 = Cfg::kBF16;
     constexpr int  KS    = D / 16;      // k-steps over the head dim
@@ -1439,18 +1443,18 @@ struct InstInfo {
 constexpr int kMaxDev = 64;
 std::mutex    g_inst_mutex;
 
-template <int KV_TYPE, int D, bool PRO>
+template <int KV_TYPE, int D, bool PRO, bool WIDE>
 const InstInfo &inst_info(int dev) {
     static InstInfo info[kMaxDev];
     static bool     done[kMaxDev];
-    using Cfg = DecCfg<KV_TYPE, D>;
+    using Cfg = DecCfg<KV_TYPE, D, WIDE>;
     std::lock_guard<std::mutex> lock(g_inst_mutex);
     InstInfo &in = info[dev];
     if (done[dev]) {
         return in;
     }
     done[dev] = true;
-    auto k    = fa_decode_kernel<KV_TYPE, D, PRO>;
+    auto k    = fa_decode_kernel<KV_TYPE, D, PRO, WIDE>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess) {
         return in;
     }
@@ -1487,34 +1491,34 @@ const InstInfo &inst_info(int dev) {
 template <int KV_TYPE, int D>
 constexpr bool kHasPro = D <= 128;
 
-template <int KV_TYPE, int D>
+template <int KV_TYPE, int D, bool WIDE>
 const InstInfo &pro_info(bool pro, int dev) {
     if constexpr (kHasPro<KV_TYPE, D>) {
         if (pro) {
-            return inst_info<KV_TYPE, D, true>(dev);
+            return inst_info<KV_TYPE, D, true, WIDE>(dev);
         }
     }
-    return inst_info<KV_TYPE, D, false>(dev);
+    return inst_info<KV_TYPE, D, false, WIDE>(dev);
 }
 
-template <int KV_TYPE, int D>
+template <int KV_TYPE, int D, bool WIDE = false>
 cudaError_t launch_impl(const DecodeLaunch &L, cudaStream_t s, int *launches) {
-    using Cfg      = DecCfg<KV_TYPE, D>;
+    using Cfg      = DecCfg<KV_TYPE, D, WIDE>;
     const bool pro = L.p.op.qp.on || L.p.kp.on;
     if (pro && !kHasPro<KV_TYPE, D>) {
         return cudaErrorInvalidValue;
     }
-    auto kern = fa_decode_kernel<KV_TYPE, D, false>;
+    auto kern = fa_decode_kernel<KV_TYPE, D, false, WIDE>;
     if constexpr (kHasPro<KV_TYPE, D>) {
         if (pro) {
-            kern = fa_decode_kernel<KV_TYPE, D, true>;
+            kern = fa_decode_kernel<KV_TYPE, D, true, WIDE>;
         }
     }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
         return cudaErrorInvalidDevice;
     }
-    const InstInfo &in = pro_info<KV_TYPE, D>(pro, dev);
+    const InstInfo &in = pro_info<KV_TYPE, D, WIDE>(pro, dev);
     if (!in.ok) {
         return cudaErrorInvalidConfiguration;
     }
@@ -1544,13 +1548,13 @@ cudaError_t launch_impl(const DecodeLaunch &L, cudaStream_t s, int *launches) {
 
 // The largest cluster size whose clusters for all `units` are resident at
 // once (so the op runs in one wave), or 1.
-template <int KV_TYPE, int D>
+template <int KV_TYPE, int D, bool WIDE = false>
 int cluster_for(bool pro, int units, int tiles_per_unit) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
         return 1;
     }
-    const InstInfo &in   = pro_info<KV_TYPE, D>(pro, dev);
+    const InstInfo &in   = pro_info<KV_TYPE, D, WIDE>(pro, dev);
     int             best = 1;
     for (int c = 2; c <= kDecMaxCluster && in.ok; ++c) {
         if (c <= tiles_per_unit && units <= in.active[c]) {
@@ -1568,6 +1572,7 @@ cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches) 
     if (t == ACEFA_TYPE_F16 && D == 64) return launch_impl<ACEFA_TYPE_F16, 64>(L, s, launches);
     if (t == ACEFA_TYPE_BF16 && D == 128) return launch_impl<ACEFA_TYPE_BF16, 128>(L, s, launches);
     if (t == ACEFA_TYPE_BF16 && D == 64) return launch_impl<ACEFA_TYPE_BF16, 64>(L, s, launches);
+    if (t == ACEFA_TYPE_Q8_0 && D == 128 && L.p.wide) return launch_impl<ACEFA_TYPE_Q8_0, 128, true>(L, s, launches);
     if (t == ACEFA_TYPE_Q8_0 && D == 128) return launch_impl<ACEFA_TYPE_Q8_0, 128>(L, s, launches);
     if (t == ACEFA_TYPE_Q8_0 && D == 64) return launch_impl<ACEFA_TYPE_Q8_0, 64>(L, s, launches);
     if (t == ACEFA_TYPE_F16 && D == 256) return launch_impl<ACEFA_TYPE_F16, 256>(L, s, launches);
@@ -1575,8 +1580,11 @@ cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches) 
     return cudaErrorInvalidValue;
 }
 
-int decode_cluster(int kv_type, int D, bool pro, int units, int tiles_per_unit) {
+int decode_cluster(int kv_type, int D, bool pro, int units, int tiles_per_unit, bool wide) {
     const int u = units, t = tiles_per_unit;
+    if (wide && kv_type == ACEFA_TYPE_Q8_0 && D == 128) {
+        return cluster_for<ACEFA_TYPE_Q8_0, 128, true>(pro, u, t);
+    }
     if (kv_type == ACEFA_TYPE_F16) {
         return D == 128 ? cluster_for<ACEFA_TYPE_F16, 128>(pro, u, t)
                         : (D == 64 ? cluster_for<ACEFA_TYPE_F16, 64>(pro, u, t) : cluster_for<ACEFA_TYPE_F16, 256>(pro, u, t));

@@ -123,6 +123,7 @@ struct DecodeParams {
     int     units;           // B * Hkv * n_rb
     int     tiles_per_unit;  // ceil(n_kv / kDecBN)
     int     cluster;         // CTAs per unit (grid = units * cluster)
+    int     wide;            // Q8_0: the three-CTAs-per-SM instance (decode_wide)
     // Fused KV-cache append (acefa_flash_attn_ext_append), or all null: the
     // new K/V row of (kv head h, set s) is f32 at k_new + h*kn_nb2 + s*kn_nb3
     // and goes into cache row append_pos[s] before that row is read.
@@ -143,7 +144,15 @@ cudaError_t launch_decode(const DecodeLaunch &L, cudaStream_t s, int *launches);
 // CTAs per unit for the decode kernel of these operands on the current
 // device: the largest size (<= kDecMaxCluster, <= the unit's key tiles)
 // whose clusters for all `units` are resident at once; 1 otherwise.
-int         decode_cluster(int kv_type, int D, bool prologue, int units, int tiles_per_unit);
+int         decode_cluster(int kv_type, int D, bool prologue, int units, int tiles_per_unit, bool wide);
+// Q8_0 ops of at least kDecWideUnits units of at least kDecWideTiles key tiles
+// run three CTAs per SM (measured crossovers: 16 sets x 8 heads gain from 1280
+// keys on; 8 sets, 2 sets and shorter windows lose to the shallower pipeline)
+constexpr int kDecWideTiles = 20;
+constexpr int kDecWideUnits = 128;
+inline bool   decode_wide(int kv_type, int D, int tiles_per_unit, int units) {
+    return kv_type == ACEFA_TYPE_Q8_0 && D == 128 && tiles_per_unit >= kDecWideTiles && units >= kDecWideUnits;
+}
 
 // ------------------------------------------------------------------ dense
 // tcgen05 kernel for query-heavy nodes (LM prefill, DiT self/cross, encoders):
