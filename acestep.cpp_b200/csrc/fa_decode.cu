@@ -53,6 +53,13 @@
 #ifndef ACEFA_Q8_CTAS
 #define ACEFA_Q8_CTAS 2
 #endif
+// The same for the wide Q8_0 instance (decode_wide).
+#ifndef ACEFA_Q8W_STAGES
+#define ACEFA_Q8W_STAGES 3
+#endif
+#ifndef ACEFA_Q8W_CTAS
+#define ACEFA_Q8W_CTAS 3
+#endif
 
 namespace acefa {
 
@@ -82,7 +89,7 @@ struct DecCfg {
     static constexpr int  kTile       = kQ8 ? (kDecBN * kRowBytes + 16 + 15) / 16 * 16 : kDecBN * D * 2;
     static constexpr int  kMaskBytes  = kDecRows * kDecBN * 2;  // up to 16 mask rows x 64 keys (f16)
     static constexpr int  kStageBytes = 2 * kTile + kMaskBytes;
-    static constexpr int  kStages     = kQ8 ? (WIDE ? 3 : ACEFA_Q8_STAGES) : kDecStages;
+    static constexpr int  kStages     = kQ8 ? (WIDE ? ACEFA_Q8W_STAGES : ACEFA_Q8_STAGES) : kDecStages;
     static_assert(kQ8 || kStageBytes % 1024 == 0, "TMA stages must stay 1 KB aligned");
     static constexpr int  kThreads     = (kDecWarps + 1) * 32;  // 4 consumer warps + the producer
     // Merge rows: F16/BF16 D + 8 floats.  Q8_0 threads write dims 16g + k
@@ -103,7 +110,7 @@ struct DecCfg {
     static constexpr int kOffFlags  = kOffMeta + kStages * 16;
     static constexpr int kSmemBytes = kOffFlags + 16 + 1024;  // + alignment slack
     // D = 256: a 66 KB stage, one CTA per SM
-    static constexpr int kCtasPerSm = D > 128 ? 1 : (kQ8 ? (WIDE ? 3 : ACEFA_Q8_CTAS) : 2);
+    static constexpr int kCtasPerSm = D > 128 ? 1 : (kQ8 ? (WIDE ? ACEFA_Q8W_CTAS : ACEFA_Q8_CTAS) : 2);
     static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024, "CTAs per SM exceed shared memory");
     static_assert(kSmemBytes <= 232448, "stages exceed the 227 KB per CTA");
     static_assert(D <= 128 || !kQ8, "D = 256 serves F16 and BF16 K/V");
