@@ -84,3 +84,10 @@ def test_append_refuses_dense_shapes():
     with pytest.raises(acefa.AcefaError):
         acefa.Op(c.q, c.k, c.v, k_new=k_new, v_new=k_new.clone(),
                  pos=torch.zeros(1, dtype=torch.int64, device="cuda"))()
+
+
+def test_append_q8_0_three_ctas_per_sm():
+    """16 sets x 8 heads over 1536 keys: the Q8_0 instance with three CTAs per
+    SM (decode_wide), new rows in different tiles and CTA ranges of each set."""
+    pos = [100 + 89 * b for b in range(16)]
+    _run("q8_0", B=16, Hq=32, Hkv=8, n_kv=1536, pos=pos, max_seq=2048, seed=83)
