@@ -1084,6 +1084,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
             const int j0 = j * kDenseBN;
+            // Fast tiles (no mask values other than 0 / -inf, no softcap,
+            // positive scale): max of the raw scores, then exp2(s * c - m) in
+            // one FMA + ex2 per score.  Binary-mask and ragged tiles use a
+            // 128-bit visibility mask per row, built (from the mask in global
+            // memory) before the wait for S, so its loads overlap the MMA.
+            // Other tiles rewrite S as finished log2-unit logits in TMEM first.
+            const bool fast    = (!(c & kClsMask) || (c & kClsBinary)) && !general;
+            const bool use_vis = fast && (c & (kClsMask | kClsBounds)) != 0;
+            uint32_t   vis[4]  = {~0u, ~0u, ~0u, ~0u};
+            if (use_vis) {
+                build_visibility(vis, c, mrow, j0, o.n_kv, o.m_ne0, rule, vlo, vhi);
+            }
             ok = mbar_wait_bounded(&s_ready[i], (uint32_t) (cnt & 1), abort_f, P.dev_err, DEVERR_TIMEOUT_MMA,
                                    P.wait_limit_ns);
             ok = __all_sync(0xffffffffu, ok);  // the collectives below need the whole warp
@@ -1091,18 +1103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            // Fast tiles (no mask values other than 0 / -inf, no softcap,
-            // positive scale): max of the raw scores, then exp2(s * c - m) in
-            // one FMA + ex2 per score.  Binary-mask and ragged tiles use a
-            // 128-bit visibility mask per row.  Other tiles rewrite S as
-            // finished log2-unit logits in TMEM first.
-            const bool fast = (!(c & kClsMask) || (c & kClsBinary)) && !general;
             if (fast) {
-                const bool use_vis = (c & (kClsMask | kClsBounds)) != 0;
-                uint32_t   vis[4]  = {~0u, ~0u, ~0u, ~0u};
-                if (use_vis) {
-                    build_visibility(vis, c, mrow, j0, o.n_kv, o.m_ne0, rule, vlo, vhi);
-                }
                 float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 if (__any_sync(0xffffffffu, m_run == -INFINITY)) {
                     // some row has no max yet: classic max pass first
