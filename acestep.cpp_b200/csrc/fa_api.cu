@@ -509,7 +509,12 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         L.p.n_full        = dp.n_full;
         L.p.n_tail        = dp.n_tail;
         L.p.n_split       = dp.n_split;
-        L.p.head_major    = c.op.mask == nullptr && c.op.mg_kind == 0;
+        // (batch, head)-major unit order (a head's pairs in flight together,
+        // sharing its K/V tiles in L2) wherever the pairs' work is uniform:
+        // no mask, or a window / padding rule.  Causal rules and f16 masks
+        // (whose pattern the host does not see) keep the heavy-first order.
+        L.p.head_major    = c.op.mask == nullptr &&
+                         (c.op.mg_kind == 0 || c.op.mg_kind == ACEFA_MASK_WINDOW || c.op.mg_kind == ACEFA_MASK_PADDING);
         L.p.cls           = dp.classify ? static_cast<const uint8_t *>(workspace) : nullptr;
         L.p.cls_out       = dp.classify ? static_cast<uint8_t *>(workspace) : nullptr;
         L.p.part          = dp.n_tail ? reinterpret_cast<float *>(static_cast<char *>(workspace) + dp.cls_bytes)
