@@ -219,3 +219,28 @@ def test_workspace_too_small_is_rejected():
     with pytest.raises(acefa.AcefaError) as e:
         op()
     assert e.value.status == -5
+
+
+@pytest.mark.parametrize("kv", ["f16", "q8_0"])
+def test_very_long_kv_single_set(kv):
+    """Long contexts on the split-KV kernel: 2 sets x 160,000 keys (2,500
+    tiles per unit over clusters of 8), a validity mask cutting each set at a
+    different length."""
+    n = 160_000
+    c = Case(1700, B=2, Hq=16, Hkv=8, n_q=1, n_kv=n, kv=kv, mask="valid", valid=[n, 99_991])
+    run_case(c)
+    assert acefa.last_path() == 1
+
+
+def test_query_heavy_node_past_dense_key_limit():
+    """A prefill-shaped node (256 query rows per K/V head) with more keys than
+    the dense kernel's class table holds (70,000 > 65,536) runs on the split-KV
+    kernel; sampled rows against the oracle."""
+    c = Case(1701, B=1, Hq=2, Hkv=1, n_q=128, n_kv=70_000, mask="random")
+    got = c.gpu()
+    assert acefa.last_path() == 1
+    rows = [0, 1, 63, 64, 127]
+    from test_dense_gpu import oracle_rows
+    want = oracle_rows(c, rows)
+    assert_close(got[:, rows], want, what="70k keys, sampled rows")
+    assert acefa.device_error() == 0
