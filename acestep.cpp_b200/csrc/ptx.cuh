@@ -20,7 +20,8 @@ enum : int {
     DEVERR_TIMEOUT_MMA   = 3,  // tensor-core completion never signalled
     DEVERR_TIMEOUT_DRAIN = 4,  // in-flight copies did not land while aborting
     DEVERR_APPEND_POS    = 5,  // an append position outside [0, n_kv): row not written
-    DEVERR_TIMEOUT_PEER  = 6,  // a CTA of the cluster never published its partial result
+    DEVERR_TIMEOUT_PEER  = 6,  // reserved: no longer raised (the cluster merge waits on the hardware
+                               // cluster barrier, which every CTA reaches after its bounded waits)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
