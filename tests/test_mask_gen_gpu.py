@@ -102,3 +102,18 @@ def test_rule_refusals():
         with pytest.raises(acefa.AcefaError) as e:
             acefa.Op(c.q, c.k, c.v, mask_gen=mg)()
         assert e.value.status == -3  # ACEFA_ERR_SHAPE
+
+
+@pytest.mark.parametrize("kv", ["bf16", "q8_0"])
+def test_dense_rules_over_bf16_and_q8_0(kv):
+    """The rules on the dense path with converted K/V: the config-5 prompt
+    prefill over a Q8_0 cache (causal) and a BF16 DiT window / padding node."""
+    c = Case(97, B=1, Hq=32, Hkv=8, n_q=300, n_kv=512, kv=kv, max_seq=1024, s0=1, mask=None)
+    got, want, _ = _pair(c, acefa.mask_gen(acefa.MASK_CAUSAL, pos0=[100]))
+    assert acefa.last_path() == 2
+    assert torch.equal(got, want), float((got - want).abs().max())
+    c2 = Case(98, B=2, Hq=16, Hkv=8, n_q=400, n_kv=400, kv=kv, mask=None)
+    got, want, _ = _pair(c2, acefa.mask_gen(acefa.MASK_WINDOW, window=96))
+    assert torch.equal(got, want), float((got - want).abs().max())
+    got, want, _ = _pair(c2, acefa.mask_gen(acefa.MASK_PADDING, lens=[150, 400]))
+    assert torch.equal(got, want), float((got - want).abs().max())

@@ -82,6 +82,19 @@ def test_dense_q_prologue(mask, D):
     assert_close(got.cpu().numpy(), _q_case(c, pos, w).oracle(), what="dense q prologue")
 
 
+@pytest.mark.parametrize("kv,D", [("bf16", 128), ("q8_0", 128), ("bf16", 64), ("q8_0", 64)])
+def test_dense_q_prologue_bf16_q8_0(kv, D):
+    # the prologue instances of the dense kernel with converted K/V (causal, GQA 2)
+    c = Case(131 + D, B=2, Hq=16, Hkv=8, n_q=300, n_kv=300, D=D, kv=kv, mask="causal")
+    w = _weights(D, 3)
+    pos = np.tile(np.arange(300, dtype=np.int32) + 50, 2)
+    pro = acefa.RopeNorm(w.cuda(), EPS, THETA, torch.from_numpy(pos).cuda())
+    got = acefa.Op(c.q, c.k, c.v, mask=c.mask, kv_type=c.kv_type, q_prologue=pro)()
+    torch.cuda.synchronize()
+    assert acefa.last_path() == 2
+    assert_close(got.cpu().numpy(), _q_case(c, pos, w).oracle(), what=f"dense q prologue {kv} D{D}")
+
+
 @pytest.mark.parametrize("kv", ["f16", "bf16", "q8_0"])
 def test_decode_q_prologue(kv):
     # batched decode: one query per set, position kv_pos of its set
