@@ -67,3 +67,13 @@ def test_mirrored_dense_split_units():
     assert np.isfinite(got).all()
     for m in mirrors:
         assert (m.cpu().numpy() == got).all()
+
+
+@pytest.mark.parametrize("kv", ["bf16", "q8_0"])
+def test_mirrored_dense_converted_kv(kv):
+    """The dense kernel's output stage with BF16 / Q8_0 K/V (the converter
+    warps' instances) writes the mirrors too."""
+    c = Case(35, B=2, Hq=16, Hkv=8, n_q=300, n_kv=400, kv=kv, mask="causal")
+    got = _run_mirrored(c, 2)
+    assert acefa.last_path() == 2
+    assert_close(got, c.oracle(), what=f"dense mirrored {kv}")
