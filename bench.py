@@ -251,7 +251,9 @@ def config_dict(args, note=None):
 
 
 # -------------------------------------------------------------------------
-def build_stack(device, kv="f16", layers=LAYERS, sets=SETS, kv_len=KV_LEN, seed=SEED):
+def build_stack(device, kv="f16", layers=LAYERS, sets=SETS, kv_len=KV_LEN, seed=SEED, valid=None):
+    """`layers` distinct decode ops over caches of kv_len rows; valid < kv_len
+    masks rows valid.. to -inf (the reference's padded decode window)."""
     import torch
 
     import acefa
@@ -259,6 +261,8 @@ def build_stack(device, kv="f16", layers=LAYERS, sets=SETS, kv_len=KV_LEN, seed=
     g = torch.Generator(device=device).manual_seed(seed)
     ops, hosts = [], []
     mask = torch.zeros(sets, 1, 1, kv_len, device=device, dtype=torch.float16)
+    if valid is not None:
+        mask[..., valid:] = float("-inf")
     ws = None
     for _ in range(layers):
         q = torch.randn(sets, HQ, 1, D, device=device, generator=g)
@@ -859,7 +863,8 @@ def decode_sweep(device, stream, layers=LAYERS):
     """BASELINE config 2's sweep: KV length {512, 2048, 8192} x KV sets
     {2, 8, 16} (1, 4, 8 requests x CFG) x F16 / Q8_0, each a stack of `layers`
     distinct layers replayed in one CUDA graph (the (8192, 16) points are the
-    headline and the q8_0_stack figures)."""
+    headline and the q8_0_stack figures), plus the padded decode windows
+    PAD(L + 1, 256) at 16 sets."""
     import torch
 
     peak, _ = read_peaks()
@@ -887,6 +892,27 @@ def decode_sweep(device, stream, layers=LAYERS):
                                                   "us_per_op": round(ms * 1e3 / layers, 2)}
                 del graph, ops
                 torch.cuda.empty_cache()
+        # the padded window of a decode step (n_kv_pad = PAD(L + 1, 256), rows
+        # past L masked): the dead tail tiles are skipped; bytes count the valid
+        # K/V rows and the whole mask
+        for kv_len in (2048, 8192):
+            win = pad256(kv_len + 1)
+            with torch.cuda.stream(stream):
+                ops, _ = build_stack(device, kv=kv, layers=layers, sets=16, kv_len=win, valid=kv_len,
+                                     seed=SEED + 19 * kv_len)
+                graph = time_graph(ops, 5, 3, stream)
+                s0.record(stream)
+                for _ in range(5):
+                    graph.replay()
+                s1.record(stream)
+                torch.cuda.synchronize()
+            ms = s0.elapsed_time(s1) / 5
+            b = (algo_bytes_per_op(sets=16, kv_len=kv_len, kv_bytes_per_row=row) + 16 * (win - kv_len) * 2) * layers
+            gbs = b / (ms / 1e3) / 1e9
+            res[f"L{kv_len}_pad{win}_N16_{kv}"] = {"gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
+                                                    "us_per_op": round(ms * 1e3 / layers, 2)}
+            del graph, ops
+            torch.cuda.empty_cache()
     return res
 
 
