@@ -87,7 +87,7 @@ struct DecCfg {
     // 128 B, 1 KB aligned); Q8_0 = whole block rows plus up to 15 lead bytes
     // (bulk copies only need 16-B alignment)
     static constexpr int  kTile       = kQ8 ? (kDecBN * kRowBytes + 16 + 15) / 16 * 16 : kDecBN * D * 2;
-    static constexpr int  kMaskBytes  = kDecRows * kDecBN * 2;  // up to 16 mask rows x 64 keys (f16)
+    static constexpr int  kMaskBytes  = kRows * kDecBN * 2;  // a mask row per unit row at most x 64 keys (f16)
     static constexpr int  kStageBytes = 2 * kTile + kMaskBytes;
     static constexpr int  kStages     = kQ8 ? (WIDE ? ACEFA_Q8W_STAGES : ACEFA_Q8_STAGES) : kDecStages;
     static_assert(kQ8 || kStageBytes % 1024 == 0, "TMA stages must stay 1 KB aligned");
@@ -99,10 +99,15 @@ struct DecCfg {
     // then hit 32 banks.
     static constexpr int  kMergeStride = kQ8 ? ((D + D / 16 - 4 + 15) / 16) * 16 + 4 : D + 8;
     __device__ static int merge_at(int row, int dim) { return row * kMergeStride + (kQ8 ? dim + (dim >> 4) : dim); }
-    // shared memory carve-up (offsets from the 1024-B aligned base)
+    // shared memory carve-up (offsets from the 1024-B aligned base).  Q8_0:
+    // the merge rows live in the stage memory, idle once every warp has left
+    // the tile loop (past the cluster merge's [C][rows] statistics table at
+    // the stages' start), so that four CTAs with three stages fit an SM.
     static constexpr int kOffStages = 0;
-    static constexpr int kOffMerge  = kStages * kStageBytes;
-    static constexpr int kOffStats  = kOffMerge + kDecRows * kMergeStride * 4;  // m,l per warp per row
+    static constexpr int kMergeBytes = kDecRows * kMergeStride * 4;
+    static constexpr int kOffMerge  = kQ8 ? 1024 : kStages * kStageBytes;
+    static_assert(!kQ8 || 1024 + kMergeBytes <= kStages * kStageBytes, "merge rows exceed the stage memory");
+    static constexpr int kOffStats  = kQ8 ? kStages * kStageBytes : kOffMerge + kMergeBytes;  // m,l per warp per row
     static constexpr int kOffFin    = kOffStats + 2 * kDecWarps * kDecRows * 4;  // merged m,l per row
     static constexpr int kOffBars   = kOffFin + 2 * kDecRows * 4;
     static constexpr int kNumBars   = 2 * kStages;  // full / empty per stage
