@@ -338,7 +338,10 @@ __global__ void __launch_bounds__(DecCfg<KV_TYPE, D, WIDE>::kThreads, DecCfg<KV_
     constexpr int  R     = Cfg::kRows;  // rows per unit
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1 KB aligned base, derived from smem_raw by an offset so that the
+    // compiler keeps the shared address space: every access through it is an
+    // ld/st.shared (a pointer rebuilt from an integer would be generic).
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
     uint64_t     *full_bar  = reinterpret_cast<uint64_t *>(smem + Cfg::kOffBars);
     uint64_t     *empty_bar = full_bar + Cfg::kStages;

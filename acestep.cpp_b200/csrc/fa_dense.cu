@@ -456,7 +456,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1 KB aligned base, derived from smem_raw by an offset so that the
+    // compiler keeps the shared address space: every access through it is an
+    // ld/st.shared (a pointer rebuilt from an integer would be generic).
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
     uint64_t     *bars    = reinterpret_cast<uint64_t *>(smem + kOffBars);
     uint64_t     *full    = bars;
