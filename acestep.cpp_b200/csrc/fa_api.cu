@@ -352,6 +352,36 @@ int encode_kv_map(CUtensorMap *map, const acefa_tensor *t, int D, int box_rows) 
     return rc == CUDA_SUCCESS ? ACEFA_OK : ACEFA_ERR_LAYOUT;
 }
 
+// f32 Q rows of one 128-row tile of a unit, for the dense kernel's TMA:
+// unit row r of kv head hk is query r / G of head hk * G + r % G, so the box
+// is {D dims, G heads, 128 / G queries, 1 batch} over dims ordered (dim,
+// head, query, batch) -- it lands in shared memory as 128 rows of D floats in
+// unit-row order.  Returns false (per-thread loads instead) when the layout
+// does not fit a tensor map: 16-B aligned base and strides, 128 % G == 0.
+bool encode_q_map(CUtensorMap *map, const acefa_tensor *q, int D, int G) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || q->type != ACEFA_TYPE_F32 || q->nb[0] != 4 || G <= 0 || kDenseBM % G != 0 ||
+        (reinterpret_cast<uintptr_t>(q->data) & 15u) != 0) {
+        return false;
+    }
+    const cuuint64_t nq = (cuuint64_t) q->ne[1], nh = (cuuint64_t) q->ne[2], nb = (cuuint64_t) q->ne[3];
+    // strides of extent-1 dimensions do not matter; keep them 16-B multiples
+    const cuuint64_t sq = nq > 1 ? (cuuint64_t) q->nb[1] : 16u * ((4u * (cuuint64_t) D + 15u) / 16u);
+    const cuuint64_t sh = nh > 1 ? (cuuint64_t) q->nb[2] : sq * nq;
+    const cuuint64_t sb = nb > 1 ? (cuuint64_t) q->nb[3] : sh * nh + sq * nq;
+    if ((sq | sh | sb) & 15u) {
+        return false;
+    }
+    cuuint64_t dims[4]    = {(cuuint64_t) D, nh, nq, nb};
+    cuuint64_t strides[3] = {sh, sq, sb};
+    cuuint32_t box[4]     = {(cuuint32_t) D, (cuuint32_t) G, (cuuint32_t) (kDenseBM / G), 1};
+    cuuint32_t estr[4]    = {1, 1, 1, 1};
+    CUresult   rc = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, q->data, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return rc == CUDA_SUCCESS;
+}
+
 }  // namespace
 }  // namespace acefa
 
@@ -522,6 +552,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         L.p.dev_err       = di->err_ptr;
         L.p.wait_limit_ns = wait_limit_ns();
         L.classify        = dp.classify;
+        L.p.q_tma         = encode_q_map(&L.qmap, q, c.op.D, c.op.G) ? 1 : 0;
         if (c.op.kv_type != ACEFA_TYPE_Q8_0 &&  // Q8_0 rows are staged by bulk copies
             ((rc = encode_kv_map(&L.kmap, k, c.op.D, kDenseBN)) != ACEFA_OK ||
              (rc = encode_kv_map(&L.vmap, v, c.op.D, kDenseBN)) != ACEFA_OK)) {

@@ -39,7 +39,7 @@ constexpr int      kQBytes     = kDenseBM * 128 * 2;  // 32 KB
 constexpr int      kOffQ       = 0;
 constexpr int      kOffRing    = kOffQ + 2 * kQBytes;
 constexpr int      kOffBars    = kOffRing + kRing * kTileBytes;
-constexpr int      kNumBars    = 2 * kRing + 2 * 3 + 1;
+constexpr int      kNumBars    = 2 * kRing + 2 * 3 + 2;  // ... + fin + the Q staging barrier
 constexpr int      kOffCls     = kOffBars + kNumBars * 8;
 constexpr int      kOffMisc    = kOffCls + 2 * kDenseMaxKT;
 constexpr int      kSmemBytes  = kOffMisc + 16 + 1024;
@@ -454,7 +454,7 @@ __device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4],
 template <bool PRO, int KVT, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
-                    const __grid_constant__ CUtensorMap vmap) {
+                    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap qmap) {
     extern __shared__ uint8_t smem_raw[];
     // 1 KB aligned base, derived from smem_raw by an offset so that the
     // compiler keeps the shared address space: every access through it is an
@@ -468,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t     *p_ready = s_ready + 2;
     uint64_t     *o_done  = p_ready + 2;
     uint64_t     *fin     = o_done + 2;
+    uint64_t     *q_full  = fin + 1;  // the unit's f32 Q rows staged in the K/V ring
     uint64_t     *ready     = reinterpret_cast<uint64_t *>(smem + kOffExt);  // [kRing] BF16 tile converted
     uint64_t     *raw_full  = ready + kRing;                                  // [kRawStages] Q8_0 half tile staged
     uint64_t     *raw_empty = raw_full + kRawStages;                         // [kRawStages] staging free again
@@ -523,12 +524,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&o_done[i], 1);
         }
         mbar_init(fin, 1);
+        mbar_init(q_full, 1);
         *abort_f = 0;
         fence_barrier_init();
     }
     if (KVT != kKvQ8 && warp == 0 && lane == 0) {
         prefetch_tensormap(&kmap);
         prefetch_tensormap(&vmap);
+    }
+    if (P.q_tma && warp == 0 && lane == 0) {
+        prefetch_tensormap(&qmap);
     }
     pdl_wait_primary();
 
@@ -553,6 +558,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     __syncthreads();  // barriers initialised, class table complete
+
+    // The unit's Q rows (f32) by TMA into the K/V ring, idle until Q has been
+    // converted: far more bytes in flight than per-thread loads give.
+    if (P.q_tma && warp == 0 && lane == 0) {
+        const uint32_t tile_bytes = kDenseBM * HD * 4;
+        mbar_arrive_expect_tx(q_full, tile_bytes * ((has_tile[0] ? 1u : 0u) + (has_tile[1] ? 1u : 0u)));
+        for (int i = 0; i < 2; ++i) {
+            if (has_tile[i]) {
+                tma_load_4d(smem + kOffRing + i * tile_bytes, &qmap, 0, hk * o.G, (t0 + i) * (kDenseBM / o.G), b,
+                            q_full);
+            }
+        }
+    }
 
     auto live_of  = [&](int i, int j) -> bool { return (s_cls[i * kDenseMaxKT + j] & kClsLive) != 0; };
     auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };
@@ -614,6 +632,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                            ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
             *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
         };
+        const float *q_st = reinterpret_cast<const float *>(smem + kOffRing);  // [2][128][HD] when q_tma
+        if (P.q_tma &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(q_full, 0u, abort_f, P.dev_err, DEVERR_TIMEOUT_FULL,
+                                                       P.wait_limit_ns))) {
+            *abort_f = 1;  // the waits below give up at once; the Q copy is drained before exit
+        }
         for (int base = threadIdx.x; base < kChunks; base += kThreads * kUnroll) {
             float4 v[kUnroll];
 #pragma unroll
@@ -623,7 +647,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int rr = ch / kCpr;
                 const int i  = rr / kDenseBM;
                 const int gr = (t0 + i) * kDenseBM + rr % kDenseBM;
-                if (ch < kChunks && has_tile[i] && gr < P.rows_total) {
+                if (P.q_tma) {
+                    if (ch < kChunks && has_tile[i] && gr < P.rows_total) {
+                        v[u] = *reinterpret_cast<const float4 *>(q_st + (size_t) rr * HD + 4 * (ch % kCpr));
+                    }
+                } else if (ch < kChunks && has_tile[i] && gr < P.rows_total) {
                     int iq, hq;
                     row_to_query(gr, o.G, hk, iq, hq);
                     const char  *qrow = o.q + (int64_t) iq * o.q_nb1 + (int64_t) hq * o.q_nb2 + (int64_t) b * o.q_nb3;
@@ -1334,6 +1362,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (P.q_tma && warp == 0 && lane == 0 && !mbar_try_wait(q_full, 0u)) {
+        // only after an abort: let the Q copy land before the CTA exits
+        const uint64_t t_start = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0u)) {
+            if (globaltimer_ns() - t_start > P.wait_limit_ns) {
+                atomicCAS(P.dev_err, 0, DEVERR_TIMEOUT_DRAIN);
+                break;
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1488,7 +1526,7 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     c.stream             = s;
     c.attrs              = attr;
     c.numAttrs           = 1;
-    cudaError_t e        = cudaLaunchKernelEx(&c, kern, L.p, L.kmap, L.vmap);
+    cudaError_t e        = cudaLaunchKernelEx(&c, kern, L.p, L.kmap, L.vmap, L.qmap);
     if (e != cudaSuccess) {
         return e;
     }

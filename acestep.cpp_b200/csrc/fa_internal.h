@@ -189,6 +189,7 @@ struct DenseParams {
     float         *part;        // [n_tail][n_split][2 tiles] partial slots (dense_part_floats each)
     int           *dev_err;
     uint64_t       wait_limit_ns;
+    int            q_tma;       // Q rows staged by TMA (qmap) instead of per-thread loads
 };
 
 constexpr int kDenseMaxSplit = 8;  // key ranges per split unit
@@ -199,6 +200,7 @@ constexpr int dense_part_floats() { return 128 * kDenseBM + 2 * kDenseBM; }
 struct DenseLaunch {
     DenseParams p;
     CUtensorMap kmap, vmap;  // box {64, 128, 1, 1}, 128-B swizzle
+    CUtensorMap qmap;        // f32 Q rows of one row tile (when p.q_tma)
     bool        classify;    // run the mask-classification pre-pass
 };
 
