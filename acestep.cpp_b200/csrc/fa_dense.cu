@@ -537,6 +537,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     pdl_wait_primary();
 
+    // The unit's Q rows (f32) by TMA into the K/V ring, idle until Q has been
+    // converted: far more bytes in flight than per-thread loads give.  Issued
+    // by the thread that initialised the barriers, before the class table.
+    if (P.q_tma && threadIdx.x == 0) {
+        const uint32_t tile_bytes = kDenseBM * HD * 4;
+        mbar_arrive_expect_tx(q_full, tile_bytes * ((has_tile[0] ? 1u : 0u) + (has_tile[1] ? 1u : 0u)));
+        for (int i = 0; i < 2; ++i) {
+            if (has_tile[i]) {
+                tma_load_4d(smem + kOffRing + i * tile_bytes, &qmap, 0, hk * o.G, (t0 + i) * (kDenseBM / o.G), b,
+                            q_full);
+            }
+        }
+    }
+
     // ---- key-tile classes of both row tiles
     for (int j = threadIdx.x; j < P.n_kt; j += kThreads) {
         for (int i = 0; i < 2; ++i) {
@@ -558,19 +572,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     __syncthreads();  // barriers initialised, class table complete
-
-    // The unit's Q rows (f32) by TMA into the K/V ring, idle until Q has been
-    // converted: far more bytes in flight than per-thread loads give.
-    if (P.q_tma && warp == 0 && lane == 0) {
-        const uint32_t tile_bytes = kDenseBM * HD * 4;
-        mbar_arrive_expect_tx(q_full, tile_bytes * ((has_tile[0] ? 1u : 0u) + (has_tile[1] ? 1u : 0u)));
-        for (int i = 0; i < 2; ++i) {
-            if (has_tile[i]) {
-                tma_load_4d(smem + kOffRing + i * tile_bytes, &qmap, 0, hk * o.G, (t0 + i) * (kDenseBM / o.G), b,
-                            q_full);
-            }
-        }
-    }
 
     auto live_of  = [&](int i, int j) -> bool { return (s_cls[i * kDenseMaxKT + j] & kClsLive) != 0; };
     auto any_live = [&](int j) -> bool { return live_of(0, j) || live_of(1, j); };

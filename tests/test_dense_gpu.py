@@ -313,3 +313,33 @@ def test_dense_d64_causal_cache_view_and_split_tail():
 def test_dense_d64_sinks_softcap_alibi():
     c = Case(42 + 6404, B=2, Hq=8, Hkv=4, n_q=200, n_kv=300, D=64, mask="random", sinks=True)
     run_case(c, max_bias=8.0, softcap=20.0)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(16, 8), (16, 16)])
+def test_q_staging_tma_and_thread_loads_agree(Hq, Hkv):
+    """The dense kernel stages a unit's f32 Q rows by TMA when a tensor map can
+    describe them (16-B aligned base and strides, 128 % G == 0) and by
+    per-thread loads otherwise.  Both convert the same values, so a Q copied to
+    a 4-byte offset (thread loads) and a head-interleaved Q (the layout of a
+    ggml_permute of the projection: head stride below query stride, TMA) give
+    outputs bit-identical to the contiguous Q."""
+    c = Case(4242 + Hq + Hkv, B=2, Hq=Hq, Hkv=Hkv, n_q=700, n_kv=900, mask="random")
+    got, _ = run_case(c)
+    buf = torch.empty(c.q.numel() + 1, device="cuda")
+    q_off = buf[1:].view(c.q.shape)
+    q_off.copy_(c.q)
+    q_perm = c.q.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)  # (B, Hq, n_q, D), heads innermost
+    assert q_perm.stride(1) < q_perm.stride(2)
+    for q in (q_off, q_perm):
+        out = acefa.Op(q, c.k, c.v, mask=c.mask, kv_type=c.kv_type)()
+        torch.cuda.synchronize()
+        assert acefa.last_path() == 2
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), got.view(np.uint32))
+    assert acefa.device_error() == 0
+
+
+def test_q_staging_group_not_dividing_the_row_tile():
+    """G = 3 (24 query heads over 8 KV heads): 128 % G != 0, so Q goes through
+    the per-thread loads; parity with the oracle."""
+    c = Case(4343, B=1, Hq=24, Hkv=8, n_q=300, n_kv=500, mask="random")
+    run_case(c)
