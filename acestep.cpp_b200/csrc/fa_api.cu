@@ -277,7 +277,8 @@ struct DensePlan {
     int    rows_total, n_rt, n_pairs, n_kt;
     int    n_full, n_tail, n_split;
     bool   classify;
-    size_t cls_bytes;  // class table at the start of the workspace (256-B aligned)
+    size_t cls_bytes;   // class table at the start of the workspace (256-B aligned)
+    size_t conv_bytes;  // F16 copies of BF16 K/V at the end of the workspace, or 0
     size_t ws_bytes;
 };
 
@@ -327,7 +328,17 @@ DensePlan plan_dense(const OpDesc &o, int sm_count, size_t ws_limit) {
     p.n_split  = (int) split;
     p.n_tail   = split > 1 ? (int) tail : 0;
     p.n_full   = (int) (units - p.n_tail);
-    p.ws_bytes = p.cls_bytes + (split > 1 ? part_bytes(split) : 0);
+    p.ws_bytes = p.cls_bytes + (split > 1 ? (part_bytes(split) + 255) / 256 * 256 : 0);
+    // BF16 K/V: F16 copies made by one conversion pass when they fit the
+    // offer (the kernel's converter warps otherwise)
+    p.conv_bytes = 0;
+    if (o.kv_type == ACEFA_TYPE_BF16) {
+        const size_t conv = ((size_t) 2 * o.Bk * o.Hkv * o.n_kv * o.D * 2 + 255) / 256 * 256;
+        if (p.ws_bytes + conv <= ws_limit && (int64_t) o.n_kv * (o.D / 8) < (1ll << 31)) {
+            p.conv_bytes = conv;
+            p.ws_bytes += conv;
+        }
+    }
     if (p.ws_bytes == 0) {
         p.ws_bytes = 256;
     }
@@ -529,6 +540,33 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         if (workspace_bytes < dp.ws_bytes || !workspace || !aligned(workspace, 256)) {
             return ACEFA_ERR_WORKSPACE;
         }
+        acefa_tensor kc, vc;  // the F16 copies of BF16 K/V, when the plan makes them
+        int          pre = 0;
+        if (dp.conv_bytes) {
+            const size_t per = dp.conv_bytes / 2 / 256 * 256;
+            uint16_t *kd = reinterpret_cast<uint16_t *>(static_cast<char *>(workspace) + dp.ws_bytes - dp.conv_bytes);
+            uint16_t *vd = reinterpret_cast<uint16_t *>(reinterpret_cast<char *>(kd) + per);
+            if (dense_bf16_to_f16(c.op, kd, vd, s) != cudaSuccess) {
+                return ACEFA_ERR_CUDA;
+            }
+            pre = 1;
+            for (int side = 0; side < 2; ++side) {
+                acefa_tensor &t = side ? vc : kc;
+                t               = side ? *v : *k;
+                t.type          = ACEFA_TYPE_F16;
+                t.data          = side ? static_cast<void *>(vd) : static_cast<void *>(kd);
+                t.nb[0]         = 2;
+                t.nb[1]         = (size_t) 2 * c.op.D;
+                t.nb[2]         = t.nb[1] * (size_t) c.op.n_kv;
+                t.nb[3]         = t.nb[2] * (size_t) c.op.Hkv;
+            }
+            c.op.k = static_cast<const char *>(kc.data), c.op.v = static_cast<const char *>(vc.data);
+            c.op.k_nb1 = c.op.v_nb1 = (int64_t) kc.nb[1];
+            c.op.k_nb2 = c.op.v_nb2 = (int64_t) kc.nb[2];
+            c.op.k_nb3 = c.op.v_nb3 = (int64_t) kc.nb[3];
+            c.op.kv_type = ACEFA_TYPE_F16;
+            k = &kc, v = &vc;
+        }
         DenseLaunch L;
         std::memset(&L, 0, sizeof(L));
         L.p.op            = c.op;
@@ -562,7 +600,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         if (launch_dense(L, s, &launches) != cudaSuccess) {
             return ACEFA_ERR_CUDA;
         }
-        t_last_launches = launches;
+        t_last_launches = launches + pre;
         t_last_path     = 2;
         return ACEFA_OK;
     }

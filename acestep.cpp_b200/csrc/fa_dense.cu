@@ -1456,6 +1456,50 @@ __global__ void __launch_bounds__(kDenseBM) fa_dense_combine(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------
+// BF16 K/V -> contiguous F16 copies [Bk][Hkv][n_kv][D] in the caller's
+// workspace, when it holds them: the dense kernel then runs its F16 instance
+// instead of converting every staged tile with two warps.  The same rounding
+// as those warps (bf16 -> f32 exactly, then f16 to nearest even), so either
+// route gives bit-identical results.  Grid (16-B chunks of one head's rows /
+// 256, Hkv * Bk, K / V); HBM-bound: 2 B read and 2 B written per value.
+namespace {
+
+struct CvtSide {
+    const char *src;
+    int64_t     nb1, nb2, nb3;
+    uint4      *dst;
+};
+
+__global__ void __launch_bounds__(256) fa_bf16_to_f16(const CvtSide ks, const CvtSide vs, int cpr_log2, int n_kv,
+                                                      int Hkv) {
+    const CvtSide &sd    = blockIdx.z ? vs : ks;
+    const int      hb    = (int) blockIdx.y;
+    const int      h     = hb % Hkv, b = hb / Hkv;
+    const int      per_h = n_kv << cpr_log2;  // chunks of one head
+    const int      x     = (int) blockIdx.x * 256 + (int) threadIdx.x;
+    if (x >= per_h) {
+        return;
+    }
+    const int   j  = x >> cpr_log2, ch = x & ((1 << cpr_log2) - 1);
+    const uint4 w  = __ldcs(reinterpret_cast<const uint4 *>(sd.src + (int64_t) j * sd.nb1 + (int64_t) h * sd.nb2 +
+                                                           (int64_t) b * sd.nb3) + ch);
+    const uint4 o4 = make_uint4(bf16x2_to_f16x2(w.x), bf16x2_to_f16x2(w.y), bf16x2_to_f16x2(w.z),
+                                bf16x2_to_f16x2(w.w));
+    sd.dst[(int64_t) hb * per_h + x] = o4;
+}
+
+}  // namespace
+
+cudaError_t dense_bf16_to_f16(const OpDesc &o, uint16_t *k_dst, uint16_t *v_dst, cudaStream_t s) {
+    CvtSide ks = {o.k, o.k_nb1, o.k_nb2, o.k_nb3, reinterpret_cast<uint4 *>(k_dst)};
+    CvtSide vs = {o.v, o.v_nb1, o.v_nb2, o.v_nb3, reinterpret_cast<uint4 *>(v_dst)};
+    const int cpr_log2 = o.D == 128 ? 4 : 3;  // 16-B chunks per row: D / 8
+    const int per_h    = o.n_kv << cpr_log2;
+    dim3      grid((unsigned) ((per_h + 255) / 256), (unsigned) (o.Hkv * o.Bk), 2);
+    fa_bf16_to_f16<<<grid, 256, 0, s>>>(ks, vs, cpr_log2, o.n_kv, o.Hkv);
+    return cudaGetLastError();
+}
+
 namespace {
 
 template <int KVT>

@@ -206,6 +206,9 @@ struct DenseLaunch {
 
 cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches);
 
+// BF16 K/V of `o` -> contiguous F16 copies [Bk][Hkv][n_kv][D] (one launch).
+cudaError_t dense_bf16_to_f16(const OpDesc &o, uint16_t *k_dst, uint16_t *v_dst, cudaStream_t s);
+
 // ------------------------------------------------------------------ workspace
 // Bytes of workspace the operator needs when it is offered at most `limit`
 // (acefa_workspace_bytes is limit = SIZE_MAX); 0 for unsupported operands.

@@ -343,3 +343,26 @@ def test_q_staging_group_not_dividing_the_row_tile():
     the per-thread loads; parity with the oracle."""
     c = Case(4343, B=1, Hq=24, Hkv=8, n_q=300, n_kv=500, mask="random")
     run_case(c)
+
+
+@pytest.mark.parametrize("mask", ["random", None])
+def test_bf16_conversion_pass_and_converter_warps_agree(mask):
+    """BF16 K/V: with room in the workspace one pass converts them to F16 copies
+    that the F16 kernel reads; without it the kernel's converter warps convert
+    each staged tile.  Both round bf16 -> f32 -> f16 to nearest even, so the
+    outputs are bit-identical (and the pass is one extra launch)."""
+    c = Case(5151, B=2, Hq=16, Hkv=8, n_q=600, n_kv=700, kv="bf16", mask=mask)
+    op = c.op()
+    conv = (2 * c.Bk * c.Hkv * c.n_kv * c.D * 2 + 255) // 256 * 256
+    assert op.ws_bytes >= conv
+    full = op().clone()
+    torch.cuda.synchronize()
+    assert acefa.last_path() == 2
+    n_full = acefa.last_launch_count()
+    op.workspace = op.workspace[: max(op.ws_bytes - conv, 256)]
+    part = op().clone()
+    torch.cuda.synchronize()
+    assert acefa.last_launch_count() == n_full - 1
+    assert torch.equal(full.view(torch.int32), part.view(torch.int32))
+    assert_close(part.cpu().numpy(), c.oracle(), what="bf16 converter warps")
+    assert acefa.device_error() == 0
