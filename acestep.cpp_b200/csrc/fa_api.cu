@@ -393,6 +393,35 @@ bool encode_q_map(CUtensorMap *map, const acefa_tensor *q, int D, int G) {
     return rc == CUDA_SUCCESS;
 }
 
+// The f32 output rows of 32 unit rows x 32 dims, for the dense kernel's TMA
+// stores: dst [D, Hq, n_q, B] ordered (dim, head, query, batch), box {32, G,
+// 32 / G, 1} with the 128-B swizzle of the kernel's per-warp staging slab.
+// Returns false (per-lane stores instead) when the layout does not fit a
+// tensor map: 16-B aligned base and strides, 32 % G == 0, or mirrors (peer
+// buffers) to store into as well.
+bool encode_o_map(CUtensorMap *map, const acefa_tensor *d, int D, int G, int n_mirror) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || n_mirror != 0 || d->type != ACEFA_TYPE_F32 || d->nb[0] != 4 || G <= 0 || 32 % G != 0 ||
+        (reinterpret_cast<uintptr_t>(d->data) & 15u) != 0) {
+        return false;
+    }
+    const cuuint64_t nh = (cuuint64_t) d->ne[1], nq = (cuuint64_t) d->ne[2], nb = (cuuint64_t) d->ne[3];
+    const cuuint64_t sh = nh > 1 ? (cuuint64_t) d->nb[1] : 16u * ((4u * (cuuint64_t) D + 15u) / 16u);
+    const cuuint64_t sq = nq > 1 ? (cuuint64_t) d->nb[2] : sh * nh;
+    const cuuint64_t sb = nb > 1 ? (cuuint64_t) d->nb[3] : sq * nq + sh * nh;
+    if ((sh | sq | sb) & 15u) {
+        return false;
+    }
+    cuuint64_t dims[4]    = {(cuuint64_t) D, nh, nq, nb};
+    cuuint64_t strides[3] = {sh, sq, sb};
+    cuuint32_t box[4]     = {32, (cuuint32_t) G, (cuuint32_t) (32 / G), 1};
+    cuuint32_t estr[4]    = {1, 1, 1, 1};
+    CUresult   rc = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->data, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return rc == CUDA_SUCCESS;
+}
+
 }  // namespace
 }  // namespace acefa
 
@@ -591,6 +620,7 @@ static int run_op(const acefa_tensor *q, const acefa_tensor *k, const acefa_tens
         L.p.wait_limit_ns = wait_limit_ns();
         L.classify        = dp.classify;
         L.p.q_tma         = encode_q_map(&L.qmap, q, c.op.D, c.op.G) ? 1 : 0;
+        L.p.o_tma         = encode_o_map(&L.omap, dst, c.op.D, c.op.G, c.op.n_mirror) ? 1 : 0;
         if (c.op.kv_type != ACEFA_TYPE_Q8_0 &&  // Q8_0 rows are staged by bulk copies
             ((rc = encode_kv_map(&L.kmap, k, c.op.D, kDenseBN)) != ACEFA_OK ||
              (rc = encode_kv_map(&L.vmap, v, c.op.D, kDenseBN)) != ACEFA_OK)) {

@@ -454,7 +454,8 @@ __device__ __forceinline__ void pass2_exp(uint32_t tS, const uint32_t (&vis)[4],
 template <bool PRO, int KVT, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_dense_kernel(const __grid_constant__ DenseParams P, const __grid_constant__ CUtensorMap kmap,
-                    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap qmap) {
+                    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap qmap,
+                    const __grid_constant__ CUtensorMap omap) {
     extern __shared__ uint8_t smem_raw[];
     // 1 KB aligned base, derived from smem_raw by an offset so that the
     // compiler keeps the shared address space: every access through it is an
@@ -1299,6 +1300,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         // j ^ (r & 7), so both the parking and the read-back are conflict-free.
         const bool al16 = __all_sync(0xffffffffu, (reinterpret_cast<uintptr_t>(orow) & 15u) == 0);
         uint8_t   *stage = smem + kOffQ + i * kQBytes + wq * 8192;
+        if (P.o_tma) {
+            // The warp's 32 rows leave by TMA stores of 32-dim chunks, two 4 KB
+            // slabs alternating (the 128-B swizzle is the slab's XOR layout);
+            // rows past the node are clipped by the tensor map.
+            const int row0 = (t0 + i) * kDenseBM + 32 * wq;  // first unit row of this warp
+#pragma unroll 1
+            for (int ch = 0; ch < HD / 32; ++ch) {
+                uint32_t x[32];
+                if (ok && cnt > 0) {
+                    tmem_ld32(tO + 32 * ch, x);
+                    tmem_ld_wait32(x);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        x[e] = 0u;
+                    }
+                }
+                uint8_t *slab = stage + (ch & 1) * 4096;
+                if (ch >= 2 && lane == 0) {
+                    bulk_wait_read<1>();  // the store of chunk ch - 2 has read this slab
+                }
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    *reinterpret_cast<float4 *>(slab + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_float4(__uint_as_float(x[4 * j]) * inv, __uint_as_float(x[4 * j + 1]) * inv,
+                                    __uint_as_float(x[4 * j + 2]) * inv, __uint_as_float(x[4 * j + 3]) * inv);
+                }
+                fence_proxy_async_smem();  // the slab is read by the async proxy
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_4d(&omap, slab, 32 * ch, hk * o.G, row0 / o.G, b);
+                    bulk_commit();
+                }
+            }
+            if (lane == 0) {
+                bulk_wait_read<0>();  // shared memory read out; the global writes complete with the grid
+            }
+            __syncwarp();
+        } else {
         char      *rowp[8];
 #pragma unroll
         for (int st = 0; st < 8; ++st) {
@@ -1350,6 +1391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+        }
         }
         if (o.n_mirror) {
             __threadfence_system();  // peer stores performed before the kernel retires
@@ -1571,7 +1613,7 @@ cudaError_t launch_dense(const DenseLaunch &L, cudaStream_t s, int *launches) {
     c.stream             = s;
     c.attrs              = attr;
     c.numAttrs           = 1;
-    cudaError_t e        = cudaLaunchKernelEx(&c, kern, L.p, L.kmap, L.vmap, L.qmap);
+    cudaError_t e        = cudaLaunchKernelEx(&c, kern, L.p, L.kmap, L.vmap, L.qmap, L.omap);
     if (e != cudaSuccess) {
         return e;
     }

@@ -190,6 +190,7 @@ struct DenseParams {
     int           *dev_err;
     uint64_t       wait_limit_ns;
     int            q_tma;       // Q rows staged by TMA (qmap) instead of per-thread loads
+    int            o_tma;       // output rows leave by TMA stores (omap) instead of per-lane stores
 };
 
 constexpr int kDenseMaxSplit = 8;  // key ranges per split unit
@@ -201,6 +202,7 @@ struct DenseLaunch {
     DenseParams p;
     CUtensorMap kmap, vmap;  // box {64, 128, 1, 1}, 128-B swizzle
     CUtensorMap qmap;        // f32 Q rows of one row tile (when p.q_tma)
+    CUtensorMap omap;        // f32 output: 32 dims x 32 unit rows, 128-B swizzle (when p.o_tma)
     bool        classify;    // run the mask-classification pre-pass
 };
 

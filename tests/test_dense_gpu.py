@@ -366,3 +366,20 @@ def test_bf16_conversion_pass_and_converter_warps_agree(mask):
     assert torch.equal(full.view(torch.int32), part.view(torch.int32))
     assert_close(part.cpu().numpy(), c.oracle(), what="bf16 converter warps")
     assert acefa.device_error() == 0
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(16, 8), (16, 16)])
+def test_output_tma_stores_and_lane_stores_agree(Hq, Hkv):
+    """Output rows leave the dense kernel by TMA stores when a tensor map can
+    describe the destination (16-B aligned base and strides, 32 % G == 0, no
+    mirrors) and by per-lane stores otherwise: an output at a 4-byte offset
+    takes the second route and must hold the same bits.  Ragged row count."""
+    c = Case(4545 + Hq + Hkv, B=2, Hq=Hq, Hkv=Hkv, n_q=333, n_kv=500, mask="random")
+    got, _ = run_case(c)
+    buf = torch.empty(got.size + 1, device="cuda")
+    out_off = buf[1:].view(got.shape)
+    acefa.Op(c.q, c.k, c.v, mask=c.mask, kv_type=c.kv_type, out=out_off)()
+    torch.cuda.synchronize()
+    assert acefa.last_path() == 2
+    assert np.array_equal(out_off.cpu().numpy().view(np.uint32), got.view(np.uint32))
+    assert acefa.device_error() == 0
