@@ -315,9 +315,13 @@ ACEFA_API int acefa_cfg_logit_combine(const float *cond, const float *uncond, in
                                       float *compact, void *stream);
 
 /* Workspace acefa_flash_attn_ext() needs for these operands on the current device
- * (split-KV partial results, mask tile classes).  A function of shapes, types
- * and the device only -- never of tensor contents -- so it can be sized once
- * before CUDA-graph capture.  Returns 0 for unsupported operands. */
+ * (split-KV partial results, mask tile classes, and for BF16 K/V on the dense
+ * path F16 copies of K and V: 4 bytes per K/V value).  A function of shapes,
+ * types and the device only -- never of tensor contents -- so it can be sized
+ * once before CUDA-graph capture.  A smaller workspace also works where the
+ * operator can do without: it then skips the BF16 copies (converting inside
+ * the attention kernel, same results) and splits fewer key ranges.  Returns 0
+ * for unsupported operands. */
 ACEFA_API size_t acefa_workspace_bytes(const acefa_tensor *q, const acefa_tensor *k, const acefa_tensor *v,
                                        const acefa_tensor *mask, const acefa_tensor *dst);
 
