@@ -383,3 +383,26 @@ def test_output_tma_stores_and_lane_stores_agree(Hq, Hkv):
     assert acefa.last_path() == 2
     assert np.array_equal(out_off.cpu().numpy().view(np.uint32), got.view(np.uint32))
     assert acefa.device_error() == 0
+
+
+def test_tma_q_and_output_with_padded_strides():
+    """Q and the output as views of padded buffers (every stride a multiple
+    of 16 B, none tight): the Q copy and the output stores still go by TMA,
+    and the results are bit-identical to the tight layouts."""
+    c = Case(4646, B=2, Hq=16, Hkv=8, n_q=300, n_kv=400, mask="random")
+    got, _ = run_case(c)
+    D = c.D
+    qbuf = torch.zeros(c.B, c.Hq + 1, c.n_q + 3, D + 4, device="cuda")
+    q_pad = qbuf[:, :c.Hq, :c.n_q, :D]
+    q_pad.copy_(c.q)
+    obuf = torch.zeros(c.B, c.n_q + 1, c.Hq + 2, D + 8, device="cuda")
+    o_pad = obuf[:, :c.n_q, :c.Hq, :D]
+    acefa.Op(q_pad, c.k, c.v, mask=c.mask, kv_type=c.kv_type, out=o_pad)()
+    torch.cuda.synchronize()
+    assert acefa.last_path() == 2
+    assert np.array_equal(o_pad.cpu().numpy().view(np.uint32), got.view(np.uint32))
+    # the padding around the output is untouched
+    rest = obuf.clone()
+    rest[:, :c.n_q, :c.Hq, :D] = 0
+    assert torch.count_nonzero(rest) == 0
+    assert acefa.device_error() == 0
