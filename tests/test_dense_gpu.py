@@ -406,3 +406,12 @@ def test_tma_q_and_output_with_padded_strides():
     rest[:, :c.n_q, :c.Hq, :D] = 0
     assert torch.count_nonzero(rest) == 0
     assert acefa.device_error() == 0
+
+
+@pytest.mark.parametrize("kv", ["f16", "bf16", "q8_0"])
+def test_dense_kv_shared_by_batches(kv):
+    """K/V with one batch shared by two query batches (ggml: K ne3 = 1, Q ne3 =
+    2; query batch b reads K/V batch b / 2): the TMA Q / output maps, the BF16
+    copies and the Q8_0 staging all index the K/V batch by bk = b / rk3."""
+    c = Case(4747 + len(kv), B=2, Bk=1, Hq=16, Hkv=8, n_q=260, n_kv=390, kv=kv, mask="random", m_batch=2)
+    run_case(c)
