@@ -17,6 +17,10 @@
 //               mask / ALiBi in log2 units, keeps a running max that only
 //               moves (and rescales O in TMEM) when it grows by more than 2^8,
 //               and writes P as f16 over the S columns it just read.
+// Q arrives as f32 rows by TMA into the K/V ring (idle until then) and every
+// thread converts it to swizzled f16 once per CTA; the output leaves by TMA
+// stores of 32-dim chunks staged in the idle Q buffers (per-thread loads and
+// per-lane stores where a tensor map cannot describe the tensor).
 // The two row tiles ping-pong: while one warpgroup exponentiates, the tensor
 // core runs the other tile's PV and next S.  When the work units leave the
 // last wave mostly idle, the leftover units are cut into key ranges whose
