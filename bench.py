@@ -958,6 +958,32 @@ def dense_pairs(S_q, S_kv, kind, extra):
     raise ValueError(kind)
 
 
+def dense_bytes(name, rule=False):
+    """Algorithmic HBM bytes of one dense op: Q read and O written in f32, K
+    and V read once (F16/BF16 2 B per value, Q8_0 34 B per 32 values), the f16
+    mask read once (none when the mask is given by rule)."""
+    B, Hq, Hkv, S_q, S_kv, kind, extra = DENSE_WORKLOADS[name][:7]
+    kv = DENSE_WORKLOADS[name][7] if len(DENSE_WORKLOADS[name]) > 7 else "f16"
+    hd = DENSE_WORKLOADS[name][8] if len(DENSE_WORKLOADS[name]) > 8 else D
+    kv_row = hd * 34 // 32 if kv == "q8_0" else hd * 2
+    qo = 2 * B * Hq * S_q * hd * 4
+    kvb = 2 * B * Hkv * S_kv * kv_row
+    m = S_q * S_kv * 2 if (kind is not None and not rule) else 0
+    return qo + kvb + m
+
+
+def dense_bound(flops, nbytes, ms, tflops_peak, hbm_peak):
+    """The op's roofline: its shortest possible time is the longer of the
+    tensor time (FLOPs / tensor peak) and the HBM time (bytes / HBM peak);
+    `bound` names the longer one and `frac_of_bound` = that time / measured."""
+    t_tensor = flops / (tflops_peak * 1e12) * 1e3
+    t_hbm = nbytes / (hbm_peak * 1e9) * 1e3
+    bound = "tensor" if t_tensor >= t_hbm else "hbm"
+    return {"bound": bound, "tensor_ms": round(t_tensor, 5), "hbm_ms": round(t_hbm, 5),
+            "frac_of_bound": round(max(t_tensor, t_hbm) / ms, 4),
+            "hbm_gbs": round(nbytes / (ms / 1e3) / 1e9, 1), "hbm_frac": round(nbytes / (ms / 1e3) / 1e9 / hbm_peak, 4)}
+
+
 def build_dense(device, name, seed=SEED + 3, rule=False):
     """The workload's op; rule=True gives its mask by rule (acefa_flash_attn_ext_gen)."""
     import torch
@@ -1032,13 +1058,18 @@ def dense_extras(device, stream, cpu=True):
     the same op through the C ABI with host buffers (e2e), and for the
     headline shapes the CPU port on sampled query rows."""
     peak = read_tflops_peak()
-    res = {"peak_tflops": peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; kernel timed alone)"}
+    hbm_peak = read_peaks()[0]
+    res = {"peak_tflops": peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; kernel timed alone)",
+           "peak_hbm_gbs": hbm_peak}
     for name in DENSE_WORKLOADS:
         r = time_dense(device, stream, name)
         r["frac_of_peak"] = round(r["tflops"] / peak, 4)
+        nbytes = dense_bytes(name)
         r["roofline"] = {"bound": "tensor", "achieved": r["tflops"], "peak": peak, "unit": "TFLOP/s",
                          "frac": r["frac_of_peak"], "traffic": read_traffic(f"fa_dense_kernel_{name}"),
-                         "peak_source": "measured bf16_tflops (burst)", "algo_flop_per_launch": int(r["gflop"] * 1e9)}
+                         "peak_source": "measured bf16_tflops (burst)", "algo_flop_per_launch": int(r["gflop"] * 1e9),
+                         "algo_bytes_per_launch": nbytes,
+                         "binding": dense_bound(r["gflop"] * 1e9, nbytes, r["ms"], peak, hbm_peak)}
         if name in ("prefill4096", "dit6000", "cross6000", "prefill1024", "dit1500"):
             r["e2e"] = dense_e2e(device, stream, name)
         if cpu and name in DENSE_CPU_SAMPLED:
@@ -1050,6 +1081,7 @@ def dense_extras(device, stream, cpu=True):
         if wl[5] is not None and len(wl) == 7:
             r = time_dense(device, stream, name, rule=True)
             r["frac_of_peak"] = round(r["tflops"] / peak, 4)
+            r["binding"] = dense_bound(r["gflop"] * 1e9, dense_bytes(name, rule=True), r["ms"], peak, hbm_peak)
             res[name + "_rule"] = r
     return res
 
