@@ -1024,12 +1024,21 @@ def build_dense(device, name, seed=SEED + 3, rule=False):
     return op, flops
 
 
-def time_dense(device, stream, name, iters=10, warmup=3, rule=False):
+L2_BYTES = 126 * 1024 * 1024  # B200 L2
+
+
+def time_dense(device, stream, name, iters=100, warmup=3, rule=False):
+    """One dense op captured in a CUDA graph, `iters` replays timed with CUDA
+    events on the launching stream.  An op whose bytes exceed twice the L2 is
+    timed as one block of back-to-back replays; a smaller one gets a 256 MB
+    L2-flushing write before every replay, outside its own event pair, so no
+    replay finds its inputs in L2."""
     import torch
 
     import acefa
 
     op, flops = build_dense(device, name, rule=rule)
+    flush = dense_bytes(name, rule) < 2 * L2_BYTES
     with torch.cuda.stream(stream):
         op(stream=stream)
         path = acefa.last_path()
@@ -1039,21 +1048,35 @@ def time_dense(device, stream, name, iters=10, warmup=3, rule=False):
             op(stream=stream)
         for _ in range(warmup):
             graph.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(iters):
-            graph.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / iters
+        if flush:
+            scrub = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+            for a, b in ev:
+                scrub.zero_()
+                a.record(stream)
+                graph.replay()
+                b.record(stream)
+            torch.cuda.synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in ev) / iters
+            del scrub
+        else:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(iters):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
     del graph, op
     return {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1), "gflop": round(flops / 1e9, 2),
+            "l2": "flushed before every replay" if flush else "inputs larger than twice the L2; no flush",
             "path": "dense tcgen05" if path == 2 else "decode"}
 
 
 def dense_extras(device, stream, cpu=True):
     """BASELINE configs 3 and 4: each dense workload timed alone (CUDA graph,
-    10 replays), with its roofline (tensor bound, measured bf16 burst peak;
+    100 replays, L2 flushed between replays of ops smaller than twice the L2),
+    with its roofline (tensor bound, measured bf16 burst peak;
     DRAM traffic of one launch from profiles/ncu_traffic.json when captured),
     the same op through the C ABI with host buffers (e2e), and for the
     headline shapes the CPU port on sampled query rows."""
