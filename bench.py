@@ -876,8 +876,13 @@ def decode_sweep(device, stream, layers=LAYERS):
             for sets in (2, 8, 16):
                 if kv_len == 8192 and sets == 16:
                     continue
+                # at least twice the L2 of distinct layers, so that no replay
+                # finds its K/V in L2 (36 layers of the smallest points hold
+                # less than the L2)
+                per_op = algo_bytes_per_op(sets=sets, kv_len=kv_len, kv_bytes_per_row=row)
+                nl = max(layers, -(-2 * L2_BYTES // per_op))
                 with torch.cuda.stream(stream):
-                    ops, _ = build_stack(device, kv=kv, layers=layers, sets=sets, kv_len=kv_len,
+                    ops, _ = build_stack(device, kv=kv, layers=nl, sets=sets, kv_len=kv_len,
                                          seed=SEED + 17 * kv_len + sets)
                     graph = time_graph(ops, 5, 3, stream)
                     s0.record(stream)
@@ -886,10 +891,10 @@ def decode_sweep(device, stream, layers=LAYERS):
                     s1.record(stream)
                     torch.cuda.synchronize()
                 ms = s0.elapsed_time(s1) / 5
-                b = algo_bytes_per_op(sets=sets, kv_len=kv_len, kv_bytes_per_row=row) * layers
+                b = per_op * nl
                 gbs = b / (ms / 1e3) / 1e9
                 res[f"L{kv_len}_N{sets}_{kv}"] = {"gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
-                                                  "us_per_op": round(ms * 1e3 / layers, 2)}
+                                                  "us_per_op": round(ms * 1e3 / nl, 2), "layers": int(nl)}
                 del graph, ops
                 torch.cuda.empty_cache()
         # the padded window of a decode step (n_kv_pad = PAD(L + 1, 256), rows
