@@ -12,7 +12,7 @@
    file.  They cross-check the C oracle; they are not reference outputs (the
    reference's ggml kernels are not in its tree).
 
-Seeds follow the survey convention: base 42.
+Seeds: base 42, the reference's own test seed (tests/debug-dit-cossim.py:17).
 """
 from __future__ import annotations
 
