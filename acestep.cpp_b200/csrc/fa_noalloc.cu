@@ -8,13 +8,15 @@
 // whole device, which a real-time audio thread cannot afford), and builds that
 // forbid runtime allocation once they have started.  They still pass Q, K, V,
 // the mask and the output; what they cannot pass is the workspace that
-// acefa_flash_attn_ext() asks for (the split-KV partial results).
+// acefa_flash_attn_ext() asks for on the dense path (the mask-class table, the
+// partial results of the last-wave key-range split, F16 copies of BF16 K/V;
+// decode nodes need none).
 //
 // The scratch therefore lives in this file-scope device array.  Every GPU that
 // loads libacefa.so holds it until the process exits.  All calls on a device
 // share it and it keeps whatever the previous call left there; nothing in it has
-// to start at zero, because each call writes every partial slot before it
-// reads it.  Two calls whose kernels overlap on the GPU (different streams, or
+// to start at zero, because each call's kernels write every class byte,
+// partial slot and K/V copy before reading it.  Two calls whose kernels overlap on the GPU (different streams, or
 // different host threads, without ordering between them) race on the array.
 #include <mutex>
 

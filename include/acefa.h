@@ -105,12 +105,14 @@ ACEFA_API int acefa_flash_attn_ext(const acefa_tensor *q, const acefa_tensor *k,
  * backend always draws flash-attention scratch from its own memory pool.
  *
  * Arguments and results are those of acefa_flash_attn_ext() without the
- * workspace pair.  The split-KV scratch is a fixed 8 MiB array inside the
- * library, one per GPU, held from library load until process exit.  The call
- * plans its work for that 8 MiB (the dense path shrinks or drops its last-wave
- * key-range split to fit, exactly as acefa_flash_attn_ext would with an 8 MiB
- * workspace); operands that need more even then -- a decode node with very many
- * split-KV partials, a mask class table over 8 MiB -- are refused with
+ * workspace pair.  The scratch is a fixed 8 MiB array inside the library, one
+ * per GPU, held from library load until process exit; only the dense
+ * (query-heavy) path uses it -- its mask-class table, the partial results of
+ * its last-wave key-range split, F16 copies of BF16 K/V when they fit -- while
+ * decode nodes need none.  The call plans its work for that 8 MiB (the dense
+ * path shrinks or drops its split and skips the BF16 copies to fit, exactly as
+ * acefa_flash_attn_ext would with an 8 MiB workspace); operands that need more
+ * even then -- a mask-class table over 8 MiB -- are refused with
  * ACEFA_ERR_NOALLOC_LIMIT and nothing is launched.  The first call on each
  * device looks up that array's device address (with the device current), so
  * make that first call before any stream capture.  The address is kept for the
@@ -315,8 +317,9 @@ ACEFA_API int acefa_cfg_logit_combine(const float *cond, const float *uncond, in
                                       float *compact, void *stream);
 
 /* Workspace acefa_flash_attn_ext() needs for these operands on the current device
- * (split-KV partial results, mask tile classes, and for BF16 K/V on the dense
- * path F16 copies of K and V: 4 bytes per K/V value).  A function of shapes,
+ * (dense path only: mask tile classes, the partial results of the last-wave
+ * key-range split, and for BF16 K/V F16 copies of K and V, 4 bytes per K/V
+ * value; decode nodes need a token 256 bytes).  A function of shapes,
  * types and the device only -- never of tensor contents -- so it can be sized
  * once before CUDA-graph capture.  A smaller workspace also works where the
  * operator can do without: it then skips the BF16 copies (converting inside

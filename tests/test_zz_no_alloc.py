@@ -2,7 +2,8 @@
 engine any device memory (a host whose allocator owns every buffer, a thread
 that must not block on cudaMalloc, a build that forbids runtime allocation).
 
-Its split-KV scratch is a fixed array inside the library, so these tests check
+Its scratch (the dense path's mask-class table and split partials) is a fixed
+array inside the library, so these tests check
 that it produces the same result as the allocating entry point, call after
 call, and that it refuses operands whose scratch would not fit.  This file is
 collected last so that a stopping run has already exercised everything else.
