@@ -1081,10 +1081,11 @@ def time_dense(device, stream, name, iters=100, warmup=3, rule=False):
 def dense_extras(device, stream, cpu=True):
     """BASELINE configs 3 and 4: each dense workload timed alone (CUDA graph,
     100 replays, L2 flushed between replays of ops smaller than twice the L2),
-    with its roofline (tensor bound, measured bf16 burst peak;
-    DRAM traffic of one launch from profiles/ncu_traffic.json when captured),
-    the same op through the C ABI with host buffers (e2e), and for the
-    headline shapes the CPU port on sampled query rows."""
+    with its roofline (tensor bound, measured bf16 burst peak; DRAM traffic of
+    one launch from profiles/ncu_traffic.json when captured; `binding`: the
+    longer of the tensor and HBM times and the fraction of it achieved), the
+    same op through the C ABI with host buffers (e2e), and for the headline
+    shapes the CPU port on sampled query rows."""
     peak = read_tflops_peak()
     hbm_peak = read_peaks()[0]
     res = {"peak_tflops": peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; kernel timed alone)",
