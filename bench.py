@@ -33,6 +33,7 @@ for _p in (ROOT, PKG):
 LAYERS, HQ, HKV, D = 36, 32, 8, 128
 SETS, KV_LEN = 16, 8192
 SEED = 42 + 1000 * 2
+L2_BYTES = 126 * 1024 * 1024  # B200 L2: timed inputs exceed twice this or are flushed
 
 
 def algo_bytes_per_op(sets=SETS, kv_len=KV_LEN, kv_bytes_per_row=2 * D, hq=HQ, hkv=HKV, d=D, mask=True):
@@ -1027,9 +1028,6 @@ def build_dense(device, name, seed=SEED + 3, rule=False):
         op = acefa.Op(q, k, v, mask=mask, kv_type=kv_type, scale=hd ** -0.5)
     flops = 4 * hd * dense_pairs(S_q, S_kv, kind, extra) * Hq * B
     return op, flops
-
-
-L2_BYTES = 126 * 1024 * 1024  # B200 L2
 
 
 def time_dense(device, stream, name, iters=100, warmup=3, rule=False):
