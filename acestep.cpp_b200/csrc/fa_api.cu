@@ -242,8 +242,9 @@ void set_scalars(OpDesc &o, float scale, float max_bias, float softcap) {
 // A unit (batch, kv head, 16-row block) runs on a cluster of C CTAs that split
 // its keys and merge through distributed shared memory.  C is the largest
 // size (<= 16, <= the unit's key tiles) for which the device keeps every
-// unit's cluster resident at once, so the op runs in one wave; units beyond
-// that run one CTA each.  A function of shapes and the device only.
+// unit's cluster resident at once, so the op runs in one wave -- and above 6
+// only while every CTA has an SM to itself; units beyond that run one CTA
+// each.  A function of shapes and the device only.
 struct DecodePlan {
     int  n_rb, units, tpu, cluster;
     bool wide;

@@ -42,9 +42,12 @@
 #include "rope_norm.cuh"
 
 // Largest cluster the host plan may pick (a tuning macro; the device may
-// allow less).
+// allow less), and the largest it picks when some SMs would hold two CTAs.
 #ifndef ACEFA_DEC_MAX_CLUSTER
 #define ACEFA_DEC_MAX_CLUSTER 8
+#endif
+#ifndef ACEFA_DEC_SHARE_CLUSTER
+#define ACEFA_DEC_SHARE_CLUSTER 6
 #endif
 // Q8_0 stages in flight and CTAs per SM (tuning macros).
 #ifndef ACEFA_Q8_STAGES
@@ -65,6 +68,7 @@ namespace acefa {
 
 namespace {
 
+constexpr int kDecShareCluster = ACEFA_DEC_SHARE_CLUSTER;
 constexpr int kMetaData = 1;
 constexpr int kMetaTerm = 3;
 
@@ -1454,6 +1458,7 @@ struct InstInfo {
     bool ok = false;
     // clusters of c CTAs the device keeps resident at once (0 = not launchable)
     int active[kDecMaxCluster + 1] = {};
+    int sms = 0;  // the device's SM count
 };
 constexpr int kMaxDev = 64;
 std::mutex    g_inst_mutex;
@@ -1474,6 +1479,7 @@ const InstInfo &inst_info(int dev) {
         return in;
     }
     in.ok = true;
+    cudaDeviceGetAttribute(&in.sms, cudaDevAttrMultiProcessorCount, dev);
     const bool big =
         ACEFA_DEC_MAX_CLUSTER > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
                                          cudaSuccess;
@@ -1572,7 +1578,12 @@ int cluster_for(bool pro, int units, int tiles_per_unit) {
     const InstInfo &in   = pro_info<KV_TYPE, D, WIDE>(pro, dev);
     int             best = 1;
     for (int c = 2; c <= kDecMaxCluster && in.ok; ++c) {
-        if (c <= tiles_per_unit && units <= in.active[c]) {
+        // Clusters of more than kDecShareCluster CTAs only while every CTA
+        // still has an SM to itself: shared SMs slow the short per-CTA key
+        // ranges more than the wider merge saves (32 units: 6 CTAs per unit
+        // 20-29 % faster than 8).
+        const bool own_sm = in.sms <= 0 || (int64_t) units * c <= in.sms;
+        if (c <= tiles_per_unit && units <= in.active[c] && (c <= kDecShareCluster || own_sm)) {
             best = c;
         }
     }
